@@ -1,0 +1,419 @@
+#!/usr/bin/env python
+"""Benchmark of Sion's operator hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload NAME]
+
+Default workload: HGEMM fp16 M=N=K=4096, A row-major, B column-major (stored
+N x K, the reference's "nt" kernel), fp32 accumulate, fp16 output, seed 1 —
+the configuration the headline metric (HGEMM/FlashAttn/SGEMM TFLOPS) is quoted
+on. Other workloads: sgemm_f32_1024, hgemm_f16_128x8192x16384_nt,
+flash_attn_fwd_f16_4x32x8192x128, hgemm_f16_16384_nt.
+
+A step is one operator call on one synthetic batch. Each rank runs its own
+copy of the workload (independent units, no data-path collective: weak
+scaling). Steps are timed one by one with CUDA events on the launching stream;
+between steps a 512 MiB buffer is written to flush the 126 MB L2 (outside the
+events). The reported time is the max over ranks of the mean step time.
+
+`e2e` times the same call through the C ABI with pinned HOST buffers: the
+host-to-device copy of the inputs, the kernel and the device-to-host copy of
+the output, all inside the events.
+
+--impl reference: the reference's host path (BASELINE: LibTorch CPU
+torch.matmul / naive fp32 softmax attention, the reference tests' comparison
+path) timed on the host cores on a bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from sion_b200 import workloads as W  # noqa: E402
+
+DEFAULT_WORKLOAD = W.HGEMM_4096.name
+METRIC = "HGEMM/FlashAttn/SGEMM TFLOPS per B200 and % of peak; 1/2/4/8-GPU aggregate"
+L2_FLUSH_BYTES = 512 << 20
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"],
+                "tflops_sustained": d.get("bf16_tflops_sustained"),
+                "sm_max_mhz": d.get("sm_max_mhz", 1965.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0,
+            "sm_max_mhz": 1965.0, "source": "fallback"}
+
+
+def _ncu_traffic(workload: str):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get(workload)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8
+                          for i in range(4) if r[5 + i].lower().startswith("active")})
+        loaded = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------- workloads
+class GemmRunner:
+    def __init__(self, cfg: W.GemmConfig, device):
+        from sion_b200 import abi
+        self.abi = abi
+        self.cfg = cfg
+        A, B = W.gemm_inputs(cfg)
+        self.hA = A.pin_memory()
+        self.hB = B.pin_memory()
+        self.dA = self.hA.to(device)
+        self.dB = self.hB.to(device)
+        dt = torch.float32 if cfg.dtype == "f32" else torch.float16
+        self.dC = torch.empty(cfg.M, cfg.N, dtype=dt, device=device)
+        self.hC = torch.empty(cfg.M, cfg.N, dtype=dt).pin_memory()
+        self.launches_per_step = 1
+
+    def step(self):
+        c = self.cfg
+        if c.dtype == "f32":
+            self.abi.sgemm(self.dA, self.dB, self.dC)
+        else:
+            self.abi.hgemm(self.dA, self.dB, self.dC,
+                           b_layout=self.abi.B_NK if c.b_layout == "nk" else self.abi.B_KN)
+
+    def step_e2e(self):
+        self.dA.copy_(self.hA, non_blocking=True)
+        self.dB.copy_(self.hB, non_blocking=True)
+        self.step()
+        self.hC.copy_(self.dC, non_blocking=True)
+
+    @property
+    def h2d_bytes(self):
+        return self.hA.numel() * self.hA.element_size() + self.hB.numel() * self.hB.element_size()
+
+    @property
+    def d2h_bytes(self):
+        return self.hC.numel() * self.hC.element_size()
+
+    def algorithmic(self):
+        c = self.cfg
+        if c.name == W.HGEMM_SKINNY.name:
+            return "hbm", float(c.io_bytes)
+        return "tensor" if c.dtype == "f16" else "ffma", c.flops
+
+
+class AttnRunner:
+    def __init__(self, cfg: W.AttnConfig, device):
+        from sion_b200 import abi
+        self.abi = abi
+        self.cfg = cfg
+        Q, K, V = W.attn_inputs(cfg)
+        self.h = [t.pin_memory() for t in (Q, K, V)]
+        self.d = [t.to(device) for t in self.h]
+        self.dO = torch.empty_like(self.d[0])
+        self.dL = torch.empty(cfg.B, cfg.H, cfg.S, device=device)
+        self.hO = torch.empty_like(self.h[0]).pin_memory()
+        self.hL = torch.empty(cfg.B, cfg.H, cfg.S).pin_memory()
+        self.launches_per_step = 1
+
+    def step(self):
+        self.abi.flash_attn_fwd(self.d[0], self.d[1], self.d[2], self.dO, self.dL)
+
+    def step_e2e(self):
+        for d, h in zip(self.d, self.h):
+            d.copy_(h, non_blocking=True)
+        self.step()
+        self.hO.copy_(self.dO, non_blocking=True)
+        self.hL.copy_(self.dL, non_blocking=True)
+
+    @property
+    def h2d_bytes(self):
+        return sum(t.numel() * t.element_size() for t in self.h)
+
+    @property
+    def d2h_bytes(self):
+        return self.hO.numel() * 2 + self.hL.numel() * 4
+
+    def algorithmic(self):
+        return "tensor", self.cfg.flops
+
+
+def make_runner(name, device):
+    cfg = W.CONFIGS[name]
+    return AttnRunner(cfg, device) if isinstance(cfg, W.AttnConfig) else GemmRunner(cfg, device)
+
+
+# ----------------------------------------------------------------- CPU host path
+def cpu_sample(cfg, budget_s: float = 10.0):
+    """Time the reference's host path on a bounded row sample; returns
+    (TFLOPS, threads, description)."""
+    threads = torch.get_num_threads()
+    if isinstance(cfg, W.AttnConfig):
+        Q, K, V = W.attn_inputs(W.AttnConfig(cfg.name, 1, 1, cfg.S, cfg.D, cfg.seed))
+        q, k, v = Q[0, 0].float(), K[0, 0].float(), V[0, 0].float()
+        rows = 1024
+        flops_per = 4.0 * rows * cfg.S * cfg.D
+        def fn():
+            s = (q[:rows] @ k.t()) / (cfg.D ** 0.5)
+            p = torch.softmax(s, dim=-1)
+            return p @ v
+        desc = (f"naive fp32 softmax(QK^T/sqrt(D))V, {rows} query rows x {cfg.S} keys of one "
+                f"(b,h) per call, torch CPU, repeated for ~{budget_s:.0f} s")
+    else:
+        rows = min(cfg.M, 512)
+        A, B = W.gemm_inputs(cfg, M=rows)
+        a = A.float()
+        b = B.float()
+        if cfg.b_layout == "nk":
+            b = b.t()
+        flops_per = 2.0 * rows * cfg.N * cfg.K
+        def fn():
+            return torch.matmul(a, b)
+        desc = (f"torch.matmul fp32 on CPU (fp16 inputs upcast), {rows} rows of A x full B "
+                f"per call, repeated for ~{budget_s:.0f} s")
+    fn()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return flops_per * n / el / 1e12, threads, desc
+
+
+# ----------------------------------------------------------------- main
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    cfg = W.CONFIGS[args.workload]
+    torch.set_num_threads(os.cpu_count() or 1)
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample(cfg, budget_s=1.0)
+    desc, threads = "", 1
+    for _ in range(args.steps):
+        v, threads, desc = cpu_sample(cfg, budget_s=max(2.0, 20.0 / max(args.steps, 1)))
+        vals.append(v)
+    value = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded torch CPU generator)",
+        "config": {"workload": cfg.name, "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(W.CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world, rank, local = init_dist() if args.impl == "ours" else (
+        int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    runner = make_runner(args.workload, device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        runner.step()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    barrier(world)
+    torch.cuda.synchronize()
+    with sampler:
+        time.sleep(0.25)
+        t_wall = time.perf_counter()
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            runner.step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall
+    barrier(world)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    mean_ms = statistics.mean(step_ms)
+    ms = max_over_ranks(mean_ms, world)
+
+    bound, work = runner.algorithmic()
+    value = world * runner.cfg.flops / (ms * 1e-3) / 1e12
+
+    # e2e through the C ABI with host buffers
+    for _ in range(2):
+        runner.step_e2e()
+    torch.cuda.synchronize()
+    e2e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e2e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    for i in range(args.steps):
+        e2e_s[i].record(stream)
+        runner.step_e2e()
+        e2e_e[i].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(e2e_s, e2e_e)),
+                            world)
+    e2e_val = world * runner.cfg.flops / (e2e_ms * 1e-3) / 1e12
+
+    peaks = _peaks()
+    if bound == "hbm":
+        achieved = work / (mean_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s"}
+    elif bound == "ffma":
+        ffma_peak = 148 * 128 * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12
+        achieved = work / (mean_ms * 1e-3) / 1e12
+        roof = {"bound": "ffma", "achieved": achieved, "peak": ffma_peak, "unit": "TFLOP/s"}
+    else:
+        achieved = work / (mean_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["tflops"],
+                "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_source"] = peaks["source"] + (" (148 SM x 128 FFMA x 2 x max clock)"
+                                             if bound == "ffma" else "")
+    roof["traffic"] = _ncu_traffic(runner.cfg.name)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        v, threads, desc = cpu_sample(runner.cfg, budget_s=10.0)
+        cpu = {"value": v, "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": desc}
+
+    clocks = sampler.summary()
+    if rank == 0:
+        cfg = runner.cfg
+        conf = {"workload": cfg.name, "parallelism": f"replicas x{world} (independent units)",
+                "l2": "flushed between steps (512 MiB write outside the timed events)"}
+        if isinstance(cfg, W.GemmConfig):
+            conf.update({"M": cfg.M, "N": cfg.N, "K": cfg.K, "b_layout": cfg.b_layout})
+        else:
+            conf.update({"B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D})
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if getattr(cfg, "dtype", "f16") == "f32" else "f16 (fp32 accumulate)",
+            "data": "synthetic (seeded torch CPU generator)", "config": conf,
+            "frac_of_peak": value / world / (roof["peak"] if bound != "hbm" else 1) if bound != "hbm" else None,
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "TFLOPS", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": runner.h2d_bytes,
+                    "d2h_bytes_per_step": runner.d2h_bytes},
+            "gpu_launches": args.steps * runner.launches_per_step,
+            "clocks": clocks, "wall_s_timed": t_wall,
+            "step_ms_min": min(step_ms), "step_ms_median": statistics.median(step_ms),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

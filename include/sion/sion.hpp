@@ -1,0 +1,21 @@
+// sion:: LibTorch wrappers over the felix operators. Same signatures as the
+// reference (include/sion/sion.hpp:4-14); flash_attention_lse is new.
+#pragma once
+#include <torch/torch.h>
+#include <tuple>
+
+namespace sion {
+
+torch::Tensor flash_attention(const torch::Tensor& query, const torch::Tensor& key,
+                              const torch::Tensor& value);
+torch::Tensor sgemm(const torch::Tensor& A, const torch::Tensor& B, float alpha, float beta);
+torch::Tensor hgemm(const torch::Tensor& A, const torch::Tensor& B, float alpha, float beta);
+torch::Tensor hgemm_nt(const torch::Tensor& A, const torch::Tensor& B, float alpha, float beta);
+torch::Tensor gemm(const torch::Tensor& A, const torch::Tensor& B, float alpha, float beta);
+
+// new: (O, LSE) with LSE fp32 [B, H, S]
+std::tuple<torch::Tensor, torch::Tensor> flash_attention_lse(const torch::Tensor& query,
+                                                             const torch::Tensor& key,
+                                                             const torch::Tensor& value);
+
+}  // namespace sion

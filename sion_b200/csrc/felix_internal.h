@@ -1,0 +1,76 @@
+// Internal host-side interfaces shared by the kernel translation units and the
+// C-ABI layer (felix_c.cu). Nothing here is exported.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/felix_c.h"
+
+namespace felix_impl {
+
+struct FelixCode {
+  int type;          // FELIX_SUCCESS / FELIX_KERNEL_LAUNCH_FAILED / ... (felix_c.h)
+  cudaError_t cuda;  // underlying CUDA error, cudaSuccess if none
+};
+
+// Record a message for felix_last_error_message() and return the code.
+FelixCode api_error(const char* msg, cudaError_t e = cudaErrorInvalidValue);
+FelixCode launch_error(cudaError_t e, const char* msg);
+
+struct DeviceInfo {
+  int ordinal;
+  int num_sms;
+  int max_smem_optin;
+  unsigned* status_word;  // device address of the watchdog word
+};
+
+// Per-device facts for the current device (initialised once per device).
+DeviceInfo* current_device_info();
+
+// Library-owned scratch for a (device, stream) pair, grown on demand and
+// zero-filled on (re)allocation. Kernels leave their counters at zero.
+void* library_workspace(DeviceInfo* dev, cudaStream_t stream, size_t bytes);
+
+// 2-D fp16 tensor map, 128-byte swizzle: inner extent `inner` elements,
+// `outer` rows, row pitch in bytes, box of box_inner x box_outer.
+int encode_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer);
+// Same without swizzle (used for plain row stores / loads).
+int encode_tmap_2d_f16_noswizzle(CUtensorMap* map, const void* base, uint64_t inner,
+                                 uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner,
+                                 uint32_t box_outer);
+
+FelixCode scale_half_matrix(__half* C, size_t n, float beta, cudaStream_t stream);
+FelixCode scale_float_matrix(float* C, size_t n, float beta, cudaStream_t stream);
+
+struct HgemmOptions {
+  int block_n = 0;   // 0 = auto, 128 or 256
+  int stream_k = 0;  // 0 = auto, 1 = off, 2 = on whenever the last wave is partial
+  int max_ctas = 0;  // 0 = one per SM; otherwise cap the persistent grid
+};
+
+size_t hgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o,
+                             int num_sms);
+FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __half* A,
+                       const __half* B, float beta, __half* C, bool b_kn, const HgemmOptions& o,
+                       void* workspace, size_t ws_bytes, cudaStream_t stream);
+
+struct SgemmOptions {
+  int split_k = 0;  // 0 = auto, 1 = none, n = n-way
+};
+size_t sgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o,
+                             int num_sms);
+FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const float* A,
+                       const float* B, float beta, float* C, const SgemmOptions& o,
+                       void* workspace, size_t ws_bytes, cudaStream_t stream);
+
+FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, __half* O,
+                            float* lse, uint32_t heads, uint32_t batch, uint32_t seqlen,
+                            uint32_t head_dim, float scale, cudaStream_t stream);
+
+FelixCode watchdog_probe_launch(uint32_t limit_us, cudaStream_t stream);
+
+}  // namespace felix_impl

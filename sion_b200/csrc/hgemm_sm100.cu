@@ -1,0 +1,578 @@
+// HGEMM for sm_100a: C = alpha * A * op(B) + beta * C, fp16 in, fp32 accumulate
+// (TMEM), fp16 out. Replaces the Ampere mma.sync kernel behind
+// felix::ampere_hgemm_launch (reference: src/felix/gemm/hgemm/
+// cute_hgemm_128x128_{nn,nt}_kernel_launch.cu, kernels/cute_ampere_hgemm_16816.cuh),
+// which accumulates in fp16; this one accumulates in fp32.
+//
+// Layouts (all row-major, as in the reference):
+//   A [M x K]; "nt": B stored [N x K] (K-major); "nn": B stored [K x N] (N-major);
+//   C [M x N].
+//
+// Design:
+//   * persistent grid, one CTA per SM, 6 warps:
+//       warp 0  TMA producer (one elected lane), multi-stage smem ring
+//       warp 1  TMEM allocator + single-thread tcgen05.mma issuer
+//       warps 2-5 epilogue: tcgen05.ld -> alpha/beta -> fp16 -> global
+//   * CTA tile 128 x BN (BN = 256 or 128), K step 64 (one 128-byte swizzle row),
+//     UMMA 128 x BN x 16; two TMEM accumulators so the epilogue of tile i
+//     overlaps the main loop of tile i+1.
+//   * schedule: whole tiles round-robin over the persistent CTAs ("data-parallel"
+//     waves); the tiles of an incomplete last wave are spread evenly over all
+//     CTAs by k-iterations (stream-K). A stream-K tile with several contributors
+//     is finished by whichever contributor arrives last (atomic ticket): every
+//     contributor writes its fp32 partial to the workspace, the last one sums all
+//     partials in contributor order (deterministic) and writes C. No CTA ever
+//     waits on another CTA.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "felix_internal.h"
+#include "sm100_ptx.cuh"
+
+namespace felix_sm100 {
+namespace hgemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  // ring + 1 KB alignment slack + barrier block
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+struct Params {
+  uint32_t M, N, K;
+  float alpha, beta;
+  __half* C;
+  uint32_t b_mn_major;  // 1 = "nn" (B is K x N), 0 = "nt" (B is N x K)
+  uint32_t tiles_m, tiles_n, kblocks;
+  uint32_t dp_tiles, sk_tiles;
+  uint64_t sk_iters;
+  uint32_t group_m;
+  float* ws_partials;     // [gridDim.x][2][BM*BN]
+  unsigned* ws_counters;  // [sk_tiles]
+  unsigned* status;       // watchdog word
+};
+
+struct Unit {
+  uint32_t tile;   // linear tile id (0..tiles-1)
+  uint32_t kb0, kb1;
+  uint32_t sk;     // stream-K tile index (valid when partial)
+  uint32_t seg;    // 0/1: which of this CTA's two partial slots
+  bool partial;
+};
+
+// Identical walk for the producer, MMA and epilogue roles of one CTA.
+struct Sched {
+  uint32_t cta, P, dp_tiles, KB;
+  uint64_t I, it, end, start;
+  uint32_t dp_next;
+
+  __device__ __forceinline__ void init(const Params& p) {
+    cta = blockIdx.x;
+    P = gridDim.x;
+    dp_tiles = p.dp_tiles;
+    KB = p.kblocks;
+    I = p.sk_iters;
+    start = I * cta / P;
+    end = I * (cta + 1) / P;
+    it = start;
+    dp_next = cta;
+  }
+  __device__ __forceinline__ bool next(Unit& u) {
+    if (dp_next < dp_tiles) {
+      u.tile = dp_next;
+      u.kb0 = 0;
+      u.kb1 = KB;
+      u.partial = false;
+      u.sk = 0;
+      u.seg = 0;
+      dp_next += P;
+      return true;
+    }
+    if (it < end) {
+      const uint32_t s = static_cast<uint32_t>(it / KB);
+      const uint32_t kb0 = static_cast<uint32_t>(it - uint64_t(s) * KB);
+      const uint64_t left = end - it;
+      const uint32_t kb1 = left < uint64_t(KB - kb0) ? kb0 + static_cast<uint32_t>(left) : KB;
+      u.tile = dp_tiles + s;
+      u.kb0 = kb0;
+      u.kb1 = kb1;
+      u.sk = s;
+      u.seg = (it == start) ? 0u : 1u;
+      u.partial = !(kb0 == 0 && kb1 == KB);
+      it += kb1 - kb0;
+      dp_next = dp_tiles;  // dp phase is over
+      return true;
+    }
+    return false;
+  }
+  // CTA whose k-range contains stream-K iteration `x`.
+  __device__ __forceinline__ uint32_t cta_of(uint64_t x) const {
+    return static_cast<uint32_t>(((x + 1) * P - 1) / I);
+  }
+};
+
+__device__ __forceinline__ void tile_coords(const Params& p, uint32_t t, uint32_t& tm,
+                                            uint32_t& tn) {
+  // Grouped raster: runs of group_m M-tiles sweep across N, so CTAs running at
+  // the same time share A row-panels and B column-panels in L2.
+  const uint32_t per_group = p.group_m * p.tiles_n;
+  const uint32_t g = t / per_group;
+  const uint32_t first_m = g * p.group_m;
+  const uint32_t gm = min(p.group_m, p.tiles_m - first_m);
+  const uint32_t r = t - g * per_group;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+// Convert 32 fp32 accumulators (columns c..c+31 of row `row`) and store to C.
+__device__ __forceinline__ void store_row_chunk(const Params& p, uint32_t row, uint32_t col,
+                                                const float (&v)[32]) {
+  if (row >= p.M) return;
+  __half* dst = p.C + size_t(row) * p.N + col;
+  const bool full = (col + 32 <= p.N) && ((p.N & 7u) == 0);
+  if (full) {
+    uint4 out[4];
+    uint32_t* o = reinterpret_cast<uint32_t*>(out);
+    if (p.beta != 0.f) {
+      uint4 old[4];
+      const uint4* src = reinterpret_cast<const uint4*>(dst);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) old[i] = src[i];
+      const __half2* oh = reinterpret_cast<const __half2*>(old);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 c = __half22float2(oh[i]);
+        o[i] = pack_half2(fmaf(p.alpha, v[2 * i], p.beta * c.x),
+                          fmaf(p.alpha, v[2 * i + 1], p.beta * c.y));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = pack_half2(p.alpha * v[2 * i], p.alpha * v[2 * i + 1]);
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d4[i] = out[i];
+  } else {
+    for (int i = 0; i < 32; ++i) {
+      if (col + i < p.N) {
+        float r = p.alpha * v[i];
+        if (p.beta != 0.f) r = fmaf(p.beta, __half2float(dst[i]), r);
+        dst[i] = __float2half_rn(r);
+      }
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
+                            const __grid_constant__ CUtensorMap tmB, const Params p) {
+  using C_ = Cfg<BN>;
+  constexpr int S = C_::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C_::kStageBytes);
+  uint64_t* full = bars;               // [S]
+  uint64_t* empty = bars + S;          // [S]
+  uint64_t* tfull = bars + 2 * S;      // [2]
+  uint64_t* tempty = bars + 2 * S + 2; // [2]
+  uint64_t* drain = bars + 2 * S + 4;  // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* bcast = tmem_slot + 2;
+
+  const uint32_t warp = threadIdx.x / 32;
+  const uint32_t lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C_::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      Sched sc;
+      sc.init(p);
+      Unit u;
+      uint32_t stage = 0, phase = 0;
+      uint32_t filled = 0;
+      bool ok = true;
+      while (ok && sc.next(u)) {
+        uint32_t tm, tn;
+        tile_coords(p, u.tile, tm, tn);
+        const int m0 = int(tm * BM), n0 = int(tn * BN);
+        for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kWdProducerEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = ring + stage * C_::kStageBytes;
+          uint8_t* sb = sa + C_::kABytes;
+          mbar_arrive_expect_tx(&full[stage], C_::kStageBytes);
+          tma_load_2d(sa, &tmA, &full[stage], int(kb * BK), m0);
+          if (p.b_mn_major) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * (64 * BK * 2), &tmB, &full[stage], n0 + 64 * j, int(kb * BK));
+          } else {
+            tma_load_2d(sb, &tmB, &full[stage], int(kb * BK), n0);
+          }
+          ++filled;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: wait (bounded) for the last fill of every stage so that no TMA
+      // write is in flight when the CTA exits.
+      const uint32_t n = filled < uint32_t(S) ? filled : uint32_t(S);
+      for (uint32_t i = 0; i < n; ++i) {
+        // stage of the i-th most recent fill, and the phase parity it filled
+        const uint32_t f = filled - 1 - i;
+        const uint32_t st = f % S;
+        const uint32_t par = (f / S) & 1u;
+        int dummy = 0;
+        mbar_wait(&full[st], par, &dummy, p.status, kWdDrain, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16_f32(BM, BN, false, p.b_mn_major != 0);
+      Sched sc;
+      sc.init(p);
+      Unit u;
+      uint32_t stage = 0, phase = 0, i = 0;
+      bool ok = true;
+      while (ok && sc.next(u)) {
+        const uint32_t buf = i & 1u;
+        if (!mbar_wait(&tempty[buf], ((i >> 1) & 1u) ^ 1u, abort_flag, p.status,
+                       kWdMmaTmemEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kWdMmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(ring + stage * C_::kStageBytes);
+          const uint32_t b0 = a0 + C_::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = make_sdesc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = p.b_mn_major ? make_sdesc_sw128(b0 + k * 2048, 64 * BK * 2, 1024)
+                                             : make_sdesc_sw128(b0 + k * 32, 16, 1024);
+            umma_f16_ss(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
+        ++i;
+      }
+      // Wait (bounded) until every issued MMA has completed before teardown.
+      umma_commit(drain);
+      int dummy = 0;
+      mbar_wait(drain, 0, &dummy, p.status, kWdDrain, 100000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const uint32_t q = warp & 3u;  // TMEM lane quarter this warp may access
+    const uint32_t row_in_tile = q * 32 + lane;
+    const uint32_t epi_tid = threadIdx.x - 64;  // 0..127
+    Sched sc;
+    sc.init(p);
+    Unit u;
+    uint32_t i = 0;
+    while (sc.next(u)) {
+      const uint32_t buf = i & 1u;
+      if (!mbar_wait(&tfull[buf], (i >> 1) & 1u, abort_flag, p.status, kWdEpilogueTmemFull))
+        break;
+      tc_fence_after();
+      uint32_t tm, tn;
+      tile_coords(p, u.tile, tm, tn);
+      const uint32_t row = tm * BM + row_in_tile;
+      const uint32_t col0 = tn * BN;
+      const uint32_t taddr = tmem_base + ((q * 32u) << 16) + buf * BN;
+
+      if (!u.partial) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c, r);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          store_row_chunk(p, row, col0 + c, v);
+        }
+      } else {
+        // Stream-K contribution: publish the fp32 partial, take a ticket.
+        float* slot = p.ws_partials + (size_t(sc.cta) * 2 + u.seg) * (BM * BN) +
+                      size_t(row_in_tile) * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c, r);
+          tmem_ld_wait();
+          float4* d4 = reinterpret_cast<float4*>(slot + c);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            __stcg(d4 + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                       __uint_as_float(r[4 * j + 2]),
+                                       __uint_as_float(r[4 * j + 3])));
+        }
+        __threadfence();
+        named_barrier_sync(1, 128);
+        const uint64_t tile_first = uint64_t(u.sk) * sc.KB;
+        const uint32_t c_first = sc.cta_of(tile_first);
+        const uint32_t c_last = sc.cta_of(tile_first + sc.KB - 1);
+        const uint32_t ncontrib = c_last - c_first + 1;
+        if (epi_tid == 0) {
+          const unsigned old = atomicAdd(&p.ws_counters[u.sk], 1u);
+          const uint32_t last = (old == ncontrib - 1) ? 1u : 0u;
+          if (last) atomicExch(&p.ws_counters[u.sk], 0u);
+          *bcast = last;
+        }
+        named_barrier_sync(1, 128);
+        const bool last = *bcast != 0;
+        if (last) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            for (uint32_t cc = c_first; cc <= c_last; ++cc) {
+              const uint32_t seg = (sc.I * cc / sc.P) / sc.KB == u.sk ? 0u : 1u;
+              const float4* s4 = reinterpret_cast<const float4*>(
+                  p.ws_partials + (size_t(cc) * 2 + seg) * (BM * BN) +
+                  size_t(row_in_tile) * BN + c);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 x = __ldcg(s4 + j);
+                v[4 * j] += x.x;
+                v[4 * j + 1] += x.y;
+                v[4 * j + 2] += x.z;
+                v[4 * j + 3] += x.w;
+              }
+            }
+            store_row_chunk(p, row, col0 + c, v);
+          }
+        }
+        // keep the broadcast slot stable until all threads have read it
+        named_barrier_sync(1, 128);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      ++i;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::kTmemCols);
+  }
+}
+
+}  // namespace hgemm
+}  // namespace felix_sm100
+
+// ============================================================ host launcher
+namespace felix_impl {
+
+using namespace felix_sm100::hgemm;
+
+namespace {
+
+template <int BN>
+int configure_once(int device) {
+  static int done[64] = {0};
+  if (device < 0 || device >= 64) return -1;
+  if (!done[device]) {
+    cudaError_t e = cudaFuncSetAttribute(felix_sm100::hgemm::hgemm_persistent_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<BN>::kSmemBytes);
+    if (e != cudaSuccess) return int(e);
+    done[device] = 1;
+  }
+  return 0;
+}
+
+struct Plan {
+  int bn;
+  uint32_t tiles_m, tiles_n, kblocks, tiles;
+  uint32_t grid;
+  uint32_t dp_tiles, sk_tiles;
+  uint64_t sk_iters;
+};
+
+Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int num_sms) {
+  Plan pl{};
+  pl.bn = o.block_n ? o.block_n : (N >= 256 ? 256 : 128);
+  pl.tiles_m = (M + BM - 1) / BM;
+  pl.tiles_n = (N + pl.bn - 1) / pl.bn;
+  pl.kblocks = (K + BK - 1) / BK;
+  pl.tiles = pl.tiles_m * pl.tiles_n;
+  uint32_t P = uint32_t(num_sms);
+  if (o.max_ctas > 0 && uint32_t(o.max_ctas) < P) P = uint32_t(o.max_ctas);
+  const uint32_t rem = pl.tiles % P;
+  bool use_sk;
+  if (o.stream_k == 1) {
+    use_sk = false;
+  } else if (o.stream_k == 2) {
+    use_sk = rem != 0 && pl.kblocks >= 2;
+  } else {
+    // Spread the incomplete wave by k-iterations when it leaves SMs idle and
+    // each CTA still gets a useful k-range.
+    use_sk = rem != 0 && pl.kblocks >= 8 && rem * 100 < P * 85 &&
+             uint64_t(rem) * pl.kblocks >= uint64_t(P) * 4;
+  }
+  if (use_sk) {
+    pl.sk_tiles = rem;
+    pl.dp_tiles = pl.tiles - rem;
+    pl.sk_iters = uint64_t(rem) * pl.kblocks;
+    pl.grid = P;
+  } else {
+    pl.sk_tiles = 0;
+    pl.dp_tiles = pl.tiles;
+    pl.sk_iters = 0;
+    pl.grid = pl.tiles < P ? pl.tiles : P;
+  }
+  return pl;
+}
+
+}  // namespace
+
+size_t hgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o,
+                             int num_sms) {
+  Plan pl = make_plan(M, N, K, o, num_sms);
+  if (pl.sk_tiles == 0) return 0;
+  return size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float) + size_t(pl.grid) * sizeof(unsigned);
+}
+
+FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __half* A,
+                       const __half* B, float beta, __half* C, bool b_kn, const HgemmOptions& o,
+                       void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  if (M == 0 || N == 0) return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  if (!C) return api_error("hgemm: null C");
+  if (K == 0) {
+    // C = beta * C: a zero-depth product; the tensor-core path needs K > 0.
+    return scale_half_matrix(C, size_t(M) * N, beta, stream);
+  }
+  if (!A || !B) return api_error("hgemm: null pointer");
+  if (o.block_n != 0 && o.block_n != 128 && o.block_n != 256)
+    return api_error("hgemm: block_n must be 0, 128 or 256");
+  // TMA: global row strides must be multiples of 16 bytes, bases 16-byte aligned.
+  if (K % 8 != 0) return api_error("hgemm: K must be a multiple of 8 (16-byte rows for TMA)");
+  if (b_kn && N % 8 != 0) return api_error("hgemm nn: N must be a multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15u)
+    return api_error("hgemm: A and B must be 16-byte aligned");
+  if ((N % 8 == 0) && (reinterpret_cast<uintptr_t>(C) & 15u))
+    return api_error("hgemm: C must be 16-byte aligned");
+
+  DeviceInfo* dev = current_device_info();
+  if (!dev) return launch_error(cudaGetLastError(), "hgemm: no CUDA device");
+  Plan pl = make_plan(M, N, K, o, dev->num_sms);
+
+  CUtensorMap tmA, tmB;
+  int rc = encode_tmap_2d_f16(&tmA, A, K, M, uint64_t(K) * 2, BK, BM);
+  if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(A) failed");
+  if (b_kn)
+    rc = encode_tmap_2d_f16(&tmB, B, N, K, uint64_t(N) * 2, 64, BK);
+  else
+    rc = encode_tmap_2d_f16(&tmB, B, K, N, uint64_t(K) * 2, BK, pl.bn);
+  if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
+
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.C = C;
+  p.b_mn_major = b_kn ? 1u : 0u;
+  p.tiles_m = pl.tiles_m;
+  p.tiles_n = pl.tiles_n;
+  p.kblocks = pl.kblocks;
+  p.dp_tiles = pl.dp_tiles;
+  p.sk_tiles = pl.sk_tiles;
+  p.sk_iters = pl.sk_iters;
+  p.group_m = 16;
+  p.status = dev->status_word;
+  if (pl.sk_tiles) {
+    const size_t need = size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float) +
+                        size_t(pl.grid) * sizeof(unsigned);
+    if (!workspace) {
+      workspace = library_workspace(dev, stream, need);
+      if (!workspace) return launch_error(cudaErrorMemoryAllocation, "hgemm: workspace");
+    } else if (ws_bytes < need) {
+      return api_error("hgemm: workspace too small");
+    }
+    p.ws_partials = static_cast<float*>(workspace);
+    p.ws_counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) +
+                                                size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float));
+  }
+
+  cudaError_t e;
+  if (pl.bn == 256) {
+    if ((rc = configure_once<256>(dev->ordinal)))
+      return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    hgemm_persistent_kernel<256><<<pl.grid, kThreads, Cfg<256>::kSmemBytes, stream>>>(tmA, tmB, p);
+  } else {
+    if ((rc = configure_once<128>(dev->ordinal)))
+      return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    hgemm_persistent_kernel<128><<<pl.grid, kThreads, Cfg<128>::kSmemBytes, stream>>>(tmA, tmB, p);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return launch_error(e, "hgemm: launch failed");
+  return FelixCode{FELIX_SUCCESS, cudaSuccess};
+}
+
+}  // namespace felix_impl

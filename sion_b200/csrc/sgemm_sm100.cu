@@ -1,0 +1,296 @@
+// SGEMM for sm_100a on the FP32 FFMA pipe: C = alpha * A * B + beta * C,
+// A [M x K], B [K x N], C [M x N] row-major fp32.
+// Replaces the SIMT kernels behind felix::ampere_sgemm_launch (reference:
+// src/felix/gemm/sgemm/cute_sgemm_64x64_nn_kernel_launch.cu:7-63 and
+// kernels/cute_ampere_sgemm_64x64_nn.cuh:9-224, default "cute_sgemm_64x64_nn";
+// the other six registered SGEMM names route here too).
+//
+// Design: 128 x 128 CTA tile, 256 threads, each thread an 8 x 8 register block
+// (two 4-wide row groups x two 4-wide column groups, so shared-memory reads are
+// 128-bit and conflict-free), K step 8, double-buffered shared memory fed by
+// 128-bit global loads staged in registers (one barrier per K step). Any M, N, K:
+// loads are predicated with zero fill, stores are bounds-checked; the 128-bit
+// path is used when rows are 16-byte aligned. Small problems are split along K
+// so that the grid covers every SM twice; the last CTA of a tile to finish
+// (atomic ticket) sums the fp32 partials in split order — deterministic, and
+// no CTA waits on another.
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "felix_internal.h"
+
+namespace felix_sm100 {
+namespace sgemm {
+
+constexpr int BM = 128, BN = 128, BK = 8, kThreads = 256;
+constexpr int APAD = 4;  // As row pitch 132 floats: transposed stores avoid bank conflicts
+
+struct Params {
+  uint32_t M, N, K;
+  float alpha, beta;
+  const float* A;
+  const float* B;
+  float* C;
+  uint32_t splits, k_per_split;  // k_per_split is a multiple of BK
+  float* ws;                     // [tiles][splits][16][256] float4
+  unsigned* counters;            // [tiles]
+};
+
+template <bool VEC>
+__device__ __forceinline__ void load_tile(const Params& p, uint32_t m0, uint32_t n0, uint32_t k0,
+                                          uint32_t kend, float4& ra, float4& rb) {
+  const uint32_t t = threadIdx.x;
+  // A: 128 rows x 8 k; thread -> row t/2, k (t%2)*4 .. +3
+  {
+    const uint32_t r = m0 + t / 2, k = k0 + (t % 2) * 4;
+    if (VEC) {
+      ra = (r < p.M && k < kend) ? __ldg(reinterpret_cast<const float4*>(p.A + size_t(r) * p.K + k))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      const float* a = p.A + size_t(r) * p.K;
+      const bool rv = r < p.M;
+      ra.x = (rv && k + 0 < kend) ? __ldg(a + k + 0) : 0.f;
+      ra.y = (rv && k + 1 < kend) ? __ldg(a + k + 1) : 0.f;
+      ra.z = (rv && k + 2 < kend) ? __ldg(a + k + 2) : 0.f;
+      ra.w = (rv && k + 3 < kend) ? __ldg(a + k + 3) : 0.f;
+    }
+  }
+  // B: 8 k x 128 cols; thread -> k t/32, cols (t%32)*4 .. +3
+  {
+    const uint32_t k = k0 + t / 32, c = n0 + (t % 32) * 4;
+    if (VEC) {
+      rb = (k < kend && c < p.N) ? __ldg(reinterpret_cast<const float4*>(p.B + size_t(k) * p.N + c))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      const float* b = p.B + size_t(k) * p.N;
+      const bool kv = k < kend;
+      rb.x = (kv && c + 0 < p.N) ? __ldg(b + c + 0) : 0.f;
+      rb.y = (kv && c + 1 < p.N) ? __ldg(b + c + 1) : 0.f;
+      rb.z = (kv && c + 2 < p.N) ? __ldg(b + c + 2) : 0.f;
+      rb.w = (kv && c + 3 < p.N) ? __ldg(b + c + 3) : 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_tile(float (*As)[BM + APAD], float (*Bs)[BN],
+                                           const float4& ra, const float4& rb) {
+  const uint32_t t = threadIdx.x;
+  const uint32_t r = t / 2, k = (t % 2) * 4;
+  As[k + 0][r] = ra.x;
+  As[k + 1][r] = ra.y;
+  As[k + 2][r] = ra.z;
+  As[k + 3][r] = ra.w;
+  *reinterpret_cast<float4*>(&Bs[t / 32][(t % 32) * 4]) = rb;
+}
+
+template <bool VEC>
+__device__ __forceinline__ void store_out(const Params& p, uint32_t row, uint32_t col,
+                                          const float (&v)[4]) {
+  if (row >= p.M) return;
+  float* c = p.C + size_t(row) * p.N + col;
+  if (VEC && col + 3 < p.N) {
+    float4 o = make_float4(p.alpha * v[0], p.alpha * v[1], p.alpha * v[2], p.alpha * v[3]);
+    if (p.beta != 0.f) {
+      const float4 old = *reinterpret_cast<const float4*>(c);
+      o.x = fmaf(p.beta, old.x, o.x);
+      o.y = fmaf(p.beta, old.y, o.y);
+      o.z = fmaf(p.beta, old.z, o.z);
+      o.w = fmaf(p.beta, old.w, o.w);
+    }
+    *reinterpret_cast<float4*>(c) = o;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (col + j < p.N) {
+        float o = p.alpha * v[j];
+        if (p.beta != 0.f) o = fmaf(p.beta, c[j], o);
+        c[j] = o;
+      }
+    }
+  }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads, 2) sgemm_kernel(const Params p) {
+  __shared__ __align__(16) float As[2][BK][BM + APAD];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+  __shared__ uint32_t s_last;
+
+  const uint32_t t = threadIdx.x;
+  const uint32_t tx = t % 16, ty = t / 16;
+  const uint32_t m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const uint32_t z = blockIdx.z;
+  const uint32_t kbeg = z * p.k_per_split;
+  const uint32_t kend = min(p.K, kbeg + p.k_per_split);
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  const uint32_t nk = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
+  float4 ra, rb;
+  if (nk > 0) {
+    load_tile<VEC>(p, m0, n0, kbeg, kend, ra, rb);
+    store_tile(As[0], Bs[0], ra, rb);
+  }
+  __syncthreads();
+
+  for (uint32_t kt = 0; kt < nk; ++kt) {
+    const uint32_t cur = kt & 1u;
+    if (kt + 1 < nk) load_tile<VEC>(p, m0, n0, kbeg + (kt + 1) * BK, kend, ra, rb);
+#pragma unroll
+    for (int k = 0; k < BK; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][k][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][k][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][k][64 + tx * 4]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (kt + 1 < nk) store_tile(As[cur ^ 1u], Bs[cur ^ 1u], ra, rb);
+    __syncthreads();
+  }
+
+  if (p.splits == 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+      const float v0[4] = {acc[i][0], acc[i][1], acc[i][2], acc[i][3]};
+      const float v1[4] = {acc[i][4], acc[i][5], acc[i][6], acc[i][7]};
+      store_out<VEC>(p, row, n0 + tx * 4, v0);
+      store_out<VEC>(p, row, n0 + 64 + tx * 4, v1);
+    }
+    return;
+  }
+
+  // Split-K: publish the partial (float4 j of thread t at [j][t]: coalesced).
+  const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
+  float4* part = reinterpret_cast<float4*>(p.ws) + (size_t(tile) * p.splits + z) * (16 * 256);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    __stcg(part + (2 * i) * 256 + t, make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]));
+    __stcg(part + (2 * i + 1) * 256 + t, make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]));
+  }
+  __threadfence();
+  __syncthreads();
+  if (t == 0) {
+    const unsigned old = atomicAdd(&p.counters[tile], 1u);
+    const uint32_t last = old == p.splits - 1 ? 1u : 0u;
+    if (last) atomicExch(&p.counters[tile], 0u);
+    s_last = last;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float4* base = reinterpret_cast<const float4*>(p.ws) + size_t(tile) * p.splits * (16 * 256);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+    for (uint32_t zz = 0; zz < p.splits; ++zz) {
+      const float4 x0 = __ldcg(base + zz * (16 * 256) + (2 * i) * 256 + t);
+      const float4 x1 = __ldcg(base + zz * (16 * 256) + (2 * i + 1) * 256 + t);
+      s0.x += x0.x; s0.y += x0.y; s0.z += x0.z; s0.w += x0.w;
+      s1.x += x1.x; s1.y += x1.y; s1.z += x1.z; s1.w += x1.w;
+    }
+    const uint32_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    const float v0[4] = {s0.x, s0.y, s0.z, s0.w};
+    const float v1[4] = {s1.x, s1.y, s1.z, s1.w};
+    store_out<VEC>(p, row, n0 + tx * 4, v0);
+    store_out<VEC>(p, row, n0 + 64 + tx * 4, v1);
+  }
+}
+
+}  // namespace sgemm
+}  // namespace felix_sm100
+
+namespace felix_impl {
+
+using namespace felix_sm100::sgemm;
+
+namespace {
+uint32_t choose_splits(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o, int num_sms) {
+  const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  uint32_t s;
+  if (o.split_k > 0) {
+    s = uint32_t(o.split_k);
+  } else {
+    // Aim for two resident CTAs per SM, keeping at least 128 of K per split.
+    const uint32_t target = 2u * uint32_t(num_sms);
+    s = tiles >= target ? 1u : target / tiles;
+    const uint32_t kmax = K / 128u;
+    if (s > kmax) s = kmax;
+    if (s < 1) s = 1;
+    if (s > 16) s = 16;
+  }
+  const uint32_t kblocks = (K + BK - 1) / BK;
+  if (s > kblocks) s = kblocks ? kblocks : 1;
+  return s;
+}
+}  // namespace
+
+size_t sgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o,
+                             int num_sms) {
+  const uint32_t s = choose_splits(M, N, K, o, num_sms);
+  if (s <= 1) return 0;
+  const size_t tiles = size_t((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  return tiles * s * BM * BN * sizeof(float) + tiles * sizeof(unsigned);
+}
+
+FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const float* A,
+                       const float* B, float beta, float* C, const SgemmOptions& o,
+                       void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  if (M == 0 || N == 0) return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  if (!C || (K > 0 && (!A || !B))) return api_error("sgemm: null pointer");
+  if (K == 0) return scale_float_matrix(C, size_t(M) * N, beta, stream);
+  DeviceInfo* dev = current_device_info();
+  if (!dev) return launch_error(cudaGetLastError(), "sgemm: no CUDA device");
+
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.A = A;
+  p.B = B;
+  p.C = C;
+  p.splits = choose_splits(M, N, K, o, dev->num_sms);
+  const uint32_t kblocks = (K + BK - 1) / BK;
+  p.k_per_split = ((kblocks + p.splits - 1) / p.splits) * BK;
+  // Recompute the split count so that no split is empty.
+  p.splits = (K + p.k_per_split - 1) / p.k_per_split;
+  const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, p.splits);
+  if (grid.y > 65535u) return api_error("sgemm: M too large");
+  if (p.splits > 1) {
+    const size_t tiles = size_t(grid.x) * grid.y;
+    const size_t need = tiles * p.splits * BM * BN * sizeof(float) + tiles * sizeof(unsigned);
+    if (!workspace) {
+      workspace = library_workspace(dev, stream, need);
+      if (!workspace) return launch_error(cudaErrorMemoryAllocation, "sgemm: workspace");
+    } else if (ws_bytes < need) {
+      return api_error("sgemm: workspace too small");
+    }
+    p.ws = static_cast<float*>(workspace);
+    p.counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) +
+                                             tiles * p.splits * BM * BN * sizeof(float));
+  }
+  const bool vec = (K % 4 == 0) && (N % 4 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
+                     reinterpret_cast<uintptr_t>(C)) &
+                    15u) == 0;
+  if (vec)
+    sgemm_kernel<true><<<grid, kThreads, 0, stream>>>(p);
+  else
+    sgemm_kernel<false><<<grid, kThreads, 0, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return launch_error(e, "sgemm: launch failed");
+  return FelixCode{FELIX_SUCCESS, cudaSuccess};
+}
+
+}  // namespace felix_impl

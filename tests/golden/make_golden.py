@@ -1,0 +1,68 @@
+"""Generate the golden fixtures in tests/golden/*.npz.
+
+The reference's own tests take their expected values from torch
+(`torch::addmm` for SGEMM/HGEMM, tests/sgemm/sgemm_test.cpp:15-18 and
+tests/hgemm/hgemm_test.cpp:3-21; `at::scaled_dot_product_attention` for
+attention, tests/flash_attention/fa_test.cpp:8-15). This script evaluates those
+same torch functions on the CPU in float64 over small seeded inputs, so the C
+oracle can be pinned against them without a GPU. LSE is pinned with
+torch.logsumexp over the float64 scores.
+
+Run from the repo root: python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def sgemm_case(name, M, N, K, alpha, beta, seed):
+    g = torch.Generator().manual_seed(seed)
+    A = torch.randn(M, K, generator=g)
+    B = torch.randn(K, N, generator=g)
+    C0 = torch.randn(M, N, generator=g)
+    ref = torch.addmm(C0.double(), A.double(), B.double(), beta=beta, alpha=alpha)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), A=A.numpy(), B=B.numpy(),
+                        C0=C0.numpy(), alpha=alpha, beta=beta, ref=ref.numpy())
+
+
+def hgemm_case(name, M, N, K, nt, alpha, beta, seed):
+    g = torch.Generator().manual_seed(seed)
+    A = (torch.rand(M, K, generator=g) * 2 - 1).half()
+    B = (torch.rand(N, K, generator=g) * 2 - 1).half() if nt else \
+        (torch.rand(K, N, generator=g) * 2 - 1).half()
+    C0 = (torch.rand(M, N, generator=g) * 2 - 1).half()
+    Bk = B.double().t() if nt else B.double()
+    ref = torch.addmm(C0.double(), A.double(), Bk, beta=beta, alpha=alpha)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), A=A.numpy(), B=B.numpy(),
+                        C0=C0.numpy(), nt=nt, alpha=alpha, beta=beta, ref=ref.numpy())
+
+
+def attn_case(name, Bn, H, S, D, seed):
+    g = torch.Generator().manual_seed(seed)
+    Q = torch.randn(Bn, H, S, D, generator=g).half()
+    K = torch.randn(Bn, H, S, D, generator=g).half()
+    V = torch.randn(Bn, H, S, D, generator=g).half()
+    q, k, v = Q.double(), K.double(), V.double()
+    O = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=None, dropout_p=0.0)
+    scores = (q @ k.transpose(-1, -2)) / (D ** 0.5)
+    lse = torch.logsumexp(scores, dim=-1)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), Q=Q.numpy(), K=K.numpy(),
+                        V=V.numpy(), O=O.numpy(), lse=lse.numpy())
+
+
+def main():
+    sgemm_case("sgemm_67x45x33", 67, 45, 33, 0.7, 0.3, 10)
+    sgemm_case("sgemm_128x128x128", 128, 128, 128, 1.0, 0.0, 11)
+    hgemm_case("hgemm_nt_128x256x64", 128, 256, 64, True, 1.0, 0.0, 12)
+    hgemm_case("hgemm_nn_200x136x72", 200, 136, 72, False, 0.5, 0.25, 13)
+    attn_case("attn_1x2x80x64", 1, 2, 80, 64, 14)
+    attn_case("attn_1x1x130x128", 1, 1, 130, 128, 15)
+
+
+if __name__ == "__main__":
+    main()

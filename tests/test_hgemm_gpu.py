@@ -1,0 +1,113 @@
+"""HGEMM (tcgen05) parity through the C ABI against the fp64 CPU oracle.
+Gate: rel-Frobenius <= 1e-3 and |err| <= max(1e-2, 1 fp16 ulp(|ref|)) per
+element (the output is fp16, whose rounding alone exceeds 1e-2 for |C| > 32)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from metrics import assert_fp16_close, compare
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(M, N, K, nt, seed, dist="uniform", std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    draw = (lambda *s: torch.rand(*s, generator=g) * 2 - 1) if dist == "uniform" else \
+        (lambda *s: torch.randn(*s, generator=g) * std)
+    A = draw(M, K).half()
+    B = draw(N, K).half() if nt else draw(K, N).half()
+    C0 = draw(M, N).half()
+    return A, B, C0
+
+
+def _run(felix, M, N, K, nt=True, alpha=1.0, beta=0.0, seed=0, **kw):
+    A, B, C0 = _inputs(M, N, K, nt, seed)
+    dC = C0.clone().cuda()
+    felix.hgemm(A.cuda(), B.cuda(), dC, alpha, beta, b_layout=felix.B_NK if nt else felix.B_KN,
+                **kw)
+    torch.cuda.synchronize()
+    ref = oracle.hgemm(A.numpy(), B.numpy(), nt, alpha, beta, C0.numpy())
+    return ref, dC.cpu().numpy().astype(np.float64)
+
+
+@pytest.mark.parametrize("nt", [True, False])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 256, 128), (512, 1024, 1024),
+                                   (128, 128, 64)])
+def test_hgemm_aligned(felix, nt, M, N, K):
+    ref, out = _run(felix, M, N, K, nt=nt)
+    assert_fp16_close(ref, out, ctx=f"{M}x{N}x{K} nt={nt}")
+
+
+@pytest.mark.parametrize("nt", [True, False])
+@pytest.mark.parametrize("M,N,K", [(200, 136, 72), (1, 8, 8), (129, 264, 200), (77, 512, 1032)])
+def test_hgemm_ragged(felix, nt, M, N, K):
+    ref, out = _run(felix, M, N, K, nt=nt)
+    assert_fp16_close(ref, out, ctx=f"{M}x{N}x{K} nt={nt}")
+
+
+@pytest.mark.parametrize("nt", [True, False])
+def test_hgemm_alpha_beta(felix, nt):
+    ref, out = _run(felix, 256, 512, 256, nt=nt, alpha=0.5, beta=-0.75)
+    assert_fp16_close(ref, out, ctx="alpha/beta")
+
+
+@pytest.mark.parametrize("block_n", [128, 256])
+@pytest.mark.parametrize("nt", [True, False])
+def test_hgemm_stream_k_forced(felix, block_n, nt):
+    # 5 x 4 tiles on 3 persistent CTAs: 18 whole tiles + 2 stream-K tiles
+    M, N, K = 640, 4 * block_n, 1024
+    ref, out = _run(felix, M, N, K, nt=nt, block_n=block_n, stream_k=2, max_ctas=3)
+    assert_fp16_close(ref, out, ctx="stream-K")
+    _, out2 = _run(felix, M, N, K, nt=nt, block_n=block_n, stream_k=2, max_ctas=3)
+    np.testing.assert_array_equal(out, out2)  # deterministic fix-up
+
+
+def test_hgemm_stream_k_all_partial(felix):
+    # fewer tiles than CTAs: every tile is split over several CTAs
+    ref, out = _run(felix, 256, 512, 4096, nt=True, block_n=256, stream_k=2, max_ctas=7)
+    assert_fp16_close(ref, out, ctx="stream-K all partial")
+
+
+def test_hgemm_skinny_config_sampled(felix):
+    # config 3 shape: M=128, N=8192, K=16384, N(0, 0.02), exercises stream-K by default
+    from sion_b200.workloads import HGEMM_SKINNY, gemm_inputs
+    A, B = gemm_inputs(HGEMM_SKINNY)
+    C = torch.empty(128, 8192, dtype=torch.half, device="cuda")
+    felix.hgemm(A.cuda(), B.cuda(), C, b_layout=felix.B_NK)
+    torch.cuda.synchronize()
+    cols = np.arange(0, 8192, 37)
+    ref = oracle.hgemm(A.numpy(), B[cols].numpy(), True)
+    out = C.cpu().numpy()[:, cols].astype(np.float64)
+    assert_fp16_close(ref, out, ctx="skinny sampled")
+
+
+def test_hgemm_config2_sampled_rows(felix):
+    from sion_b200.workloads import HGEMM_4096, gemm_inputs
+    A, B = gemm_inputs(HGEMM_4096)
+    C = torch.empty(4096, 4096, dtype=torch.half, device="cuda")
+    felix.hgemm(A.cuda(), B.cuda(), C, b_layout=felix.B_NK)
+    torch.cuda.synchronize()
+    rows = np.r_[0:3, 127:130, 2047, 4093:4096]
+    ref = oracle.hgemm(A[rows].numpy(), B.numpy(), True)
+    out = C.cpu().numpy()[rows].astype(np.float64)
+    assert_fp16_close(ref, out, ctx="4096 sampled rows")
+
+
+def test_hgemm_k_zero(felix):
+    C0 = torch.randn(64, 64).half().cuda()
+    out = C0.clone()
+    A = torch.empty(64, 0, dtype=torch.half, device="cuda")
+    B = torch.empty(64, 0, dtype=torch.half, device="cuda")
+    felix.hgemm(A, B, out, 1.0, 2.0)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), (2 * C0.float()).half().cpu().numpy())
+
+
+def test_hgemm_rejects_unaligned_k(felix):
+    A = torch.zeros(128, 65, dtype=torch.half, device="cuda")
+    B = torch.zeros(128, 65, dtype=torch.half, device="cuda")
+    C = torch.zeros(128, 128, dtype=torch.half, device="cuda")
+    with pytest.raises(felix.FelixError) as e:
+        felix.hgemm(A, B, C)
+    assert e.value.code == felix.API_ERROR

@@ -1,0 +1,69 @@
+"""SGEMM parity through the C ABI against the fp64 CPU oracle.
+Gate (north star): relative Frobenius error <= 1e-5 vs the fp64 host product;
+plus the reference test's own max-abs 1e-3 (tests/sgemm/sgemm_test.cpp:44,62)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from metrics import compare
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(felix, M, N, K, alpha=1.0, beta=0.0, seed=0, split_k=None, dist="normal"):
+    g = torch.Generator().manual_seed(seed)
+    if dist == "normal":
+        A = torch.randn(M, K, generator=g)
+        B = torch.randn(K, N, generator=g)
+    else:
+        A = torch.rand(M, K, generator=g)
+        B = torch.rand(K, N, generator=g)
+    C0 = torch.randn(M, N, generator=g)
+    dA, dB, dC = A.cuda(), B.cuda(), C0.clone().cuda()
+    felix.sgemm(dA, dB, dC, alpha, beta, split_k=split_k)
+    torch.cuda.synchronize()
+    ref = oracle.sgemm(A.numpy(), B.numpy(), alpha, beta, C0.numpy())
+    return ref, dC.cpu().numpy()
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (128, 128, 8), (256, 384, 512),
+                                   (433, 477, 466), (1, 1, 1), (67, 45, 33), (5, 3000, 17),
+                                   (2048, 64, 4096)])
+def test_sgemm_shapes(felix, M, N, K):
+    ref, out = _run(felix, M, N, K)
+    m = compare(ref, out)
+    assert m["nan"] == 0 and m["rel_frob"] <= 1e-5, m
+
+
+@pytest.mark.parametrize("split_k", [1, 2, 3, 7])
+def test_sgemm_split_k_deterministic(felix, split_k):
+    ref, out = _run(felix, 512, 640, 1000, split_k=split_k)
+    m = compare(ref, out)
+    assert m["rel_frob"] <= 1e-5, m
+    _, out2 = _run(felix, 512, 640, 1000, split_k=split_k)
+    np.testing.assert_array_equal(out, out2)
+
+
+def test_sgemm_alpha_beta(felix):
+    ref, out = _run(felix, 300, 200, 100, alpha=0.4, beta=0.3)
+    m = compare(ref, out)
+    assert m["rel_frob"] <= 1e-5, m
+
+
+def test_sgemm_reference_test_cases(felix):
+    # tests/sgemm/sgemm_test.cpp:30-63: U(0,1), alpha = beta = 1, tol 1e-3 max-abs
+    for (M, N, K) in [(2048, 2048, 2048), (2048, 1536, 1024)]:
+        ref, out = _run(felix, M, N, K, alpha=1.0, beta=1.0, dist="uniform")
+        m = compare(ref, out)
+        assert m["max_abs"] <= 1e-3 and m["rel_frob"] <= 1e-5, m
+
+
+def test_sgemm_k_zero_scales_c(felix):
+    C0 = torch.randn(33, 17).cuda()
+    A = torch.empty(33, 0).cuda()
+    B = torch.empty(0, 17).cuda()
+    out = C0.clone()
+    felix.sgemm(A, B, out, 1.0, 0.5)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), 0.5 * C0.cpu().numpy(), rtol=1e-7)
