@@ -30,6 +30,14 @@ struct DeviceInfo {
 // Per-device facts for the current device (initialised once per device).
 DeviceInfo* current_device_info();
 
+// Scratch layout shared by every kernel that uses a workspace: a fixed block
+// of kWsMaxCounters 32-bit tile counters at offset 0 (always left at zero by
+// the kernels), then the fp32 partial tiles. Keeping the counters at a fixed
+// place lets operators share one buffer without clobbering each other's
+// zero invariant.
+constexpr size_t kWsCounterBytes = 16384;
+constexpr uint32_t kWsMaxCounters = kWsCounterBytes / 4;
+
 // Library-owned scratch for a (device, stream) pair, grown on demand and
 // zero-filled on (re)allocation. Kernels leave their counters at zero.
 void* library_workspace(DeviceInfo* dev, cudaStream_t stream, size_t bytes);
@@ -38,6 +46,10 @@ void* library_workspace(DeviceInfo* dev, cudaStream_t stream, size_t bytes);
 // `outer` rows, row pitch in bytes, box of box_inner x box_outer.
 int encode_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                        uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer);
+// 3-D fp16 tensor map, 128-byte swizzle: [outer2][outer1][inner].
+int encode_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer1,
+                       uint64_t outer2, uint64_t pitch1_bytes, uint64_t pitch2_bytes,
+                       uint32_t box_inner, uint32_t box_outer1, uint32_t box_outer2);
 // Same without swizzle (used for plain row stores / loads).
 int encode_tmap_2d_f16_noswizzle(CUtensorMap* map, const void* base, uint64_t inner,
                                  uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner,

@@ -1,7 +1,439 @@
+// Flash-attention forward for sm_100a, fp16 in/out, no mask:
+//   O = softmax(Q K^T * scale) V per (batch, head), plus the fp32 natural-log
+//   log-sum-exp of every query row.
+// Replaces the Ampere mma.sync kernel behind felix::ampere_flash_attn_launch
+// (reference: src/felix/flash_attention/ampere_flash_attn_mma16168_64_1D_warp_tiling_kernel_launch.cu:8-55,
+// kernels/ampere_flash_attn_mma16168_64_1D_warp_tiling.cuh:23-466), which keeps S
+// and O in fp16, fixes scale = 1/sqrt(D), requires seqlen % 64 == 0 and has no
+// LSE output. Here S and O accumulate in fp32 (TMEM), any seqlen >= 1 works
+// (TMA zero-fills the ragged tail, the softmax masks it), and LSE is written.
+//
+// Layout: Q, K, V, O are [B, H, S, D] contiguous; LSE is [B, H, S].
+//
+// CTA = one (b, h) and 256 query rows as two 128-row tiles "A" and "B".
+//   warp 0      TMA loader: Q_A, Q_B once; K_j, V_j through a smem ring
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 4-7   softmax of tile A (one query row per thread)
+//   warps 8-11  softmax of tile B
+// TMEM (512 columns): S_A | S_B | O_A | O_B, 128 columns each (D = 128);
+// P (fp16, two per 32-bit column) overwrites the first half of its S tile.
+// Per KV block j the issue order is
+//   PV_A(j-1), PV_B(j-1), S_A(j), S_B(j)
+// so the softmax of one tile overlaps the tensor-core work of the other.
+// S_X(j) is issued only after PV_X(j-1) completed (its P shares S_X's columns).
+// Online softmax in the log2 domain; O and l are rescaled only when the row
+// maximum grows by more than 8 (P then stays below 2^8, safe in fp16), and O
+// is normalised once at the end.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
 #include "felix_internal.h"
-namespace felix_impl {
-FelixCode flash_attn_launch(const __half*, const __half*, const __half*, __half*, float*, uint32_t,
-                            uint32_t, uint32_t, uint32_t, float, cudaStream_t) {
-  return api_error("flash attention: not built yet");
+#include "sm100_ptx.cuh"
+
+namespace felix_sm100 {
+namespace attn {
+
+constexpr int kBlockQ = 128;   // rows per Q tile (UMMA M)
+constexpr int kBlockKV = 128;  // keys per KV block (UMMA N of QK^T, K of PV)
+constexpr int kThreads = 384;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+template <int D>
+struct Cfg {
+  static constexpr int kStages = D == 128 ? 2 : 4;
+  static constexpr int kChunks = D / 64;                 // 128-byte swizzle chunks per row
+  static constexpr int kTileBytes = kBlockQ * D * 2;     // one 128 x D fp16 tile
+  static constexpr int kQOff = 0;                        // Q_A, Q_B
+  static constexpr int kKVOff = 2 * kTileBytes;          // ring of (K, V)
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kBarOff = kKVOff + kStages * kStageBytes;
+  static constexpr int kSmemBytes = kBarOff + 256 + 1024;
+};
+
+// TMEM columns of tile t's S (and P) and O accumulators.
+__device__ __forceinline__ uint32_t col_s(int t) { return uint32_t(t) * 128u; }
+__device__ __forceinline__ uint32_t col_o(int t) { return 256u + uint32_t(t) * 128u; }
+
+struct Params {
+  __half* O;
+  float* lse;
+  uint32_t S;        // sequence length
+  uint32_t n_kv;     // KV blocks
+  uint32_t q_tiles;  // CTAs per (b, h) along the query axis
+  float scale_log2;  // scale * log2(e)
+  unsigned* status;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
+
+// Smem descriptor of a K-major 128 x D tile (chunks of 64 columns, 16 KB each
+// for 128 rows), advanced to K step k (16 elements).
+template <int D>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int k) {
+  const uint32_t chunk = uint32_t(k) >> 2;
+  return make_sdesc_sw128(tile_addr + chunk * (kBlockQ * 128) + (uint32_t(k) & 3u) * 32, 16, 1024);
+}
+// Smem descriptor of V (kBlockKV rows x D, D contiguous) as the MN-major B
+// operand of PV, advanced to K step k (16 keys).
+template <int D>
+__device__ __forceinline__ uint64_t vmajor_desc(uint32_t tile_addr, int k) {
+  return make_sdesc_sw128(tile_addr + uint32_t(k) * 2048, kBlockKV * 128, 1024);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                          const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C_ = Cfg<D>;
+  constexpr int ST = C_::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
+  uint64_t* q_full = bars;                 // [1]
+  uint64_t* k_full = bars + 1;             // [ST]
+  uint64_t* v_full = bars + 1 + ST;        // [ST]
+  uint64_t* kv_empty = bars + 1 + 2 * ST;  // [ST]
+  uint64_t* s_full = bars + 1 + 3 * ST;    // [2]
+  uint64_t* p_full = s_full + 2;           // [2]
+  uint64_t* pv_done = s_full + 4;          // [2]
+  uint64_t* drain = s_full + 6;            // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = threadIdx.x / 32;
+  const uint32_t lane = threadIdx.x % 32;
+  const uint32_t bh = blockIdx.x / p.q_tiles;
+  const uint32_t q0 = (blockIdx.x % p.q_tiles) * (2 * kBlockQ);
+  const uint32_t n = p.n_kv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- loader
+    if (elect_one()) {
+      uint8_t* sq = smem + C_::kQOff;
+      mbar_arrive_expect_tx(q_full, 2 * C_::kTileBytes);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < C_::kChunks; ++c)
+          tma_load_3d(sq + t * C_::kTileBytes + c * (kBlockQ * 128), &tmQ, q_full, 64 * c,
+                      int(q0 + t * kBlockQ), int(bh));
+      uint32_t filled = 0;
+      for (uint32_t j = 0; j < n; ++j) {
+        const uint32_t st = j % ST;
+        const uint32_t ph = (j / ST) & 1u;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
+        uint8_t* sk = smem + C_::kKVOff + st * C_::kStageBytes;
+        uint8_t* sv = sk + C_::kTileBytes;
+        mbar_arrive_expect_tx(&k_full[st], C_::kTileBytes);
+#pragma unroll
+        for (int c = 0; c < C_::kChunks; ++c)
+          tma_load_3d(sk + c * (kBlockKV * 128), &tmK, &k_full[st], 64 * c, int(j * kBlockKV),
+                      int(bh));
+        mbar_arrive_expect_tx(&v_full[st], C_::kTileBytes);
+#pragma unroll
+        for (int c = 0; c < C_::kChunks; ++c)
+          tma_load_3d(sv + c * (kBlockKV * 128), &tmV, &v_full[st], 64 * c, int(j * kBlockKV),
+                      int(bh));
+        ++filled;
+      }
+      // drain: the last fill of each stage must land before the CTA exits
+      int dummy = 0;
+      mbar_wait(q_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
+      const uint32_t m = filled < uint32_t(ST) ? filled : uint32_t(ST);
+      for (uint32_t i = 0; i < m; ++i) {
+        const uint32_t f = filled - 1 - i;
+        mbar_wait(&k_full[f % ST], (f / ST) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
+        mbar_wait(&v_full[f % ST], (f / ST) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = make_idesc_f16_f32(kBlockQ, kBlockKV, false, false);
+      const uint32_t idesc_pv = make_idesc_f16_f32(kBlockQ, D, false, true);
+      const uint32_t sq = smem_u32(smem + C_::kQOff);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kWdAttnMma);
+      auto issue_s = [&](uint32_t j, int t) {
+        const uint32_t sk = smem_u32(smem + C_::kKVOff + (j % ST) * C_::kStageBytes);
+        const uint32_t qa = sq + t * C_::kTileBytes;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16_ss(tmem + col_s(t), kmajor_desc<D>(qa, k), kmajor_desc<D>(sk, k),
+                      idesc_qk, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](uint32_t j, int t) {
+        const uint32_t sv =
+            smem_u32(smem + C_::kKVOff + (j % ST) * C_::kStageBytes + C_::kTileBytes);
+#pragma unroll
+        for (int k = 0; k < kBlockKV / 16; ++k)
+          umma_f16_ts(tmem + col_o(t), tmem + col_s(t) + k * 8, vmajor_desc<D>(sv, k),
+                      idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&pv_done[t]);
+      };
+      if (ok && n > 0) {
+        ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, kWdAttnMma);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, 0);
+          issue_s(0, 1);
+        }
+      }
+      for (uint32_t j = 0; ok && j < n; ++j) {
+        const uint32_t st = j % ST, ph = (j / ST) & 1u;
+        // PV for block j of both tiles
+        if (!(ok = mbar_wait(&v_full[st], ph, abort_flag, p.status, kWdAttnMma))) break;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!(ok = mbar_wait(&p_full[t], j & 1u, abort_flag, p.status, kWdAttnMma))) break;
+          tc_fence_after();
+          issue_pv(j, t);
+        }
+        if (!ok) break;
+        umma_commit(&kv_empty[st]);
+        // S for block j+1 of both tiles, each after its PV(j) completed
+        if (j + 1 < n) {
+          const uint32_t st1 = (j + 1) % ST, ph1 = ((j + 1) / ST) & 1u;
+          if (!(ok = mbar_wait(&k_full[st1], ph1, abort_flag, p.status, kWdAttnMma))) break;
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!(ok = mbar_wait(&pv_done[t], j & 1u, abort_flag, p.status, kWdAttnMma))) break;
+            tc_fence_after();
+            issue_s(j + 1, t);
+          }
+        }
+      }
+      umma_commit(drain);
+      int dummy = 0;
+      mbar_wait(drain, 0, &dummy, p.status, kWdDrain, 100000000ull);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- softmax
+    const int t = warp >= 8 ? 1 : 0;
+    const uint32_t q = warp & 3u;
+    const uint32_t row = q * 32 + lane;  // row within the tile == TMEM lane
+    const uint32_t lane_addr = (q * 32u) << 16;
+    const uint32_t tS = tmem + lane_addr + col_s(t);
+    const uint32_t tO = tmem + lane_addr + col_o(t);
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY;  // running max in log2 units (the one P is relative to)
+    float l = 0.f;
+    bool ok = true;
+    for (uint32_t j = 0; j < n; ++j) {
+      if (!(ok = mbar_wait(&s_full[t], j & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
+      tc_fence_after();
+      float s[kBlockKV];
+#pragma unroll
+      for (int c = 0; c < kBlockKV; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tS + c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(r[i]);
+      }
+      tmem_ld_wait();
+      const uint32_t valid = p.S - j * kBlockKV;  // keys left in this block
+      if (valid < uint32_t(kBlockKV)) {
+#pragma unroll
+        for (int i = 0; i < kBlockKV; ++i)
+          if (uint32_t(i) >= valid) s[i] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < kBlockKV; ++i) mx = fmaxf(mx, s[i]);
+      const float mc = mx * sl2;
+      const bool need = mc > m + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_new = need ? mc : m;
+        const float alpha = ex2(m - m_new);  // 0 when m == -inf
+        l *= alpha;
+        m = m_new;
+        if (j > 0) {
+          // O_t holds PV(0..j-1): rescale it once PV(j-1) has completed.
+          if (!(ok = mbar_wait(&pv_done[t], (j - 1) & 1u, abort_flag, p.status,
+                               kWdAttnCorrection)))
+            break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D; c += 16) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(tO + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st_32x32b_x16(tO + c, r);
+          }
+        }
+      }
+      const float neg_m = -m;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBlockKV; c += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2(fmaf(s[c + 2 * i], sl2, neg_m));
+          const float p1 = ex2(fmaf(s[c + 2 * i + 1], sl2, neg_m));
+          rs += p0 + p1;
+          pk[i] = pack_half2(p0, p1);
+        }
+        tmem_st_32x32b_x16(tS + c / 2, pk);
+      }
+      l += rs;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    // ---------------------------------------------------------------- epilogue
+    if (ok && n > 0 &&
+        mbar_wait(&pv_done[t], (n - 1) & 1u, abort_flag, p.status, kWdAttnSoftmax)) {
+      tc_fence_after();
+      const uint32_t qrow = q0 + t * kBlockQ + row;
+      const float inv_l = 1.f / l;
+      __half* dst = p.O + (size_t(bh) * p.S + qrow) * D;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tO + c, r);
+        tmem_ld_wait();
+        if (qrow < p.S) {
+          uint4 o4[4];
+          uint32_t* o = reinterpret_cast<uint32_t*>(o4);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            o[i] = pack_half2(__uint_as_float(r[2 * i]) * inv_l,
+                              __uint_as_float(r[2 * i + 1]) * inv_l);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = o4[i];
+        }
+      }
+      if (p.lse && qrow < p.S)
+        p.lse[size_t(bh) * p.S + qrow] = (m + __log2f(l)) * 0.69314718055994531f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace attn
+}  // namespace felix_sm100
+
+// ============================================================ host launcher
+namespace felix_impl {
+
+using namespace felix_sm100::attn;
+
+namespace {
+
+int encode_qkv(CUtensorMap* map, const void* base, uint32_t BH, uint32_t S, uint32_t D) {
+  // 3-D view [BH][S][D] so that a tile never crosses into the next head:
+  // rows past S are zero-filled by the TMA unit.
+  static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
+  return encode_tmap_3d_f16(map, base, D, S, BH, uint64_t(D) * 2, uint64_t(S) * D * 2, 64,
+                            kBlockQ, 1);
+}
+
+template <int D>
+int configure_once(int device) {
+  static int done[64] = {0};
+  if (device < 0 || device >= 64) return -1;
+  if (!done[device]) {
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_fwd_kernel<D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<D>::kSmemBytes);
+    if (e != cudaSuccess) return int(e);
+    done[device] = 1;
+  }
+  return 0;
+}
+
+}  // namespace
+
+FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, __half* O,
+                            float* lse, uint32_t heads, uint32_t batch, uint32_t seqlen,
+                            uint32_t head_dim, float scale, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128)
+    return api_error("flash_attn: head_dim must be 64 or 128");
+  if (heads == 0 || batch == 0 || seqlen == 0) return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  if (!Q || !K || !V || !O) return api_error("flash_attn: null pointer");
+  if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+       reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(O)) & 15u)
+    return api_error("flash_attn: Q, K, V, O must be 16-byte aligned");
+  const uint64_t bh = uint64_t(heads) * batch;
+  if (bh > (1u << 31) || seqlen > (1u << 30)) return api_error("flash_attn: problem too large");
+  DeviceInfo* dev = current_device_info();
+  if (!dev) return launch_error(cudaGetLastError(), "flash_attn: no CUDA device");
+
+  CUtensorMap tq, tk, tv;
+  if (encode_qkv(&tq, Q, uint32_t(bh), seqlen, head_dim) ||
+      encode_qkv(&tk, K, uint32_t(bh), seqlen, head_dim) ||
+      encode_qkv(&tv, V, uint32_t(bh), seqlen, head_dim))
+    return api_error("flash_attn: cuTensorMapEncodeTiled failed");
+
+  Params p{};
+  p.O = O;
+  p.lse = lse;
+  p.S = seqlen;
+  p.n_kv = (seqlen + kBlockKV - 1) / kBlockKV;
+  p.q_tiles = (seqlen + 2 * kBlockQ - 1) / (2 * kBlockQ);
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf(float(head_dim));
+  p.scale_log2 = sc * 1.4426950408889634f;
+  p.status = dev->status_word;
+  const uint64_t grid = bh * p.q_tiles;
+  if (grid > 0x7fffffffull) return api_error("flash_attn: grid too large");
+
+  int rc;
+  if (head_dim == 128) {
+    if ((rc = configure_once<128>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    flash_attn_fwd_kernel<128><<<unsigned(grid), kThreads, Cfg<128>::kSmemBytes, stream>>>(tq, tk, tv, p);
+  } else {
+    if ((rc = configure_once<64>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    flash_attn_fwd_kernel<64><<<unsigned(grid), kThreads, Cfg<64>::kSmemBytes, stream>>>(tq, tk, tv, p);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return launch_error(e, "flash_attn: launch failed");
+  return FelixCode{FELIX_SUCCESS, cudaSuccess};
+}
+
 }  // namespace felix_impl

@@ -58,8 +58,8 @@ struct Params {
   uint32_t dp_tiles, sk_tiles;
   uint64_t sk_iters;
   uint32_t group_m;
-  float* ws_partials;     // [gridDim.x][2][BM*BN]
-  unsigned* ws_counters;  // [sk_tiles]
+  float* ws_partials;     // [gridDim.x][2] slots of BM*BN fp32, see partial_index()
+  unsigned* ws_counters;  // [sk_tiles], zero between launches
   unsigned* status;       // watchdog word
 };
 
@@ -133,6 +133,12 @@ __device__ __forceinline__ void tile_coords(const Params& p, uint32_t t, uint32_
   const uint32_t r = t - g * per_group;
   tm = first_m + r % gm;
   tn = r / gm;
+}
+
+// Float4 index of (chunk c of 32 columns, float4 j within the chunk, row r) in
+// a partial-tile slot: a warp's 32 rows touch 512 contiguous bytes.
+__device__ __forceinline__ uint32_t partial_index(uint32_t c, uint32_t j, uint32_t r) {
+  return (c * 8u + j) * BM + r;
 }
 
 // Convert 32 fp32 accumulators (columns c..c+31 of row `row`) and store to C.
@@ -350,19 +356,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         // Stream-K contribution: publish the fp32 partial, take a ticket.
-        float* slot = p.ws_partials + (size_t(sc.cta) * 2 + u.seg) * (BM * BN) +
-                      size_t(row_in_tile) * BN;
+        float4* slot = reinterpret_cast<float4*>(p.ws_partials) +
+                       (size_t(sc.cta) * 2 + u.seg) * (BM * BN / 4);
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(taddr + c, r);
           tmem_ld_wait();
-          float4* d4 = reinterpret_cast<float4*>(slot + c);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            __stcg(d4 + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                       __uint_as_float(r[4 * j + 2]),
-                                       __uint_as_float(r[4 * j + 3])));
+            __stcg(slot + partial_index(c / 32, j, row_in_tile),
+                   make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
         }
         __threadfence();
         named_barrier_sync(1, 128);
@@ -380,26 +385,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool last = *bcast != 0;
         if (last) {
           __threadfence();
+          // Sum the partials in contributor order (deterministic), two
+          // 32-column chunks at a time so 16 loads are in flight per thread.
 #pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            float v[32];
+          for (int c = 0; c < BN; c += 64) {
+            float v0[32], v1[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            for (int j = 0; j < 32; ++j) v0[j] = v1[j] = 0.f;
+#pragma unroll 1
             for (uint32_t cc = c_first; cc <= c_last; ++cc) {
               const uint32_t seg = (sc.I * cc / sc.P) / sc.KB == u.sk ? 0u : 1u;
-              const float4* s4 = reinterpret_cast<const float4*>(
-                  p.ws_partials + (size_t(cc) * 2 + seg) * (BM * BN) +
-                  size_t(row_in_tile) * BN + c);
+              const float4* s4 = reinterpret_cast<const float4*>(p.ws_partials) +
+                                 (size_t(cc) * 2 + seg) * (BM * BN / 4);
+              float4 x0[8], x1[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const float4 x = __ldcg(s4 + j);
-                v[4 * j] += x.x;
-                v[4 * j + 1] += x.y;
-                v[4 * j + 2] += x.z;
-                v[4 * j + 3] += x.w;
+                x0[j] = __ldcg(s4 + partial_index(c / 32, j, row_in_tile));
+                x1[j] = __ldcg(s4 + partial_index(c / 32 + 1, j, row_in_tile));
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                v0[4 * j] += x0[j].x; v0[4 * j + 1] += x0[j].y;
+                v0[4 * j + 2] += x0[j].z; v0[4 * j + 3] += x0[j].w;
+                v1[4 * j] += x1[j].x; v1[4 * j + 1] += x1[j].y;
+                v1[4 * j + 2] += x1[j].z; v1[4 * j + 3] += x1[j].w;
               }
             }
-            store_row_chunk(p, row, col0 + c, v);
+            store_row_chunk(p, row, col0 + c, v0);
+            store_row_chunk(p, row, col0 + c + 32, v1);
           }
         }
         // keep the broadcast slot stable until all threads have read it
@@ -494,7 +507,7 @@ size_t hgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const HgemmOpti
                              int num_sms) {
   Plan pl = make_plan(M, N, K, o, num_sms);
   if (pl.sk_tiles == 0) return 0;
-  return size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float) + size_t(pl.grid) * sizeof(unsigned);
+  return kWsCounterBytes + size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float);
 }
 
 FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __half* A,
@@ -547,17 +560,16 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   p.group_m = 16;
   p.status = dev->status_word;
   if (pl.sk_tiles) {
-    const size_t need = size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float) +
-                        size_t(pl.grid) * sizeof(unsigned);
+    const size_t need = kWsCounterBytes + size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float);
     if (!workspace) {
       workspace = library_workspace(dev, stream, need);
       if (!workspace) return launch_error(cudaErrorMemoryAllocation, "hgemm: workspace");
     } else if (ws_bytes < need) {
       return api_error("hgemm: workspace too small");
     }
-    p.ws_partials = static_cast<float*>(workspace);
-    p.ws_counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) +
-                                                size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float));
+    p.ws_counters = static_cast<unsigned*>(workspace);
+    p.ws_partials =
+        reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
   }
 
   cudaError_t e;

@@ -230,6 +230,7 @@ uint32_t choose_splits(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o
   }
   const uint32_t kblocks = (K + BK - 1) / BK;
   if (s > kblocks) s = kblocks ? kblocks : 1;
+  if (tiles > kWsMaxCounters) s = 1;  // one counter per tile lives in the fixed block
   return s;
 }
 }  // namespace
@@ -239,7 +240,7 @@ size_t sgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const SgemmOpti
   const uint32_t s = choose_splits(M, N, K, o, num_sms);
   if (s <= 1) return 0;
   const size_t tiles = size_t((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  return tiles * s * BM * BN * sizeof(float) + tiles * sizeof(unsigned);
+  return kWsCounterBytes + tiles * s * BM * BN * sizeof(float);
 }
 
 FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const float* A,
@@ -269,16 +270,15 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
   if (grid.y > 65535u) return api_error("sgemm: M too large");
   if (p.splits > 1) {
     const size_t tiles = size_t(grid.x) * grid.y;
-    const size_t need = tiles * p.splits * BM * BN * sizeof(float) + tiles * sizeof(unsigned);
+    const size_t need = kWsCounterBytes + tiles * p.splits * BM * BN * sizeof(float);
     if (!workspace) {
       workspace = library_workspace(dev, stream, need);
       if (!workspace) return launch_error(cudaErrorMemoryAllocation, "sgemm: workspace");
     } else if (ws_bytes < need) {
       return api_error("sgemm: workspace too small");
     }
-    p.ws = static_cast<float*>(workspace);
-    p.counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) +
-                                             tiles * p.splits * BM * BN * sizeof(float));
+    p.counters = static_cast<unsigned*>(workspace);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
   }
   const bool vec = (K % 4 == 0) && (N % 4 == 0) &&
                    ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |

@@ -1,0 +1,102 @@
+"""Flash-attention forward (tcgen05) parity through the C ABI against the fp64
+CPU oracle. Gate (north star): max-abs <= 1e-2 and rel-Frobenius <= 1e-3 on O;
+LSE (new output, natural log) within 1e-3 relative."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from metrics import compare
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(B, H, S, D, seed):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(B, H, S, D, generator=g).half() for _ in range(3)]
+
+
+def _run(felix, B, H, S, D, seed=0, rows=None, scale=0.0):
+    Q, K, V = _inputs(B, H, S, D, seed)
+    O = torch.empty(B, H, S, D, dtype=torch.half, device="cuda")
+    L = torch.empty(B, H, S, device="cuda")
+    felix.flash_attn_fwd(Q.cuda(), K.cuda(), V.cuda(), O, L, scale=scale)
+    torch.cuda.synchronize()
+    Oref, Lref = oracle.attention(Q.numpy(), K.numpy(), V.numpy(), scale=scale, rows=rows)
+    o = O.cpu().numpy().astype(np.float64)
+    l = L.cpu().numpy().astype(np.float64)
+    if rows is not None:
+        o, l = o[:, :, rows], l[:, :, rows]
+    return Oref, Lref, o, l
+
+
+def _check(Oref, Lref, o, l, ctx):
+    m = compare(Oref, o)
+    assert m["nan"] == 0 and m["inf"] == 0, (ctx, m)
+    assert m["max_abs"] <= 1e-2, (ctx, m)
+    assert m["rel_frob"] <= 1e-3, (ctx, m)
+    ml = compare(Lref, l)
+    assert ml["max_rel"] <= 1e-3 and ml["max_abs"] <= 1e-3 * max(1.0, np.abs(Lref).max()), (ctx, ml)
+
+
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("S", [128, 256, 512, 1024])
+def test_attention_aligned(felix, S, D):
+    _check(*_run(felix, 1, 2, S, D), ctx=f"S={S} D={D}")
+
+
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("S", [1, 17, 64, 130, 200, 333, 1000])
+def test_attention_ragged(felix, S, D):
+    _check(*_run(felix, 2, 1, S, D, seed=S), ctx=f"S={S} D={D}")
+
+
+def test_attention_reference_test_case(felix):
+    # tests/flash_attention/fa_test.cpp:24-42: B=16, H=16, N=1280, D=128, tol 1e-2;
+    # rows sampled for the CPU oracle
+    rows = np.r_[0:5, 640, 1000, 1275:1280]
+    _check(*_run(felix, 16, 16, 1280, 128, seed=0, rows=rows), ctx="fa_test 16x16x1280x128")
+
+
+def test_attention_custom_scale(felix):
+    _check(*_run(felix, 1, 1, 300, 64, seed=5, scale=0.05), ctx="scale 0.05")
+
+
+def test_attention_large_logits_rescale(felix):
+    # growing scores force the conditional O rescale path many times
+    B, H, S, D = 1, 1, 1024, 128
+    g = torch.Generator().manual_seed(9)
+    Q = (torch.randn(B, H, S, D, generator=g) * 3).half()
+    K = (torch.randn(B, H, S, D, generator=g) * 3 * torch.linspace(0.2, 2.0, S).view(1, 1, S, 1)).half()
+    V = torch.randn(B, H, S, D, generator=g).half()
+    O = torch.empty(B, H, S, D, dtype=torch.half, device="cuda")
+    L = torch.empty(B, H, S, device="cuda")
+    felix.flash_attn_fwd(Q.cuda(), K.cuda(), V.cuda(), O, L)
+    torch.cuda.synchronize()
+    Oref, Lref = oracle.attention(Q.numpy(), K.numpy(), V.numpy())
+    _check(Oref, Lref, O.cpu().numpy().astype(np.float64), L.cpu().numpy().astype(np.float64),
+           "large logits")
+
+
+def test_attention_config4_sampled(felix):
+    # config 4 shape [4, 32, 8192, 128], seed 3; oracle on sampled rows of 3 heads
+    from sion_b200.workloads import FA_8192, attn_inputs
+    Q, K, V = attn_inputs(FA_8192)
+    O = torch.empty_like(Q, device="cuda")
+    L = torch.empty(4, 32, 8192, device="cuda")
+    felix.flash_attn_fwd(Q.cuda(), K.cuda(), V.cuda(), O, L)
+    torch.cuda.synchronize()
+    rows = np.r_[0, 1, 4095, 8190, 8191]
+    for (b, h) in [(0, 0), (1, 17), (3, 31)]:
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        Oref, Lref = oracle.attention(Q[sl].numpy(), K[sl].numpy(), V[sl].numpy(), rows=rows)
+        o = O[sl].cpu().numpy()[:, :, rows].astype(np.float64)
+        l = L[sl].cpu().numpy()[:, :, rows].astype(np.float64)
+        _check(Oref, Lref, o, l, ctx=f"config4 b={b} h={h}")
+
+
+def test_attention_rejects_bad_head_dim(felix):
+    Q = torch.zeros(1, 1, 64, 96, dtype=torch.half, device="cuda")
+    with pytest.raises(felix.FelixError) as e:
+        felix.flash_attn_fwd(Q, Q, Q, torch.empty_like(Q))
+    assert e.value.code == felix.API_ERROR
