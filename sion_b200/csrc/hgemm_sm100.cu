@@ -45,8 +45,10 @@ struct Cfg {
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
-  // ring + 1 KB alignment slack + barrier block
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  // epilogue staging for TMA stores: 4 warps x 2 buffers x (32 rows x 128 B)
+  static constexpr int kStagingBytes = 4 * 2 * 4096;
+  // ring + staging + 1 KB alignment slack + barrier block
+  static constexpr int kSmemBytes = kStages * kStageBytes + kStagingBytes + 1024 + 256;
 };
 
 struct Params {
@@ -58,6 +60,7 @@ struct Params {
   uint32_t dp_tiles, sk_tiles;
   uint64_t sk_iters;
   uint32_t group_m;
+  uint32_t tma_store;     // 1: epilogue writes C through smem + TMA (beta == 0)
   float* ws_partials;     // [gridDim.x][2] slots of BM*BN fp32, see partial_index()
   unsigned* ws_counters;  // [sk_tiles], zero between launches
   unsigned* status;       // watchdog word
@@ -72,24 +75,43 @@ struct Unit {
 };
 
 // Identical walk for the producer, MMA and epilogue roles of one CTA.
+// Stream-K units come first (tiles [0, sk_tiles) spread over all CTAs by
+// k-iterations), then whole tiles sk_tiles + cta + i * P. Doing the split tiles
+// first lets their fix-up in the epilogue warps overlap the main loop of the
+// following whole tiles instead of forming a tail.
 struct Sched {
-  uint32_t cta, P, dp_tiles, KB;
+  uint32_t cta, P, sk_tiles, tiles, KB;
   uint64_t I, it, end, start;
   uint32_t dp_next;
 
   __device__ __forceinline__ void init(const Params& p) {
     cta = blockIdx.x;
     P = gridDim.x;
-    dp_tiles = p.dp_tiles;
+    sk_tiles = p.sk_tiles;
+    tiles = p.sk_tiles + p.dp_tiles;
     KB = p.kblocks;
     I = p.sk_iters;
     start = I * cta / P;
     end = I * (cta + 1) / P;
     it = start;
-    dp_next = cta;
+    dp_next = sk_tiles + cta;
   }
   __device__ __forceinline__ bool next(Unit& u) {
-    if (dp_next < dp_tiles) {
+    if (it < end) {
+      const uint32_t s = static_cast<uint32_t>(it / KB);
+      const uint32_t kb0 = static_cast<uint32_t>(it - uint64_t(s) * KB);
+      const uint64_t left = end - it;
+      const uint32_t kb1 = left < uint64_t(KB - kb0) ? kb0 + static_cast<uint32_t>(left) : KB;
+      u.tile = s;
+      u.kb0 = kb0;
+      u.kb1 = kb1;
+      u.sk = s;
+      u.seg = (it == start) ? 0u : 1u;
+      u.partial = !(kb0 == 0 && kb1 == KB);
+      it += kb1 - kb0;
+      return true;
+    }
+    if (dp_next < tiles) {
       u.tile = dp_next;
       u.kb0 = 0;
       u.kb1 = KB;
@@ -97,21 +119,6 @@ struct Sched {
       u.sk = 0;
       u.seg = 0;
       dp_next += P;
-      return true;
-    }
-    if (it < end) {
-      const uint32_t s = static_cast<uint32_t>(it / KB);
-      const uint32_t kb0 = static_cast<uint32_t>(it - uint64_t(s) * KB);
-      const uint64_t left = end - it;
-      const uint32_t kb1 = left < uint64_t(KB - kb0) ? kb0 + static_cast<uint32_t>(left) : KB;
-      u.tile = dp_tiles + s;
-      u.kb0 = kb0;
-      u.kb1 = kb1;
-      u.sk = s;
-      u.seg = (it == start) ? 0u : 1u;
-      u.partial = !(kb0 == 0 && kb1 == KB);
-      it += kb1 - kb0;
-      dp_next = dp_tiles;  // dp phase is over
       return true;
     }
     return false;
@@ -183,14 +190,16 @@ __device__ __forceinline__ void store_row_chunk(const Params& p, uint32_t row, u
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
-                            const __grid_constant__ CUtensorMap tmB, const Params p) {
+                            const __grid_constant__ CUtensorMap tmB,
+                            const __grid_constant__ CUtensorMap tmC, const Params p) {
   using C_ = Cfg<BN>;
   constexpr int S = C_::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C_::kStageBytes);
+  uint8_t* staging = smem + S * C_::kStageBytes;  // 1 KB aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + C_::kStagingBytes);
   uint64_t* full = bars;               // [S]
   uint64_t* empty = bars + S;          // [S]
   uint64_t* tfull = bars + 2 * S;      // [2]
@@ -217,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.tma_store) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C_::kTmemCols);
@@ -343,7 +353,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t col0 = tn * BN;
       const uint32_t taddr = tmem_base + ((q * 32u) << 16) + buf * BN;
 
-      if (!u.partial) {
+      if (!u.partial && p.tma_store) {
+        // 64-column chunks: TMEM -> registers -> fp16 -> 128-byte-swizzled
+        // smem rows (conflict-free) -> one TMA store of 32 rows x 64 columns
+        // per warp. Two staging buffers per warp; TMA clips the ragged edge.
+        uint8_t* stg = staging + (warp - 2) * 8192;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(taddr + c, r0);
+          tmem_ld_32x32b_x32(taddr + c + 32, r1);
+          tmem_ld_wait();
+          uint8_t* buf = stg + ((c / 64) & 1) * 4096;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* src = j < 4 ? &r0[8 * j] : &r1[8 * (j - 4)];
+            uint4 v;
+            v.x = pack_half2(p.alpha * __uint_as_float(src[0]), p.alpha * __uint_as_float(src[1]));
+            v.y = pack_half2(p.alpha * __uint_as_float(src[2]), p.alpha * __uint_as_float(src[3]));
+            v.z = pack_half2(p.alpha * __uint_as_float(src[4]), p.alpha * __uint_as_float(src[5]));
+            v.w = pack_half2(p.alpha * __uint_as_float(src[6]), p.alpha * __uint_as_float(src[7]));
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((uint32_t(j) ^ (lane & 7u)) * 16)) = v;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, buf, int(col0 + c), int(tm * BM + q * 32));
+            bulk_commit_group();
+          }
+        }
+      } else if (!u.partial) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -423,6 +464,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[buf]);
       ++i;
     }
+    // staging smem must stay valid until the TMA stores have read it
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -543,7 +587,17 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
     rc = encode_tmap_2d_f16(&tmB, B, K, N, uint64_t(K) * 2, BK, pl.bn);
   if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
 
+  // C through TMA when nothing has to be read back (beta == 0) and its rows
+  // are 16-byte multiples.
+  CUtensorMap tmC;
+  const bool tma_store = beta == 0.f && (N % 8 == 0) &&
+                         (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
+  if (tma_store && encode_tmap_2d_f16(&tmC, C, N, M, uint64_t(N) * 2, 64, 32))
+    return api_error("hgemm: cuTensorMapEncodeTiled(C) failed");
+  if (!tma_store) tmC = tmA;  // unused placeholder
+
   Params p{};
+  p.tma_store = tma_store ? 1u : 0u;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -576,11 +630,11 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   if (pl.bn == 256) {
     if ((rc = configure_once<256>(dev->ordinal)))
       return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    hgemm_persistent_kernel<256><<<pl.grid, kThreads, Cfg<256>::kSmemBytes, stream>>>(tmA, tmB, p);
+    hgemm_persistent_kernel<256><<<pl.grid, kThreads, Cfg<256>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
   } else {
     if ((rc = configure_once<128>(dev->ordinal)))
       return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    hgemm_persistent_kernel<128><<<pl.grid, kThreads, Cfg<128>::kSmemBytes, stream>>>(tmA, tmB, p);
+    hgemm_persistent_kernel<128><<<pl.grid, kThreads, Cfg<128>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return launch_error(e, "hgemm: launch failed");
