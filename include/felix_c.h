@@ -81,7 +81,7 @@ int felix_hgemm(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* A, 
 /*
  * HGEMM with explicit schedule and caller-owned workspace (no reference
  * counterpart; the reference has no split-K / stream-K).
- * block_n: 0 auto, 128 or 256. stream_k: 0 auto, 1 off, 2 on whenever the last
+ * block_n: 0 auto, 64, 128 or 256. stream_k: 0 auto, 1 off, 2 on whenever the last
  * wave of tiles is incomplete. max_ctas: 0 = one persistent CTA per SM.
  * workspace: NULL = library-owned per-(device, stream) scratch; otherwise at
  * least felix_hgemm_workspace_size() bytes, zero-filled before first use.

@@ -59,7 +59,7 @@ FelixCode scale_half_matrix(__half* C, size_t n, float beta, cudaStream_t stream
 FelixCode scale_float_matrix(float* C, size_t n, float beta, cudaStream_t stream);
 
 struct HgemmOptions {
-  int block_n = 0;   // 0 = auto, 128 or 256
+  int block_n = 0;   // 0 = auto, 64, 128 or 256
   int stream_k = 0;  // 0 = auto, 1 = off, 2 = on whenever the last wave is partial
   int max_ctas = 0;  // 0 = one per SM; otherwise cap the persistent grid
 };

@@ -11,19 +11,21 @@
 // Layout: Q, K, V, O are [B, H, S, D] contiguous; LSE is [B, H, S].
 //
 // CTA = one (b, h) and 256 query rows as two 128-row tiles "A" and "B".
-//   warp 0      TMA loader: Q_A, Q_B once; K_j, V_j through a smem ring
+//   warp 0      TMA loader: Q_A, Q_B once, then the K ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warp 2      TMA loader of the V ring
 //   warps 4-7   softmax of tile A (one query row per thread)
 //   warps 8-11  softmax of tile B
 // TMEM (512 columns): S_A | S_B | O_A | O_B, 128 columns each (D = 128);
 // P (fp16, two per 32-bit column) overwrites the first half of its S tile.
-// Per KV block j the issue order is
-//   PV_A(j-1), PV_B(j-1), S_A(j), S_B(j)
-// so the softmax of one tile overlaps the tensor-core work of the other.
-// S_X(j) is issued only after PV_X(j-1) completed (its P shares S_X's columns).
-// Online softmax in the log2 domain; O and l are rescaled only when the row
-// maximum grows by more than 8 (P then stays below 2^8, safe in fp16), and O
-// is normalised once at the end.
+// Per KV block j the issue order is PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), so
+// the softmax of one tile overlaps the tensor-core work of the other. S_t(j+1)
+// is issued right behind PV_t(j): the tensor pipe executes a CTA's MMAs in
+// issue order, so S_t(j+1)'s writes cannot overtake PV_t(j)'s reads of P_t.
+// K and V have separate rings so K(j+1) streams in while V(j) is still used.
+// Online softmax in the log2 domain with packed fp32x2 arithmetic; O and l are
+// rescaled only when the row maximum grows by more than 8 (P then stays below
+// 2^8, safe in fp16), and O is normalised once at the end.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -42,13 +44,14 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int D>
 struct Cfg {
-  static constexpr int kStages = D == 128 ? 2 : 4;
+  static constexpr int kKStages = D == 128 ? 3 : 4;      // K ring
+  static constexpr int kVStages = D == 128 ? 2 : 4;      // V ring
   static constexpr int kChunks = D / 64;                 // 128-byte swizzle chunks per row
   static constexpr int kTileBytes = kBlockQ * D * 2;     // one 128 x D fp16 tile
   static constexpr int kQOff = 0;                        // Q_A, Q_B
-  static constexpr int kKVOff = 2 * kTileBytes;          // ring of (K, V)
-  static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kBarOff = kKVOff + kStages * kStageBytes;
+  static constexpr int kKOff = 2 * kTileBytes;
+  static constexpr int kVOff = kKOff + kKStages * kTileBytes;
+  static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;
 };
 
@@ -66,10 +69,90 @@ struct Params {
   unsigned* status;
 };
 
+#ifdef FELIX_FA_TRACE
+// Development-only phase trace of CTA 0 (compiled out of the library build):
+// [role][block j][event] = clock64 value.
+__device__ unsigned long long g_fa_trace[3][64][8];
+#define FA_TRACE(role, j, ev)                                           \
+  do {                                                                  \
+    if (blockIdx.x == 0 && (j) < 64) g_fa_trace[role][j][ev] = clock64(); \
+  } while (0)
+#else
+#define FA_TRACE(role, j, ev) \
+  do {                        \
+  } while (0)
+#endif
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32x2 arithmetic (sm_100): two lanes of fp32 in one 64-bit register,
+// one instruction for both.
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float lo_f32(uint64_t v) {
+  return __uint_as_float(static_cast<uint32_t>(v));
+}
+__device__ __forceinline__ float hi_f32(uint64_t v) {
+  return __uint_as_float(static_cast<uint32_t>(v >> 32));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+#ifndef FELIX_FA_EMU_EVERY
+#define FELIX_FA_EMU_EVERY 0
+#endif
+#ifndef FELIX_FA_WAIT_PV
+#define FELIX_FA_WAIT_PV 0
+#endif
+// 1: S_t(j+1) is issued only after PV_t(j) has completed. 0: it is issued
+// right behind PV_t(j); tcgen05.mma operations of a CTA execute in issue
+// order, so the later MMA's accumulator writes to S_t cannot overtake the
+// earlier MMA's reads of P_t from the same columns.
+constexpr int kWaitPV = FELIX_FA_WAIT_PV;
+// One column pair in kEmuEvery takes its exponentials on the FMA pipe
+// (exp2_fma_x2) instead of MUFU; 0 disables the split.
+constexpr int kEmuEvery = FELIX_FA_EMU_EVERY;
+
+// 2^x for two lanes on the FMA pipe, x <= 8 (softmax exponents are relative to
+// a running max that is at most 8 below the true one). Range reduction
+// x = j + f with j = round(x) (magic-number add), f in [-1/2, 1/2]; 2^f from a
+// degree-3 polynomial fitted here by a Remez exchange on the relative error
+// over [-1/2, 1/2] (max relative error 7.5e-5 in fp32 evaluation, below the
+// fp16 half-ulp 4.9e-4 of P); 2^j is added into the exponent field. Inputs are
+// clamped at -125 so masked keys (-inf) give 2^-125, which rounds to 0 in fp16.
+__device__ __forceinline__ uint64_t exp2_fma_x2(uint64_t x2) {
+  const float x0 = fmaxf(lo_f32(x2), -125.0f), x1 = fmaxf(hi_f32(x2), -125.0f);
+  const uint64_t x = pack_f32x2(x0, x1);
+  const uint64_t t = fadd2(x, pack_f32x2(12582912.0f, 12582912.0f));  // 1.5 * 2^23
+  const uint64_t jf = fadd2(t, pack_f32x2(-12582912.0f, -12582912.0f));
+  const uint64_t f = ffma2(jf, pack_f32x2(-1.0f, -1.0f), x);
+  uint64_t p = ffma2(pack_f32x2(0.0551716685295105f, 0.0551716685295105f), f,
+                     pack_f32x2(0.2426111251115799f, 0.2426111251115799f));
+  p = ffma2(p, f, pack_f32x2(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, pack_f32x2(0.9999280571937561f, 0.9999280571937561f));
+  const float r0 = __int_as_float(__float_as_int(lo_f32(p)) + (__float_as_int(lo_f32(t)) << 23));
+  const float r1 = __int_as_float(__float_as_int(hi_f32(p)) + (__float_as_int(hi_f32(t)) << 23));
+  return pack_f32x2(r0, r1);
 }
 
 // Smem descriptor of a K-major 128 x D tile (chunks of 64 columns, 16 KB each
@@ -92,19 +175,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C_ = Cfg<D>;
-  constexpr int ST = C_::kStages;
+  constexpr int KST = C_::kKStages;
+  constexpr int VST = C_::kVStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
-  uint64_t* q_full = bars;                 // [1]
-  uint64_t* k_full = bars + 1;             // [ST]
-  uint64_t* v_full = bars + 1 + ST;        // [ST]
-  uint64_t* kv_empty = bars + 1 + 2 * ST;  // [ST]
-  uint64_t* s_full = bars + 1 + 3 * ST;    // [2]
-  uint64_t* p_full = s_full + 2;           // [2]
-  uint64_t* pv_done = s_full + 4;          // [2]
-  uint64_t* drain = s_full + 6;            // [1]
+  uint64_t* q_full = bars;                   // [1]
+  uint64_t* k_full = q_full + 1;             // [KST]
+  uint64_t* k_empty = k_full + KST;          // [KST]
+  uint64_t* v_full = k_empty + KST;          // [VST]
+  uint64_t* v_empty = v_full + VST;          // [VST]
+  uint64_t* s_full = v_empty + VST;          // [2]
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* pv_done = s_full + 4;            // [2]
+  uint64_t* drain = s_full + 6;              // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -116,10 +201,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < ST; ++i) {
+    for (int i = 0; i < KST; ++i) {
       mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VST; ++i) {
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -142,44 +230,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ---------------------------------------------------------------- loader
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------- loaders: warp 0 Q + K, warp 2 V
     if (elect_one()) {
-      uint8_t* sq = smem + C_::kQOff;
-      mbar_arrive_expect_tx(q_full, 2 * C_::kTileBytes);
+      const bool is_k = warp == 0;
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      const int NS = is_k ? KST : VST;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint8_t* ring = smem + (is_k ? C_::kKOff : C_::kVOff);
+      if (is_k) {
+        uint8_t* sq = smem + C_::kQOff;
+        mbar_arrive_expect_tx(q_full, 2 * C_::kTileBytes);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+        for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int c = 0; c < C_::kChunks; ++c)
-          tma_load_3d(sq + t * C_::kTileBytes + c * (kBlockQ * 128), &tmQ, q_full, 64 * c,
-                      int(q0 + t * kBlockQ), int(bh));
+          for (int c = 0; c < C_::kChunks; ++c)
+            tma_load_3d(sq + t * C_::kTileBytes + c * (kBlockQ * 128), &tmQ, q_full, 64 * c,
+                        int(q0 + t * kBlockQ), int(bh));
+      }
       uint32_t filled = 0;
       for (uint32_t j = 0; j < n; ++j) {
-        const uint32_t st = j % ST;
-        const uint32_t ph = (j / ST) & 1u;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
-        uint8_t* sk = smem + C_::kKVOff + st * C_::kStageBytes;
-        uint8_t* sv = sk + C_::kTileBytes;
-        mbar_arrive_expect_tx(&k_full[st], C_::kTileBytes);
+        const uint32_t st = j % NS;
+        const uint32_t ph = (j / NS) & 1u;
+        if (!mbar_wait(&empty[st], ph ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
+        uint8_t* dst = ring + st * C_::kTileBytes;
+        mbar_arrive_expect_tx(&full[st], C_::kTileBytes);
 #pragma unroll
         for (int c = 0; c < C_::kChunks; ++c)
-          tma_load_3d(sk + c * (kBlockKV * 128), &tmK, &k_full[st], 64 * c, int(j * kBlockKV),
-                      int(bh));
-        mbar_arrive_expect_tx(&v_full[st], C_::kTileBytes);
-#pragma unroll
-        for (int c = 0; c < C_::kChunks; ++c)
-          tma_load_3d(sv + c * (kBlockKV * 128), &tmV, &v_full[st], 64 * c, int(j * kBlockKV),
+          tma_load_3d(dst + c * (kBlockKV * 128), map, &full[st], 64 * c, int(j * kBlockKV),
                       int(bh));
         ++filled;
       }
       // drain: the last fill of each stage must land before the CTA exits
       int dummy = 0;
-      mbar_wait(q_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
-      const uint32_t m = filled < uint32_t(ST) ? filled : uint32_t(ST);
+      if (is_k) mbar_wait(q_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
+      const uint32_t m = filled < uint32_t(NS) ? filled : uint32_t(NS);
       for (uint32_t i = 0; i < m; ++i) {
         const uint32_t f = filled - 1 - i;
-        mbar_wait(&k_full[f % ST], (f / ST) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
-        mbar_wait(&v_full[f % ST], (f / ST) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
+        mbar_wait(&full[f % NS], (f / NS) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
       }
     }
   } else if (warp == 1) {
@@ -190,22 +279,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t sq = smem_u32(smem + C_::kQOff);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kWdAttnMma);
       auto issue_s = [&](uint32_t j, int t) {
-        const uint32_t sk = smem_u32(smem + C_::kKVOff + (j % ST) * C_::kStageBytes);
+        const uint32_t sk = smem_u32(smem + C_::kKOff + (j % KST) * C_::kTileBytes);
         const uint32_t qa = sq + t * C_::kTileBytes;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k)
-          umma_f16_ss(tmem + col_s(t), kmajor_desc<D>(qa, k), kmajor_desc<D>(sk, k),
-                      idesc_qk, k > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + col_s(t), kmajor_desc<D>(qa, k), kmajor_desc<D>(sk, k), idesc_qk,
+                      k > 0 ? 1u : 0u);
         umma_commit(&s_full[t]);
+        if (t == 1) umma_commit(&k_empty[j % KST]);  // K_j consumed by both tiles
       };
       auto issue_pv = [&](uint32_t j, int t) {
-        const uint32_t sv =
-            smem_u32(smem + C_::kKVOff + (j % ST) * C_::kStageBytes + C_::kTileBytes);
+        const uint32_t sv = smem_u32(smem + C_::kVOff + (j % VST) * C_::kTileBytes);
 #pragma unroll
         for (int k = 0; k < kBlockKV / 16; ++k)
-          umma_f16_ts(tmem + col_o(t), tmem + col_s(t) + k * 8, vmajor_desc<D>(sv, k),
-                      idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + col_o(t), tmem + col_s(t) + k * 8, vmajor_desc<D>(sv, k), idesc_pv,
+                      (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(&pv_done[t]);
+        if (t == 1) umma_commit(&v_empty[j % VST]);  // V_j consumed by both tiles
       };
       if (ok && n > 0) {
         ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, kWdAttnMma);
@@ -215,24 +305,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_s(0, 1);
         }
       }
+      // Per block j and tile t: PV_t(j) as soon as P_t(j) is ready, then
+      // S_t(j+1) once PV_t(j) has completed (P_t shares S_t's columns). The
+      // two tiles run half a period apart, so while one tile's S(j+1) waits
+      // for its PV(j), the tensor pipe works on the other tile.
       for (uint32_t j = 0; ok && j < n; ++j) {
-        const uint32_t st = j % ST, ph = (j / ST) & 1u;
-        // PV for block j of both tiles
-        if (!(ok = mbar_wait(&v_full[st], ph, abort_flag, p.status, kWdAttnMma))) break;
-        for (int t = 0; t < 2 && ok; ++t) {
+        if (!(ok = mbar_wait(&v_full[j % VST], (j / VST) & 1u, abort_flag, p.status,
+                             kWdAttnMma)))
+          break;
+        for (int t = 0; t < 2; ++t) {
+          FA_TRACE(2, j, 4 * t + 0);
           if (!(ok = mbar_wait(&p_full[t], j & 1u, abort_flag, p.status, kWdAttnMma))) break;
           tc_fence_after();
+          FA_TRACE(2, j, 4 * t + 1);
           issue_pv(j, t);
-        }
-        if (!ok) break;
-        umma_commit(&kv_empty[st]);
-        // S for block j+1 of both tiles, each after its PV(j) completed
-        if (j + 1 < n) {
-          const uint32_t st1 = (j + 1) % ST, ph1 = ((j + 1) / ST) & 1u;
-          if (!(ok = mbar_wait(&k_full[st1], ph1, abort_flag, p.status, kWdAttnMma))) break;
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (!(ok = mbar_wait(&pv_done[t], j & 1u, abort_flag, p.status, kWdAttnMma))) break;
+          if (j + 1 < n) {
+            FA_TRACE(2, j, 4 * t + 2);
+            if (t == 0 && !(ok = mbar_wait(&k_full[(j + 1) % KST], ((j + 1) / KST) & 1u,
+                                           abort_flag, p.status, kWdAttnMma)))
+              break;
+            if (kWaitPV &&
+                !(ok = mbar_wait(&pv_done[t], j & 1u, abort_flag, p.status, kWdAttnMma)))
+              break;
             tc_fence_after();
+            FA_TRACE(2, j, 4 * t + 3);
             issue_s(j + 1, t);
           }
         }
@@ -254,8 +350,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;
     bool ok = true;
     for (uint32_t j = 0; j < n; ++j) {
+      if (lane == 0 && q == 0) FA_TRACE(t, j, 0);
       if (!(ok = mbar_wait(&s_full[t], j & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
       tc_fence_after();
+      if (lane == 0 && q == 0) FA_TRACE(t, j, 1);
       float s[kBlockKV];
 #pragma unroll
       for (int c = 0; c < kBlockKV; c += 32) {
@@ -265,16 +363,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(r[i]);
       }
       tmem_ld_wait();
+      if (lane == 0 && q == 0) FA_TRACE(t, j, 2);
       const uint32_t valid = p.S - j * kBlockKV;  // keys left in this block
       if (valid < uint32_t(kBlockKV)) {
 #pragma unroll
         for (int i = 0; i < kBlockKV; ++i)
           if (uint32_t(i) >= valid) s[i] = -INFINITY;
       }
-      float mx = s[0];
+      // row max: 3-input max, 4 independent chains
+      float m4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-      for (int i = 1; i < kBlockKV; ++i) mx = fmaxf(mx, s[i]);
+      for (int i = 4; i < kBlockKV; i += 8) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) m4[c] = fmax3(m4[c], s[i + c], s[i + 4 + c]);
+      }
+      const float mx = fmax3(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
       const float mc = mx * sl2;
+      if (lane == 0 && q == 0) FA_TRACE(t, j, 3);
       const bool need = mc > m + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
         const float m_new = need ? mc : m;
@@ -298,25 +403,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      const float neg_m = -m;
-      float rs = 0.f;
+      // P = 2^(s * scale_log2 - m), two columns at a time in packed fp32x2;
+      // one pair in kEmuEvery on the FMA pipe, the rest on MUFU.
+      const uint64_t scale2 = pack_f32x2(sl2, sl2);
+      const uint64_t negm2 = pack_f32x2(-m, -m);
+      uint64_t l2[2] = {0ull, 0ull};  // packed partial row sums
 #pragma unroll
       for (int c = 0; c < kBlockKV; c += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(fmaf(s[c + 2 * i], sl2, neg_m));
-          const float p1 = ex2(fmaf(s[c + 2 * i + 1], sl2, neg_m));
-          rs += p0 + p1;
-          pk[i] = pack_half2(p0, p1);
+          const int e = c + 2 * i;
+          const uint64_t x2 = ffma2(pack_f32x2(s[e], s[e + 1]), scale2, negm2);
+          uint64_t p2;
+          if (kEmuEvery > 0 && (i % (kEmuEvery > 0 ? kEmuEvery : 1)) == kEmuEvery - 1) {
+            p2 = exp2_fma_x2(x2);
+          } else {
+            p2 = pack_f32x2(ex2(lo_f32(x2)), ex2(hi_f32(x2)));
+          }
+          l2[i & 1] = fadd2(l2[i & 1], p2);
+          pk[i] = pack_half2(lo_f32(p2), hi_f32(p2));
         }
         tmem_st_32x32b_x16(tS + c / 2, pk);
       }
-      l += rs;
+      const uint64_t lsum = fadd2(l2[0], l2[1]);
+      l += lo_f32(lsum) + hi_f32(lsum);
+      if (lane == 0 && q == 0) FA_TRACE(t, j, 4);
       tmem_st_wait();
+      if (lane == 0 && q == 0) FA_TRACE(t, j, 5);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0 && q == 0) FA_TRACE(t, j, 6);
     }
     // ---------------------------------------------------------------- epilogue
     if (ok && n > 0 &&
@@ -379,6 +497,7 @@ int configure_once(int device) {
   static int done[64] = {0};
   if (device < 0 || device >= 64) return -1;
   if (!done[device]) {
+
     cudaError_t e = cudaFuncSetAttribute(flash_attn_fwd_kernel<D>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg<D>::kSmemBytes);
@@ -437,3 +556,9 @@ FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, _
 }
 
 }  // namespace felix_impl
+
+#ifdef FELIX_FA_TRACE
+extern "C" void fa_trace_fetch(void* dst) {
+  cudaMemcpyFromSymbol(dst, felix_sm100::attn::g_fa_trace, sizeof(felix_sm100::attn::g_fa_trace));
+}
+#endif

@@ -13,7 +13,7 @@
 //       warp 0  TMA producer (one elected lane), multi-stage smem ring
 //       warp 1  TMEM allocator + single-thread tcgen05.mma issuer
 //       warps 2-5 epilogue: tcgen05.ld -> alpha/beta -> fp16 -> global
-//   * CTA tile 128 x BN (BN = 256 or 128), K step 64 (one 128-byte swizzle row),
+//   * CTA tile 128 x BN (BN = 256, 128 or 64), K step 64 (one 128-byte swizzle row),
 //     UMMA 128 x BN x 16; two TMEM accumulators so the epilogue of tile i
 //     overlaps the main loop of tile i+1.
 //   * schedule: whole tiles round-robin over the persistent CTAs ("data-parallel"
@@ -40,7 +40,7 @@ constexpr int kThreads = 192;
 
 template <int BN>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -510,9 +510,9 @@ struct Plan {
   uint64_t sk_iters;
 };
 
-Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int num_sms) {
+Plan plan_for(uint32_t M, uint32_t N, uint32_t K, int bn, const HgemmOptions& o, int num_sms) {
   Plan pl{};
-  pl.bn = o.block_n ? o.block_n : (N >= 256 ? 256 : 128);
+  pl.bn = bn;
   pl.tiles_m = (M + BM - 1) / BM;
   pl.tiles_n = (N + pl.bn - 1) / pl.bn;
   pl.kblocks = (K + BK - 1) / BK;
@@ -528,7 +528,11 @@ Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int nu
   } else {
     // Spread the incomplete wave by k-iterations when it leaves SMs idle and
     // each CTA still gets a useful k-range.
-    use_sk = rem != 0 && pl.kblocks >= 8 && rem * 100 < P * 85 &&
+    // Narrow tiles have cheap fix-ups (32 KB partials at BN = 64), so any
+    // incomplete wave is worth spreading; wide tiles only when the wave is
+    // clearly incomplete.
+    const uint32_t pct = bn == 64 ? 100 : 85;
+    use_sk = rem != 0 && pl.kblocks >= 8 && rem * 100 < P * pct &&
              uint64_t(rem) * pl.kblocks >= uint64_t(P) * 4;
   }
   if (use_sk) {
@@ -543,6 +547,19 @@ Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int nu
     pl.grid = pl.tiles < P ? pl.tiles : P;
   }
   return pl;
+}
+
+Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int num_sms) {
+  if (o.block_n) return plan_for(M, N, K, o.block_n, o, num_sms);
+  // Fewer 128x256 tiles than SMs (skinny / decode shapes): the stream-K
+  // fix-up of 128 KB partials with many contributors per tile becomes a
+  // latency-bound tail, so narrow the tile until there are at least ~0.8
+  // tiles per SM (BN = 64 at most halves the A re-reads' efficiency, which
+  // only matters when M is large, and then tiles are plentiful).
+  const uint32_t tiles_m = (M + BM - 1) / BM;
+  int bn = N >= 256 ? 256 : 128;
+  while (bn > 128 && uint64_t(tiles_m) * ((N + bn - 1) / bn) * 5 < uint64_t(num_sms) * 4) bn /= 2;
+  return plan_for(M, N, K, bn, o, num_sms);
 }
 
 }  // namespace
@@ -564,8 +581,8 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
     return scale_half_matrix(C, size_t(M) * N, beta, stream);
   }
   if (!A || !B) return api_error("hgemm: null pointer");
-  if (o.block_n != 0 && o.block_n != 128 && o.block_n != 256)
-    return api_error("hgemm: block_n must be 0, 128 or 256");
+  if (o.block_n != 0 && o.block_n != 64 && o.block_n != 128 && o.block_n != 256)
+    return api_error("hgemm: block_n must be 0, 64, 128 or 256");
   // TMA: global row strides must be multiples of 16 bytes, bases 16-byte aligned.
   if (K % 8 != 0) return api_error("hgemm: K must be a multiple of 8 (16-byte rows for TMA)");
   if (b_kn && N % 8 != 0) return api_error("hgemm nn: N must be a multiple of 8");
@@ -627,14 +644,25 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   }
 
   cudaError_t e;
-  if (pl.bn == 256) {
-    if ((rc = configure_once<256>(dev->ordinal)))
-      return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    hgemm_persistent_kernel<256><<<pl.grid, kThreads, Cfg<256>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
-  } else {
-    if ((rc = configure_once<128>(dev->ordinal)))
-      return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    hgemm_persistent_kernel<128><<<pl.grid, kThreads, Cfg<128>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
+  switch (pl.bn) {
+    case 256:
+      if ((rc = configure_once<256>(dev->ordinal)))
+        return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+      hgemm_persistent_kernel<256>
+          <<<pl.grid, kThreads, Cfg<256>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
+      break;
+    case 128:
+      if ((rc = configure_once<128>(dev->ordinal)))
+        return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+      hgemm_persistent_kernel<128>
+          <<<pl.grid, kThreads, Cfg<128>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
+      break;
+    default:
+      if ((rc = configure_once<64>(dev->ordinal)))
+        return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+      hgemm_persistent_kernel<64>
+          <<<pl.grid, kThreads, Cfg<64>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
+      break;
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return launch_error(e, "hgemm: launch failed");

@@ -52,7 +52,7 @@ def test_hgemm_alpha_beta(felix, nt):
     assert_fp16_close(ref, out, ctx="alpha/beta")
 
 
-@pytest.mark.parametrize("block_n", [128, 256])
+@pytest.mark.parametrize("block_n", [64, 128, 256])
 @pytest.mark.parametrize("nt", [True, False])
 def test_hgemm_stream_k_forced(felix, block_n, nt):
     # 5 x 4 tiles on 3 persistent CTAs: 18 whole tiles + 2 stream-K tiles
