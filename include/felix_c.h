@@ -63,6 +63,32 @@ int felix_sgemm_workspace_size(uint32_t M, uint32_t N, uint32_t K, int split_k,
                                size_t* bytes);
 
 /*
+ * SGEMM that allocates nothing. No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc from inside an operator call: hosts
+ * that own all device memory through their own pool or a fixed memory budget,
+ * plugin runtimes that forbid allocation in a kernel launch path, and
+ * latency-critical code that cannot accept cudaMalloc's implicit device-wide
+ * synchronisation. Same arithmetic and arguments as felix_sgemm_ex; the
+ * split-K scratch (tile counters + fp32 partial tiles) lives in a static
+ * array inside the library's device image instead of being allocated:
+ *   - size: 16 MiB of partial tiles + 16 KiB of counters, held by every GPU
+ *     that loads the library until the process exits;
+ *   - split_k = 0 picks the largest automatic split whose partials fit;
+ *     an explicit split_k needing more (tiles x split_k > 256, tiles =
+ *     ceil(M/128) * ceil(N/128)) is rejected with FELIX_API_ERROR;
+ *   - the first call on a device looks up the scratch's device address
+ *     (cudaGetSymbolAddress) for that device; make that first call before any
+ *     stream capture;
+ *   - each call clears the counters on `stream` before its kernel;
+ *   - all calls share the one array: calls whose execution overlaps on the GPU
+ *     (different streams without ordering) race and give wrong results.
+ * The caller still owns A, B and C.
+ */
+int felix_sgemm_noalloc(uint32_t M, uint32_t N, uint32_t K, float alpha, const float* A,
+                        const float* B, float beta, float* C, int split_k, void* stream);
+
+/*
  * HGEMM, fp16 tensor cores (tcgen05, fp32 accumulate in TMEM, fp16 output):
  * C = alpha * A * op(B) + beta * C. A [M x K] row-major; B per b_layout
  * (FELIX_B_KN or FELIX_B_NK); C [M x N] row-major.

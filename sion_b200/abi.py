@@ -28,6 +28,9 @@ _SIGS = {
     "felix_sgemm_ex": (C.c_int, [C.c_uint32] * 3 + [C.c_float, C.c_void_p, C.c_void_p,
                                                      C.c_float, C.c_void_p, C.c_int, C.c_void_p,
                                                      C.c_size_t, C.c_void_p]),
+    "felix_sgemm_noalloc": (C.c_int, [C.c_uint32] * 3 + [C.c_float, C.c_void_p, C.c_void_p,
+                                                          C.c_float, C.c_void_p, C.c_int,
+                                                          C.c_void_p]),
     "felix_sgemm_workspace_size": (C.c_int, [C.c_uint32] * 3 + [C.c_int,
                                                                  C.POINTER(C.c_size_t)]),
     "felix_hgemm": (C.c_int, [C.c_uint32] * 3 + [C.c_float, C.c_void_p, C.c_void_p, C.c_float,
@@ -107,6 +110,16 @@ def sgemm(A, B, C_out, alpha=1.0, beta=0.0, split_k=None, workspace=None, stream
         ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
         check(L.felix_sgemm_ex(M, N, K, alpha, _ptr(A), _ptr(B), beta, _ptr(C_out),
                                int(split_k or 0), _ptr(workspace), ws_bytes, _stream(stream)))
+    return C_out
+
+
+def sgemm_noalloc(A, B, C_out, alpha=1.0, beta=0.0, split_k=0, stream=None):
+    """SGEMM through felix_sgemm_noalloc (split-K scratch in the library's
+    static device array; nothing is allocated)."""
+    M, K = A.shape
+    N = B.shape[1]
+    check(lib().felix_sgemm_noalloc(M, N, K, alpha, _ptr(A), _ptr(B), beta, _ptr(C_out),
+                                    int(split_k), _stream(stream)))
     return C_out
 
 

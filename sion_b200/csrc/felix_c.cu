@@ -238,6 +238,12 @@ int felix_sgemm_ex(uint32_t M, uint32_t N, uint32_t K, float alpha, const float*
                              static_cast<cudaStream_t>(stream)));
 }
 
+int felix_sgemm_noalloc(uint32_t M, uint32_t N, uint32_t K, float alpha, const float* A,
+                        const float* B, float beta, float* C, int split_k, void* stream) {
+  return finish(sgemm_noalloc_launch(M, N, K, alpha, A, B, beta, C, split_k,
+                                     static_cast<cudaStream_t>(stream)));
+}
+
 int felix_sgemm_workspace_size(uint32_t M, uint32_t N, uint32_t K, int split_k, size_t* bytes) {
   DeviceInfo* d = current_device_info();
   if (!d) return launch_error(cudaGetLastError(), "no device").type;

@@ -79,6 +79,10 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
                        const float* B, float beta, float* C, const SgemmOptions& o,
                        void* workspace, size_t ws_bytes, cudaStream_t stream);
 
+FelixCode sgemm_noalloc_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const float* A,
+                               const float* B, float beta, float* C, int split_k,
+                               cudaStream_t stream);
+
 FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, __half* O,
                             float* lse, uint32_t heads, uint32_t batch, uint32_t seqlen,
                             uint32_t head_dim, float scale, cudaStream_t stream);

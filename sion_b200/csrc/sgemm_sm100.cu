@@ -16,6 +16,7 @@
 // no CTA waits on another.
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <mutex>
 
 #include "felix_internal.h"
 
@@ -209,6 +210,15 @@ __global__ void __launch_bounds__(kThreads, 2) sgemm_kernel(const Params p) {
 }  // namespace sgemm
 }  // namespace felix_sm100
 
+// Scratch of felix_sgemm_noalloc: the fixed counter block followed by room
+// for 256 partial 128 x 128 fp32 tiles (16 MiB + 16 KiB). It is part of the
+// library's device image, so every GPU that loads the library holds it until
+// the process exits. Zero-initialised at load; the kernel leaves the counters
+// at zero and the entry point clears them again before every launch.
+constexpr size_t kNoAllocPartialBytes = size_t(16) << 20;
+constexpr size_t kNoAllocScratchBytes = felix_impl::kWsCounterBytes + kNoAllocPartialBytes;
+static __device__ __align__(256) unsigned char g_sgemm_noalloc_scratch[kNoAllocScratchBytes];
+
 namespace felix_impl {
 
 using namespace felix_sm100::sgemm;
@@ -291,6 +301,62 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return launch_error(e, "sgemm: launch failed");
   return FelixCode{FELIX_SUCCESS, cudaSuccess};
+}
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+}  // namespace
+
+// Device address of the static scratch on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device, with that device current, and cached.
+static void* noalloc_scratch(int device, cudaError_t* err) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_sgemm_noalloc_scratch);
+    if (e != cudaSuccess) {
+      *err = e;
+      return nullptr;
+    }
+    g_noalloc_ptr[device] = ptr;
+  }
+  return g_noalloc_ptr[device];
+}
+
+FelixCode sgemm_noalloc_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const float* A,
+                               const float* B, float beta, float* C, int split_k,
+                               cudaStream_t stream) {
+  if (split_k < 0) return api_error("sgemm_noalloc: split_k must be >= 0");
+  if (M == 0 || N == 0) return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  if (K == 0) return sgemm_launch(M, N, K, alpha, A, B, beta, C, SgemmOptions{}, nullptr, 0, stream);
+  DeviceInfo* dev = current_device_info();
+  if (!dev) return launch_error(cudaGetLastError(), "sgemm_noalloc: no CUDA device");
+  SgemmOptions o;
+  o.split_k = split_k;
+  size_t need = sgemm_workspace_bytes(M, N, K, o, dev->num_sms);
+  if (need > kNoAllocScratchBytes) {
+    if (split_k > 0)
+      return api_error(
+          "sgemm_noalloc: this split_k needs more split-K scratch than the 16 MiB static "
+          "scratch holds (at most 256 partial 128x128 tiles: tiles x split_k <= 256)");
+    // automatic split: the largest one whose partial tiles fit
+    const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    o.split_k = int(kNoAllocPartialBytes / (size_t(BM) * BN * sizeof(float)) / tiles);
+    if (o.split_k < 1) o.split_k = 1;
+    need = sgemm_workspace_bytes(M, N, K, o, dev->num_sms);
+  }
+  void* scratch = nullptr;
+  if (need > 0) {
+    cudaError_t e = cudaSuccess;
+    scratch = noalloc_scratch(dev->ordinal, &e);
+    if (!scratch) return launch_error(e, "sgemm_noalloc: cudaGetSymbolAddress(scratch)");
+    // the tile counters must start at zero
+    e = cudaMemsetAsync(scratch, 0, kWsCounterBytes, stream);
+    if (e != cudaSuccess) return launch_error(e, "sgemm_noalloc: clearing the counters");
+  }
+  return sgemm_launch(M, N, K, alpha, A, B, beta, C, o, scratch, kNoAllocScratchBytes, stream);
 }
 
 }  // namespace felix_impl
