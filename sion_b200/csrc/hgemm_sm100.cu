@@ -532,7 +532,12 @@ Plan plan_for(uint32_t M, uint32_t N, uint32_t K, int bn, const HgemmOptions& o,
     // incomplete wave is worth spreading; wide tiles only when the wave is
     // clearly incomplete.
     const uint32_t pct = bn == 64 ? 100 : 85;
-    use_sk = rem != 0 && pl.kblocks >= 8 && rem * 100 < P * pct &&
+    // Only worth it while whole-tile waves would waste more than ~5% of the
+    // SMs: with many waves (e.g. 16384^3: 55 waves, 1.2% loss) the fix-up
+    // traffic costs more than the quantisation it removes.
+    const uint64_t waves = (pl.tiles + P - 1) / P;
+    const bool dp_wasteful = uint64_t(pl.tiles) * 100 < waves * P * 95;
+    use_sk = rem != 0 && dp_wasteful && pl.kblocks >= 8 && rem * 100 < P * pct &&
              uint64_t(rem) * pl.kblocks >= uint64_t(P) * 4;
   }
   if (use_sk) {
