@@ -120,11 +120,21 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- workloads
 class GemmRunner:
-    def __init__(self, cfg: W.GemmConfig, device):
+    def __init__(self, cfg: W.GemmConfig, device, shard_rank=None, world=1):
         from sion_b200 import abi
         self.abi = abi
         self.cfg = cfg
         A, B = W.gemm_inputs(cfg)
+        self.work_fraction = 1.0
+        if shard_rank is not None:
+            # strong scaling: this rank owns a contiguous column block of C
+            from sion_b200.shard import gemm_column_shard
+            n0, n1 = gemm_column_shard(cfg.N, world, shard_rank)
+            B = (B[n0:n1] if cfg.b_layout == "nk" else B[:, n0:n1]).contiguous()
+            self.work_fraction = (n1 - n0) / cfg.N
+            cfg = W.GemmConfig(cfg.name, cfg.M, n1 - n0, cfg.K, cfg.dtype, cfg.b_layout, cfg.dist,
+                               cfg.std, cfg.seed)
+            self.cfg = cfg
         self.hA = A.pin_memory()
         self.hB = B.pin_memory()
         self.dA = self.hA.to(device)
@@ -164,11 +174,22 @@ class GemmRunner:
 
 
 class AttnRunner:
-    def __init__(self, cfg: W.AttnConfig, device):
+    def __init__(self, cfg: W.AttnConfig, device, shard_rank=None, world=1):
         from sion_b200 import abi
         self.abi = abi
         self.cfg = cfg
         Q, K, V = W.attn_inputs(cfg)
+        self.work_fraction = 1.0
+        if shard_rank is not None:
+            # strong scaling: this rank owns a contiguous group of (b, h) pairs
+            from sion_b200.shard import attention_shard
+            s0, s1 = attention_shard(cfg.B, cfg.H, world, shard_rank)
+            Q, K, V = [t.reshape(cfg.B * cfg.H, cfg.S, cfg.D)[s0:s1].reshape(1, s1 - s0, cfg.S,
+                                                                            cfg.D).contiguous()
+                       for t in (Q, K, V)]
+            self.work_fraction = (s1 - s0) / (cfg.B * cfg.H)
+            cfg = W.AttnConfig(cfg.name, 1, s1 - s0, cfg.S, cfg.D, cfg.seed)
+            self.cfg = cfg
         self.h = [t.pin_memory() for t in (Q, K, V)]
         self.d = [t.to(device) for t in self.h]
         self.dO = torch.empty_like(self.d[0])
@@ -199,9 +220,10 @@ class AttnRunner:
         return "tensor", self.cfg.flops
 
 
-def make_runner(name, device):
+def make_runner(name, device, shard_rank=None, world=1):
     cfg = W.CONFIGS[name]
-    return AttnRunner(cfg, device) if isinstance(cfg, W.AttnConfig) else GemmRunner(cfg, device)
+    cls = AttnRunner if isinstance(cfg, W.AttnConfig) else GemmRunner
+    return cls(cfg, device, shard_rank, world)
 
 
 # ----------------------------------------------------------------- CPU host path
@@ -303,6 +325,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(W.CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", action="store_true",
+                    help="strong scaling: split one workload over the ranks (GEMM N-column "
+                         "blocks, attention (b, h) groups) instead of one copy per rank")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -314,7 +339,8 @@ def main():
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    runner = make_runner(args.workload, device)
+    runner = make_runner(args.workload, device, rank if args.shard else None, world)
+    full_cfg = W.CONFIGS[args.workload]
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream()
 
@@ -343,7 +369,8 @@ def main():
     ms = max_over_ranks(mean_ms, world)
 
     bound, work = runner.algorithmic()
-    value = world * runner.cfg.flops / (ms * 1e-3) / 1e12
+    job_flops = full_cfg.flops if args.shard else world * full_cfg.flops
+    value = job_flops / (ms * 1e-3) / 1e12
 
     # e2e through the C ABI with host buffers
     for _ in range(2):
@@ -359,7 +386,7 @@ def main():
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(e2e_s, e2e_e)),
                             world)
-    e2e_val = world * runner.cfg.flops / (e2e_ms * 1e-3) / 1e12
+    e2e_val = job_flops / (e2e_ms * 1e-3) / 1e12
 
     peaks = _peaks()
     if bound == "hbm":
@@ -387,8 +414,10 @@ def main():
 
     clocks = sampler.summary()
     if rank == 0:
-        cfg = runner.cfg
-        conf = {"workload": cfg.name, "parallelism": f"replicas x{world} (independent units)",
+        cfg = full_cfg
+        par = (f"shards x{world} (N-column / (b,h) blocks, no collective)" if args.shard
+               else f"replicas x{world} (independent units)")
+        conf = {"workload": cfg.name, "parallelism": par,
                 "l2": "flushed between steps (512 MiB write outside the timed events)"}
         if isinstance(cfg, W.GemmConfig):
             conf.update({"M": cfg.M, "N": cfg.N, "K": cfg.K, "b_layout": cfg.b_layout})
@@ -397,7 +426,8 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if args.shard else "weak",
+            "vs_baseline": None,
             "dtype": "f32" if getattr(cfg, "dtype", "f16") == "f32" else "f16 (fp32 accumulate)",
             "data": "synthetic (seeded torch CPU generator)", "config": conf,
             "frac_of_peak": value / world / (roof["peak"] if bound != "hbm" else 1) if bound != "hbm" else None,
