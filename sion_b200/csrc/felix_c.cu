@@ -121,6 +121,16 @@ int encode_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint6
                        uint64_t pitch, uint32_t bi, uint32_t bo) {
   return encode_2d(map, base, inner, outer, pitch, bi, bo, CU_TENSOR_MAP_SWIZZLE_128B);
 }
+int encode_tmap_2d_f16_swizzle(CUtensorMap* map, const void* base, uint64_t inner,
+                               uint64_t outer, uint64_t pitch, uint32_t bi, uint32_t bo,
+                               int swizzle_bytes) {
+  CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (swizzle_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
+  else if (swizzle_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  else if (swizzle_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  return encode_2d(map, base, inner, outer, pitch, bi, bo, sw);
+}
+
 int encode_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer1,
                        uint64_t outer2, uint64_t pitch1, uint64_t pitch2, uint32_t bi,
                        uint32_t bo1, uint32_t bo2) {

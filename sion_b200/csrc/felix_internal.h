@@ -46,6 +46,10 @@ void* library_workspace(DeviceInfo* dev, cudaStream_t stream, size_t bytes);
 // `outer` rows, row pitch in bytes, box of box_inner x box_outer.
 int encode_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                        uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer);
+// 2-D fp16 tensor map with an explicit swizzle span (0, 32, 64 or 128 bytes).
+int encode_tmap_2d_f16_swizzle(CUtensorMap* map, const void* base, uint64_t inner,
+                               uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner,
+                               uint32_t box_outer, int swizzle_bytes);
 // 3-D fp16 tensor map, 128-byte swizzle: [outer2][outer1][inner].
 int encode_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer1,
                        uint64_t outer2, uint64_t pitch1_bytes, uint64_t pitch2_bytes,

@@ -35,12 +35,21 @@ namespace felix_sm100 {
 namespace hgemm {
 
 constexpr int BM = 128;
-constexpr int BK = 64;
+// K step of one pipeline stage: 64 (128-byte operand rows, SWIZZLE_128B).
+// 32 (SWIZZLE_64B, twice as many half-size stages) is kept as a build option;
+// measured on B200 it is slower (4096^3: 1005 vs 1335 TFLOP/s) because the
+// per-stage barrier and issue work doubles.
+#ifndef FELIX_HGEMM_BK
+#define FELIX_HGEMM_BK 64
+#endif
+constexpr int BK = FELIX_HGEMM_BK;
+static_assert(BK == 32 || BK == 64, "k step");
+constexpr int kSwizzleK = BK * 2;  // bytes per K-major operand row = swizzle span
 constexpr int kThreads = 192;
 
 template <int BN>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int kStages = (192 * 1024) / ((BM + BN) * BK * 2);
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -48,7 +57,7 @@ struct Cfg {
   // epilogue staging for TMA stores: 4 warps x 2 buffers x (32 rows x 128 B)
   static constexpr int kStagingBytes = 4 * 2 * 4096;
   // ring + staging + 1 KB alignment slack + barrier block
-  static constexpr int kSmemBytes = kStages * kStageBytes + kStagingBytes + 1024 + 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kStagingBytes + 1024 + 512;
 };
 
 struct Params {
@@ -313,9 +322,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b0 = a0 + C_::kABytes;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = make_sdesc_sw128(a0 + k * 32, 16, 1024);
-            const uint64_t bd = p.b_mn_major ? make_sdesc_sw128(b0 + k * 2048, 64 * BK * 2, 1024)
-                                             : make_sdesc_sw128(b0 + k * 32, 16, 1024);
+            uint64_t ad, bd;
+            if constexpr (BK == 64) {
+              ad = make_sdesc_sw128(a0 + k * 32, 16, 1024);
+              bd = p.b_mn_major ? make_sdesc_sw128(b0 + k * 2048, 64 * BK * 2, 1024)
+                                : make_sdesc_sw128(b0 + k * 32, 16, 1024);
+            } else {
+              ad = make_sdesc_sw64(a0 + k * 32, 16, 512);
+              bd = p.b_mn_major ? make_sdesc_sw128(b0 + k * 2048, 64 * BK * 2, 1024)
+                                : make_sdesc_sw64(b0 + k * 32, 16, 512);
+            }
             umma_f16_ss(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
@@ -601,12 +617,12 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   Plan pl = make_plan(M, N, K, o, dev->num_sms);
 
   CUtensorMap tmA, tmB;
-  int rc = encode_tmap_2d_f16(&tmA, A, K, M, uint64_t(K) * 2, BK, BM);
+  int rc = encode_tmap_2d_f16_swizzle(&tmA, A, K, M, uint64_t(K) * 2, BK, BM, kSwizzleK);
   if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(A) failed");
   if (b_kn)
     rc = encode_tmap_2d_f16(&tmB, B, N, K, uint64_t(N) * 2, 64, BK);
   else
-    rc = encode_tmap_2d_f16(&tmB, B, K, N, uint64_t(K) * 2, BK, pl.bn);
+    rc = encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK, pl.bn, kSwizzleK);
   if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
 
   // C through TMA when nothing has to be read back (beta == 0) and its rows

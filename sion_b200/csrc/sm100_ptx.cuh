@@ -275,6 +275,19 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_
   return d;
 }
 
+// Same with 64-byte swizzle (layout 4): K-major tiles whose rows are 64 B
+// (32 fp16); 8-row groups SBO bytes apart.
+__device__ __forceinline__ uint64_t make_sdesc_sw64(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= uint64_t((smem_addr >> 4) & 0x3FFFu);
+  d |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(4) << 61;
+  return d;
+}
+
 // TMEM -> registers: 32 lanes x 32 bits, 32 consecutive columns per thread.
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
