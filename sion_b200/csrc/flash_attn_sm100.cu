@@ -42,17 +42,26 @@ constexpr int kBlockKV = 128;  // keys per KV block (UMMA N of QK^T, K of PV)
 constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-template <int D>
+// CG = 1: one CTA per 256 query rows. CG = 2 (D = 128): a cluster of two CTAs
+// per 512 query rows whose MMAs are cta_group::2 (M = 256); each CTA then
+// holds half of every K block (64 keys) and half of every V block (64 of the
+// D columns), so per-SM shared-memory operand traffic drops by ~40%.
+template <int D, int CG>
 struct Cfg {
-  static constexpr int kKStages = D == 128 ? 3 : 4;      // K ring
-  static constexpr int kVStages = D == 128 ? 2 : 4;      // V ring
+  static constexpr int kKStages = CG == 2 ? 4 : (D == 128 ? 3 : 4);  // K ring
+  static constexpr int kVStages = CG == 2 ? 4 : (D == 128 ? 2 : 4);  // V ring
   static constexpr int kChunks = D / 64;                 // 128-byte swizzle chunks per row
-  static constexpr int kTileBytes = kBlockQ * D * 2;     // one 128 x D fp16 tile
+  static constexpr int kTileBytes = kBlockQ * D * 2;     // one 128 x D fp16 Q tile
+  static constexpr int kKeys = kBlockKV / CG;            // K rows held per CTA
+  static constexpr int kKBytes = kKeys * D * 2;          // K slot
+  static constexpr int kVCols = D / CG;                  // V columns held per CTA
+  static constexpr int kVBytes = kBlockKV * kVCols * 2;  // V slot
   static constexpr int kQOff = 0;                        // Q_A, Q_B
   static constexpr int kKOff = 2 * kTileBytes;
-  static constexpr int kVOff = kKOff + kKStages * kTileBytes;
-  static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
+  static constexpr int kVOff = kKOff + kKStages * kKBytes;
+  static constexpr int kBarOff = kVOff + kVStages * kVBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;
+  static_assert(CG == 1 || D == 128, "CTA pairs need D = 128");
 };
 
 // TMEM columns of tile t's S (and P) and O accumulators.
@@ -64,7 +73,7 @@ struct Params {
   float* lse;
   uint32_t S;        // sequence length
   uint32_t n_kv;     // KV blocks
-  uint32_t q_tiles;  // CTAs per (b, h) along the query axis
+  uint32_t q_tiles;  // CTA groups per (b, h) along the query axis
   float scale_log2;  // scale * log2(e)
   unsigned* status;
 };
@@ -155,39 +164,38 @@ __device__ __forceinline__ uint64_t exp2_fma_x2(uint64_t x2) {
   return pack_f32x2(r0, r1);
 }
 
-// Smem descriptor of a K-major 128 x D tile (chunks of 64 columns, 16 KB each
-// for 128 rows), advanced to K step k (16 elements).
-template <int D>
+// Smem descriptor of a K-major ROWS x D tile (chunks of 64 columns, ROWS*128
+// bytes each), advanced to K step k (16 elements).
+template <int ROWS>
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int k) {
   const uint32_t chunk = uint32_t(k) >> 2;
-  return make_sdesc_sw128(tile_addr + chunk * (kBlockQ * 128) + (uint32_t(k) & 3u) * 32, 16, 1024);
+  return make_sdesc_sw128(tile_addr + chunk * (ROWS * 128) + (uint32_t(k) & 3u) * 32, 16, 1024);
 }
-// Smem descriptor of V (kBlockKV rows x D, D contiguous) as the MN-major B
-// operand of PV, advanced to K step k (16 keys).
-template <int D>
+// Smem descriptor of V (kBlockKV keys x its D columns, D contiguous, chunks of
+// 64 columns) as the MN-major B operand of PV, advanced to K step k (16 keys).
 __device__ __forceinline__ uint64_t vmajor_desc(uint32_t tile_addr, int k) {
   return make_sdesc_sw128(tile_addr + uint32_t(k) * 2048, kBlockKV * 128, 1024);
 }
 
-template <int D>
+template <int D, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const Params p) {
-  using C_ = Cfg<D>;
+  using C_ = Cfg<D, CG>;
   constexpr int KST = C_::kKStages;
   constexpr int VST = C_::kVStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
-  uint64_t* q_full = bars;                   // [1]
-  uint64_t* k_full = q_full + 1;             // [KST]
+  uint64_t* q_full = bars;                   // [1]   (leader's counts both CTAs)
+  uint64_t* k_full = q_full + 1;             // [KST] (leader's counts both CTAs)
   uint64_t* k_empty = k_full + KST;          // [KST]
-  uint64_t* v_full = k_empty + KST;          // [VST]
+  uint64_t* v_full = k_empty + KST;          // [VST] (leader's counts both CTAs)
   uint64_t* v_empty = v_full + VST;          // [VST]
   uint64_t* s_full = v_empty + VST;          // [2]
-  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* p_full = s_full + 2;             // [2]   (leader's counts both CTAs)
   uint64_t* pv_done = s_full + 4;            // [2]
   uint64_t* drain = s_full + 6;              // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 7);
@@ -195,8 +203,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const uint32_t warp = threadIdx.x / 32;
   const uint32_t lane = threadIdx.x % 32;
-  const uint32_t bh = blockIdx.x / p.q_tiles;
-  const uint32_t q0 = (blockIdx.x % p.q_tiles) * (2 * kBlockQ);
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const uint32_t grp = blockIdx.x / CG;
+  const uint32_t bh = grp / p.q_tiles;
+  const uint32_t q0 = (grp % p.q_tiles) * (2 * kBlockQ * CG) + rank * (2 * kBlockQ);
   const uint32_t n = p.n_kv;
 
   if (threadIdx.x == 0) {
@@ -211,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 4 * CG);
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -221,14 +231,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
   }
+  if constexpr (CG == 2) cluster_sync();  // peer barriers initialised before any remote use
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  // Barrier address the loads of this CTA signal (the leader's in a pair).
+  auto leader_bar = [&](uint64_t* bar) -> uint32_t {
+    return CG == 2 ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar);
+  };
+  auto load3d = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+    if constexpr (CG == 2)
+      tma_load_3d_pair(dst, map, leader_bar(bar), x, y, z);
+    else
+      tma_load_3d(dst, map, bar, x, y, z);
+  };
 
   if (warp == 0 || warp == 2) {
     // ------------------------------------------------- loaders: warp 0 Q + K, warp 2 V
@@ -236,66 +263,100 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool is_k = warp == 0;
       const CUtensorMap* map = is_k ? &tmK : &tmV;
       const int NS = is_k ? KST : VST;
+      const uint32_t slot_bytes = is_k ? C_::kKBytes : C_::kVBytes;
       uint64_t* full = is_k ? k_full : v_full;
       uint64_t* empty = is_k ? k_empty : v_empty;
       uint8_t* ring = smem + (is_k ? C_::kKOff : C_::kVOff);
       if (is_k) {
         uint8_t* sq = smem + C_::kQOff;
-        mbar_arrive_expect_tx(q_full, 2 * C_::kTileBytes);
+        if (rank == 0) mbar_arrive_expect_tx(q_full, CG * 2 * C_::kTileBytes);
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
           for (int c = 0; c < C_::kChunks; ++c)
-            tma_load_3d(sq + t * C_::kTileBytes + c * (kBlockQ * 128), &tmQ, q_full, 64 * c,
-                        int(q0 + t * kBlockQ), int(bh));
+            load3d(sq + t * C_::kTileBytes + c * (kBlockQ * 128), &tmQ, q_full, 64 * c,
+                   int(q0 + t * kBlockQ), int(bh));
       }
       uint32_t filled = 0;
       for (uint32_t j = 0; j < n; ++j) {
         const uint32_t st = j % NS;
         const uint32_t ph = (j / NS) & 1u;
         if (!mbar_wait(&empty[st], ph ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
-        uint8_t* dst = ring + st * C_::kTileBytes;
-        mbar_arrive_expect_tx(&full[st], C_::kTileBytes);
+        uint8_t* dst = ring + st * slot_bytes;
+        if (rank == 0) mbar_arrive_expect_tx(&full[st], CG * slot_bytes);
+        if (is_k) {
+          // K rows [key0, key0 + kKeys) of block j, all D columns
+          const int key0 = int(j * kBlockKV + rank * C_::kKeys);
 #pragma unroll
-        for (int c = 0; c < C_::kChunks; ++c)
-          tma_load_3d(dst + c * (kBlockKV * 128), map, &full[st], 64 * c, int(j * kBlockKV),
-                      int(bh));
+          for (int c = 0; c < C_::kChunks; ++c)
+            load3d(dst + c * (C_::kKeys * 128), map, &full[st], 64 * c, key0, int(bh));
+        } else {
+          // all keys of block j, D columns [col0, col0 + kVCols)
+          const int col0 = int(rank * C_::kVCols);
+#pragma unroll
+          for (int c = 0; c < C_::kVCols / 64; ++c)
+            load3d(dst + c * (kBlockKV * 128), map, &full[st], col0 + 64 * c,
+                   int(j * kBlockKV), int(bh));
+        }
         ++filled;
       }
-      // drain: the last fill of each stage must land before the CTA exits
-      int dummy = 0;
-      if (is_k) mbar_wait(q_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
-      const uint32_t m = filled < uint32_t(NS) ? filled : uint32_t(NS);
-      for (uint32_t i = 0; i < m; ++i) {
-        const uint32_t f = filled - 1 - i;
-        mbar_wait(&full[f % NS], (f / NS) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
+      // drain: the last fill of each stage must land before the CTA exits; the
+      // leader's barriers count the bytes of both CTAs of a pair
+      if (rank == 0) {
+        int dummy = 0;
+        if (is_k) mbar_wait(q_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
+        const uint32_t m = filled < uint32_t(NS) ? filled : uint32_t(NS);
+        for (uint32_t i = 0; i < m; ++i) {
+          const uint32_t f = filled - 1 - i;
+          mbar_wait(&full[f % NS], (f / NS) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc_qk = make_idesc_f16_f32(kBlockQ, kBlockKV, false, false);
-      const uint32_t idesc_pv = make_idesc_f16_f32(kBlockQ, D, false, true);
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc_qk = make_idesc_f16_f32(kBlockQ * CG, kBlockKV, false, false);
+      const uint32_t idesc_pv = make_idesc_f16_f32(kBlockQ * CG, D, false, true);
       const uint32_t sq = smem_u32(smem + C_::kQOff);
+      auto commit_all = [&](uint64_t* bar) {
+        if constexpr (CG == 2) {
+          const uint32_t a = smem_u32(bar);
+          umma_commit_pair(a);
+          umma_commit_pair(mapa_shared(a, 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kWdAttnMma);
       auto issue_s = [&](uint32_t j, int t) {
-        const uint32_t sk = smem_u32(smem + C_::kKOff + (j % KST) * C_::kTileBytes);
+        const uint32_t sk = smem_u32(smem + C_::kKOff + (j % KST) * C_::kKBytes);
         const uint32_t qa = sq + t * C_::kTileBytes;
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k)
-          umma_f16_ss(tmem + col_s(t), kmajor_desc<D>(qa, k), kmajor_desc<D>(sk, k), idesc_qk,
-                      k > 0 ? 1u : 0u);
-        umma_commit(&s_full[t]);
-        if (t == 1) umma_commit(&k_empty[j % KST]);  // K_j consumed by both tiles
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t ad = kmajor_desc<kBlockQ>(qa, k);
+          const uint64_t bd = kmajor_desc<C_::kKeys>(sk, k);
+          if constexpr (CG == 2)
+            umma_f16_ss_pair(tmem + col_s(t), ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+          else
+            umma_f16_ss(tmem + col_s(t), ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+        }
+        commit_all(&s_full[t]);
+        if (t == 1) commit_all(&k_empty[j % KST]);  // K_j consumed by both tiles
       };
       auto issue_pv = [&](uint32_t j, int t) {
-        const uint32_t sv = smem_u32(smem + C_::kVOff + (j % VST) * C_::kTileBytes);
+        const uint32_t sv = smem_u32(smem + C_::kVOff + (j % VST) * C_::kVBytes);
 #pragma unroll
-        for (int k = 0; k < kBlockKV / 16; ++k)
-          umma_f16_ts(tmem + col_o(t), tmem + col_s(t) + k * 8, vmajor_desc<D>(sv, k), idesc_pv,
-                      (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&pv_done[t]);
-        if (t == 1) umma_commit(&v_empty[j % VST]);  // V_j consumed by both tiles
+        for (int k = 0; k < kBlockKV / 16; ++k) {
+          const uint32_t a = tmem + col_s(t) + k * 8;
+          if constexpr (CG == 2)
+            umma_f16_ts_pair(tmem + col_o(t), a, vmajor_desc(sv, k), idesc_pv,
+                             (j > 0 || k > 0) ? 1u : 0u);
+          else
+            umma_f16_ts(tmem + col_o(t), a, vmajor_desc(sv, k), idesc_pv,
+                        (j > 0 || k > 0) ? 1u : 0u);
+        }
+        commit_all(&pv_done[t]);
+        if (t == 1) commit_all(&v_empty[j % VST]);  // V_j consumed by both tiles
       };
       if (ok && n > 0) {
         ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, kWdAttnMma);
@@ -306,9 +367,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Per block j and tile t: PV_t(j) as soon as P_t(j) is ready, then
-      // S_t(j+1) once PV_t(j) has completed (P_t shares S_t's columns). The
-      // two tiles run half a period apart, so while one tile's S(j+1) waits
-      // for its PV(j), the tensor pipe works on the other tile.
+      // S_t(j+1) right behind it (the tensor pipe executes the MMAs in issue
+      // order, so S_t(j+1)'s writes cannot overtake PV_t(j)'s reads of P_t).
+      // The two tiles run half a period apart, so the softmax of one tile
+      // overlaps the other tile's MMAs.
       for (uint32_t j = 0; ok && j < n; ++j) {
         if (!(ok = mbar_wait(&v_full[j % VST], (j / VST) & 1u, abort_flag, p.status,
                              kWdAttnMma)))
@@ -333,7 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      umma_commit(drain);
+      if constexpr (CG == 2)
+        umma_commit_pair(smem_u32(drain));
+      else
+        umma_commit(drain);
       int dummy = 0;
       mbar_wait(drain, 0, &dummy, p.status, kWdDrain, 100000000ull);
     }
@@ -345,6 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = (q * 32u) << 16;
     const uint32_t tS = tmem + lane_addr + col_s(t);
     const uint32_t tO = tmem + lane_addr + col_o(t);
+    const uint32_t p_full_addr = leader_bar(&p_full[t]);
     const float sl2 = p.scale_log2;
     float m = -INFINITY;  // running max in log2 units (the one P is relative to)
     float l = 0.f;
@@ -433,7 +499,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0 && q == 0) FA_TRACE(t, j, 5);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbar_arrive_cluster(p_full_addr);
+        else
+          mbar_arrive(&p_full[t]);
+      }
       if (lane == 0 && q == 0) FA_TRACE(t, j, 6);
     }
     // ---------------------------------------------------------------- epilogue
@@ -467,10 +538,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // no remote signal may target an exited CTA
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem, 512);
+    else
+      tmem_dealloc(tmem, 512);
   }
 }
 
@@ -484,27 +559,55 @@ using namespace felix_sm100::attn;
 
 namespace {
 
-int encode_qkv(CUtensorMap* map, const void* base, uint32_t BH, uint32_t S, uint32_t D) {
+// CTA-pair attention is a build option, off by default: on B200 it is exact
+// (bit-identical O) but slower (4x32x8192x128: 896 vs 1148 TFLOP/s; the
+// pair's cross-CTA barriers cost more than the halved K/V operand traffic saves).
+#ifndef FELIX_FA_PAIRS
+#define FELIX_FA_PAIRS 0
+#endif
+constexpr bool felix_fa_pairs_enabled() { return FELIX_FA_PAIRS != 0; }
+
+int encode_qkv(CUtensorMap* map, const void* base, uint32_t BH, uint32_t S, uint32_t D,
+               uint32_t box_rows) {
   // 3-D view [BH][S][D] so that a tile never crosses into the next head:
   // rows past S are zero-filled by the TMA unit.
   static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
   return encode_tmap_3d_f16(map, base, D, S, BH, uint64_t(D) * 2, uint64_t(S) * D * 2, 64,
-                            kBlockQ, 1);
+                            box_rows, 1);
 }
 
-template <int D>
+template <int D, int CG>
 int configure_once(int device) {
   static int done[64] = {0};
   if (device < 0 || device >= 64) return -1;
   if (!done[device]) {
-
-    cudaError_t e = cudaFuncSetAttribute(flash_attn_fwd_kernel<D>,
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_fwd_kernel<D, CG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg<D>::kSmemBytes);
+                                         Cfg<D, CG>::kSmemBytes);
     if (e != cudaSuccess) return int(e);
     done[device] = 1;
   }
   return 0;
+}
+
+template <int D, int CG>
+cudaError_t launch(uint64_t groups, const CUtensorMap& tq, const CUtensorMap& tk,
+                   const CUtensorMap& tv, const Params& p, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(groups * CG), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg<D, CG>::kSmemBytes;
+  cfg.stream = stream;
+  if (CG == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, flash_attn_fwd_kernel<D, CG>, tq, tk, tv, p);
 }
 
 }  // namespace
@@ -524,10 +627,12 @@ FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, _
   DeviceInfo* dev = current_device_info();
   if (!dev) return launch_error(cudaGetLastError(), "flash_attn: no CUDA device");
 
+  // CTA pairs (D = 128) once a head has at least 512 query rows.
+  const int cg = (head_dim == 128 && seqlen >= 512 && felix_fa_pairs_enabled()) ? 2 : 1;
   CUtensorMap tq, tk, tv;
-  if (encode_qkv(&tq, Q, uint32_t(bh), seqlen, head_dim) ||
-      encode_qkv(&tk, K, uint32_t(bh), seqlen, head_dim) ||
-      encode_qkv(&tv, V, uint32_t(bh), seqlen, head_dim))
+  if (encode_qkv(&tq, Q, uint32_t(bh), seqlen, head_dim, kBlockQ) ||
+      encode_qkv(&tk, K, uint32_t(bh), seqlen, head_dim, kBlockKV / cg) ||
+      encode_qkv(&tv, V, uint32_t(bh), seqlen, head_dim, kBlockKV))
     return api_error("flash_attn: cuTensorMapEncodeTiled failed");
 
   Params p{};
@@ -535,22 +640,26 @@ FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, _
   p.lse = lse;
   p.S = seqlen;
   p.n_kv = (seqlen + kBlockKV - 1) / kBlockKV;
-  p.q_tiles = (seqlen + 2 * kBlockQ - 1) / (2 * kBlockQ);
+  p.q_tiles = (seqlen + 2 * kBlockQ * cg - 1) / (2 * kBlockQ * cg);
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf(float(head_dim));
   p.scale_log2 = sc * 1.4426950408889634f;
   p.status = dev->status_word;
-  const uint64_t grid = bh * p.q_tiles;
-  if (grid > 0x7fffffffull) return api_error("flash_attn: grid too large");
+  const uint64_t groups = bh * p.q_tiles;
+  if (groups * cg > 0x7fffffffull) return api_error("flash_attn: grid too large");
 
   int rc;
-  if (head_dim == 128) {
-    if ((rc = configure_once<128>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    flash_attn_fwd_kernel<128><<<unsigned(grid), kThreads, Cfg<128>::kSmemBytes, stream>>>(tq, tk, tv, p);
+  cudaError_t e;
+  if (head_dim == 128 && cg == 2) {
+    if ((rc = configure_once<128, 2>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    e = launch<128, 2>(groups, tq, tk, tv, p, stream);
+  } else if (head_dim == 128) {
+    if ((rc = configure_once<128, 1>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    e = launch<128, 1>(groups, tq, tk, tv, p, stream);
   } else {
-    if ((rc = configure_once<64>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    flash_attn_fwd_kernel<64><<<unsigned(grid), kThreads, Cfg<64>::kSmemBytes, stream>>>(tq, tk, tv, p);
+    if ((rc = configure_once<64, 1>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    e = launch<64, 1>(groups, tq, tk, tv, p, stream);
   }
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return launch_error(e, "flash_attn: launch failed");
   return FelixCode{FELIX_SUCCESS, cudaSuccess};
 }
