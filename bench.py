@@ -289,6 +289,47 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def reference_gpu_timing(cfg, steps: int, warmup: int):
+    """Time the reference's own kernels (oracle/_ref, built from the unmodified
+    reference sources for sm_100a) on this workload, same protocol as our arm
+    (L2 flushed between steps, CUDA events). None when unavailable."""
+    try:
+        from oracle import reference as ref
+    except Exception:
+        return None
+    if not (ref.available() and torch.cuda.is_available()):
+        return None
+    dev = torch.device("cuda", 0)
+    if isinstance(cfg, W.AttnConfig):
+        Q, K, V = [t.to(dev) for t in W.attn_inputs(cfg)]
+        O = torch.empty_like(Q)
+        step = lambda: ref.flash_attn(Q, K, V, O)  # noqa: E731
+    else:
+        A, B = [t.to(dev) for t in W.gemm_inputs(cfg)]
+        if cfg.dtype == "f32":
+            C = torch.empty(cfg.M, cfg.N, device=dev)
+            step = lambda: ref.sgemm(A, B, C)  # noqa: E731
+        else:
+            C = torch.empty(cfg.M, cfg.N, dtype=torch.half, device=dev)
+            step = lambda: ref.hgemm(A, B, C, nt=cfg.b_layout == "nk")  # noqa: E731
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    for _ in range(warmup):
+        step()
+    times = []
+    for i in range(steps):
+        flush.fill_(float(i))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        step()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    ms = statistics.mean(times)
+    return {"value": cfg.flops / (ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": ms,
+            "what": "the reference's own kernels (fp16-accumulate HGEMM/attention, SIMT "
+                    "SGEMM) built unmodified for sm_100a, timed on the same B200"}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return 0
@@ -313,6 +354,10 @@ def run_reference(args, world, rank):
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    try:
+        line["reference_gpu"] = reference_gpu_timing(cfg, max(args.steps, 5), args.warmup)
+    except Exception as e:  # the comparator is informative only
+        line["reference_gpu"] = {"unavailable": str(e)[:200]}
     print(json.dumps(line), flush=True)
     return 0
 
