@@ -11,7 +11,8 @@
 // memory fed by 128-bit global loads staged in registers (one barrier per K
 // step), operand fragments double-buffered in registers. Measured on B200
 // (1024^3 / 4096^3 TFLOP/s): BK 16 + 2 CTAs/SM 29.9 / 44.7, BK 8 + 2 CTAs/SM
-// 28.3 / 42.3; a packed fma.rn.f32x2 inner product was slower (25.0 / 38.7). Any M, N, K:
+// 28.3 / 42.3; a packed fma.rn.f32x2 inner product was slower (25.0 / 38.7),
+// and so was an 8 x 16 register block with a 128 x 256 tile (16.4 / 33.5). Any M, N, K:
 // loads are predicated with zero fill, stores are bounds-checked; the 128-bit
 // path is used when rows are 16-byte aligned. Small problems are split along K
 // so that the grid covers every SM twice; the last CTA of a tile to finish
@@ -32,8 +33,17 @@ namespace sgemm {
 #ifndef FELIX_SGEMM_MINB
 #define FELIX_SGEMM_MINB 2
 #endif
-constexpr int BM = 128, BN = 128, BK = FELIX_SGEMM_BK, kThreads = 256;
-constexpr int kLd = BK / 8;  // float4 loads of A and of B per thread per k-tile
+#ifndef FELIX_SGEMM_TN
+#define FELIX_SGEMM_TN 8
+#endif
+// Per-thread register block 8 x TN (TN = 8: CTA tile 128 x 128; TN = 16: 128 x 256).
+constexpr int TN = FELIX_SGEMM_TN;
+constexpr int NB = TN / 4;  // 4-wide column groups per thread, 64 columns apart
+constexpr int BM = 128, BN = 16 * TN, BK = FELIX_SGEMM_BK, kThreads = 256;
+constexpr int kLd = BK / 8;             // float4 loads of A per thread per k-tile
+constexpr int kLdB = BN * BK / 1024;    // float4 loads of B per thread per k-tile
+constexpr int kPartF4 = 2 * TN;         // float4s of a thread's partial block
+static_assert(TN == 8 || TN == 16, "register block");
 static_assert(BK == 8 || BK == 16, "k-tile");
 constexpr int APAD = 4;  // As row pitch 132 floats: transposed stores avoid bank conflicts
 
@@ -52,7 +62,7 @@ struct Params {
 // B: thread -> k row t/(256/BK), columns (t%(256/BK))*BK/2 ...
 template <bool VEC>
 __device__ __forceinline__ void load_tile(const Params& p, uint32_t m0, uint32_t n0, uint32_t k0,
-                                          uint32_t kend, float4 (&ra)[kLd], float4 (&rb)[kLd]) {
+                                          uint32_t kend, float4 (&ra)[kLd], float4 (&rb)[kLdB]) {
   const uint32_t t = threadIdx.x;
   {
     const uint32_t r = m0 + t / 2;
@@ -78,8 +88,8 @@ __device__ __forceinline__ void load_tile(const Params& p, uint32_t m0, uint32_t
     const bool kv = k < kend;
     const float* b = p.B + size_t(k) * p.N;
 #pragma unroll
-    for (int q = 0; q < kLd; ++q) {
-      const uint32_t c = n0 + (t % tpr) * (BK / 2) + 4 * q;
+    for (int q = 0; q < kLdB; ++q) {
+      const uint32_t c = n0 + (t % tpr) * (4 * kLdB) + 4 * q;
       if (VEC) {
         rb[q] = (kv && c < p.N) ? __ldg(reinterpret_cast<const float4*>(b + c))
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -94,7 +104,7 @@ __device__ __forceinline__ void load_tile(const Params& p, uint32_t m0, uint32_t
 }
 
 __device__ __forceinline__ void store_tile(float (*As)[BM + APAD], float (*Bs)[BN],
-                                           const float4 (&ra)[kLd], const float4 (&rb)[kLd]) {
+                                           const float4 (&ra)[kLd], const float4 (&rb)[kLdB]) {
   const uint32_t t = threadIdx.x;
   const uint32_t r = t / 2;
 #pragma unroll
@@ -107,8 +117,8 @@ __device__ __forceinline__ void store_tile(float (*As)[BM + APAD], float (*Bs)[B
   }
   constexpr uint32_t tpr = 256 / BK;
 #pragma unroll
-  for (int q = 0; q < kLd; ++q)
-    *reinterpret_cast<float4*>(&Bs[t / tpr][(t % tpr) * (BK / 2) + 4 * q]) = rb[q];
+  for (int q = 0; q < kLdB; ++q)
+    *reinterpret_cast<float4*>(&Bs[t / tpr][(t % tpr) * (4 * kLdB) + 4 * q]) = rb[q];
 }
 
 template <bool VEC>
@@ -151,14 +161,14 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
   const uint32_t kbeg = z * p.k_per_split;
   const uint32_t kend = min(p.K, kbeg + p.k_per_split);
 
-  float acc[8][8];
+  float acc[8][TN];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
 
   const uint32_t nk = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
-  float4 ra[kLd], rb[kLd];
+  float4 ra[kLd], rb[kLdB];
   if (nk > 0) {
     load_tile<VEC>(p, m0, n0, kbeg, kend, ra, rb);
     store_tile(As[0], Bs[0], ra, rb);
@@ -169,28 +179,36 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
     const uint32_t cur = kt & 1u;
     if (kt + 1 < nk) load_tile<VEC>(p, m0, n0, kbeg + (kt + 1) * BK, kend, ra, rb);
     // register double-buffered fragments: load step k+1 before the FFMAs of k
-    float4 fa[2][2], fb[2][2];
+    float4 fa[2][2], fb[2][NB];
     fa[0][0] = *reinterpret_cast<const float4*>(&As[cur][0][ty * 4]);
     fa[0][1] = *reinterpret_cast<const float4*>(&As[cur][0][64 + ty * 4]);
-    fb[0][0] = *reinterpret_cast<const float4*>(&Bs[cur][0][tx * 4]);
-    fb[0][1] = *reinterpret_cast<const float4*>(&Bs[cur][0][64 + tx * 4]);
+#pragma unroll
+    for (int g = 0; g < NB; ++g)
+      fb[0][g] = *reinterpret_cast<const float4*>(&Bs[cur][0][64 * g + tx * 4]);
 #pragma unroll
     for (int k = 0; k < BK; ++k) {
       const int c = k & 1, n = c ^ 1;
       if (k + 1 < BK) {
         fa[n][0] = *reinterpret_cast<const float4*>(&As[cur][k + 1][ty * 4]);
         fa[n][1] = *reinterpret_cast<const float4*>(&As[cur][k + 1][64 + ty * 4]);
-        fb[n][0] = *reinterpret_cast<const float4*>(&Bs[cur][k + 1][tx * 4]);
-        fb[n][1] = *reinterpret_cast<const float4*>(&Bs[cur][k + 1][64 + tx * 4]);
+#pragma unroll
+        for (int g = 0; g < NB; ++g)
+          fb[n][g] = *reinterpret_cast<const float4*>(&Bs[cur][k + 1][64 * g + tx * 4]);
       }
       const float a[8] = {fa[c][0].x, fa[c][0].y, fa[c][0].z, fa[c][0].w,
                           fa[c][1].x, fa[c][1].y, fa[c][1].z, fa[c][1].w};
-      const float b[8] = {fb[c][0].x, fb[c][0].y, fb[c][0].z, fb[c][0].w,
-                          fb[c][1].x, fb[c][1].y, fb[c][1].z, fb[c][1].w};
+      float b[TN];
+#pragma unroll
+      for (int g = 0; g < NB; ++g) {
+        b[4 * g] = fb[c][g].x;
+        b[4 * g + 1] = fb[c][g].y;
+        b[4 * g + 2] = fb[c][g].z;
+        b[4 * g + 3] = fb[c][g].w;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
     if (kt + 1 < nk) store_tile(As[cur ^ 1u], Bs[cur ^ 1u], ra, rb);
     __syncthreads();
@@ -200,22 +218,24 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint32_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
-      const float v0[4] = {acc[i][0], acc[i][1], acc[i][2], acc[i][3]};
-      const float v1[4] = {acc[i][4], acc[i][5], acc[i][6], acc[i][7]};
-      store_out<VEC>(p, row, n0 + tx * 4, v0);
-      store_out<VEC>(p, row, n0 + 64 + tx * 4, v1);
+#pragma unroll
+      for (int g = 0; g < NB; ++g) {
+        const float v[4] = {acc[i][4 * g], acc[i][4 * g + 1], acc[i][4 * g + 2], acc[i][4 * g + 3]};
+        store_out<VEC>(p, row, n0 + 64 * g + tx * 4, v);
+      }
     }
     return;
   }
 
-  // Split-K: publish the partial (float4 j of thread t at [j][t]: coalesced).
+  // Split-K: publish the partial (float4 q of thread t at [q][t]: coalesced).
   const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
-  float4* part = reinterpret_cast<float4*>(p.ws) + (size_t(tile) * p.splits + z) * (16 * 256);
+  float4* part = reinterpret_cast<float4*>(p.ws) + (size_t(tile) * p.splits + z) * (kPartF4 * 256);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    __stcg(part + (2 * i) * 256 + t, make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]));
-    __stcg(part + (2 * i + 1) * 256 + t, make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]));
-  }
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int g = 0; g < NB; ++g)
+      __stcg(part + (i * NB + g) * 256 + t,
+             make_float4(acc[i][4 * g], acc[i][4 * g + 1], acc[i][4 * g + 2], acc[i][4 * g + 3]));
   __threadfence();
   __syncthreads();
   if (t == 0) {
@@ -227,21 +247,21 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const float4* base = reinterpret_cast<const float4*>(p.ws) + size_t(tile) * p.splits * (16 * 256);
+  const float4* base =
+      reinterpret_cast<const float4*>(p.ws) + size_t(tile) * p.splits * (kPartF4 * 256);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
-    for (uint32_t zz = 0; zz < p.splits; ++zz) {
-      const float4 x0 = __ldcg(base + zz * (16 * 256) + (2 * i) * 256 + t);
-      const float4 x1 = __ldcg(base + zz * (16 * 256) + (2 * i + 1) * 256 + t);
-      s0.x += x0.x; s0.y += x0.y; s0.z += x0.z; s0.w += x0.w;
-      s1.x += x1.x; s1.y += x1.y; s1.z += x1.z; s1.w += x1.w;
-    }
     const uint32_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
-    const float v0[4] = {s0.x, s0.y, s0.z, s0.w};
-    const float v1[4] = {s1.x, s1.y, s1.z, s1.w};
-    store_out<VEC>(p, row, n0 + tx * 4, v0);
-    store_out<VEC>(p, row, n0 + 64 + tx * 4, v1);
+#pragma unroll
+    for (int g = 0; g < NB; ++g) {
+      float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (uint32_t zz = 0; zz < p.splits; ++zz) {
+        const float4 x0 = __ldcg(base + zz * (kPartF4 * 256) + (i * NB + g) * 256 + t);
+        s0.x += x0.x; s0.y += x0.y; s0.z += x0.z; s0.w += x0.w;
+      }
+      const float v[4] = {s0.x, s0.y, s0.z, s0.w};
+      store_out<VEC>(p, row, n0 + 64 * g + tx * 4, v);
+    }
   }
 }
 
