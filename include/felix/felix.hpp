@@ -19,9 +19,8 @@ FelixStatus ampere_hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha,
                                 half const* B, float beta, half* C, cudaStream_t stream,
                                 const std::string& kernel_name = "cute_hgemm_128x128_nn");
 
-// Declared for signature compatibility; top-k is not part of this library and
-// dispatch throws std::runtime_error("No matching kernel found") like any
-// unregistered name.
+// k-th largest / smallest value per slice ("sorting_radix_select" and
+// "sm100_topk" both select the sm_100a radix-select kernels).
 FelixStatus sorting_radix_select_launch(float const* data, float* out, uint32_t num_slices,
                                         uint32_t slice_size, uint32_t k, bool largest,
                                         cudaStream_t stream,

@@ -135,6 +135,19 @@ int felix_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, f
                          float scale, void* stream);
 
 /*
+ * k-th value per slice (radix select): out[s] = the k-th largest (largest != 0)
+ * or k-th smallest value of data[s * slice_size, (s + 1) * slice_size), fp32,
+ * returned bit-exactly (order: NaN above +inf, -0.0 below +0.0).
+ * Replaces felix::sorting_radix_select_launch / "sorting_radix_select"
+ * (reference include/felix/felix.hpp:17-20,
+ * src/felix/topk/sorting_radix_select_kernel_launch.cu:7-38); same argument
+ * rules: num_slices == 0 is a no-op, null pointers or k outside
+ * [1, slice_size] are FELIX_API_ERROR.
+ */
+int felix_topk_select(const float* data, float* out, uint32_t num_slices, uint32_t slice_size,
+                      uint32_t k, int largest, void* stream);
+
+/*
  * Device watchdog. Every bounded wait inside the kernels records a nonzero
  * site code in a per-device status word when it gives up. Reads (and, when
  * clear != 0, resets) the word of the current device; synchronises the device.

@@ -43,6 +43,7 @@ def lib() -> C.CDLL:
         L.oracle_double_to_half.argtypes = [C.c_double]
         L.oracle_half_to_double_array.argtypes = [P, P, C.c_int64]
         L.oracle_double_to_half_array.argtypes = [P, P, C.c_int64]
+        L.oracle_topk.argtypes = [P, P, C.c_int64, C.c_int64, C.c_int64, C.c_int]
         L.oracle_set_threads.argtypes = [C.c_int]
         L.oracle_get_threads.restype = C.c_int
         _lib = L
@@ -105,6 +106,16 @@ def attention(Q, K, V, scale=0.0, rows=None):
     lib().oracle_attention_rows(Bn, H, S, D, _p(Q), _p(K), _p(V), float(scale), _p(r),
                                 0 if r is None else len(r), _p(O), _p(L))
     return O, L
+
+
+def topk(data: np.ndarray, k: int, largest: bool = True) -> np.ndarray:
+    """data [num_slices, slice_size] float32 -> [num_slices] float32: the k-th
+    largest / smallest value of each slice, bit-exact."""
+    d = np.ascontiguousarray(data, dtype=np.float32)
+    ns, n = d.shape
+    out = np.empty(ns, np.uint32)
+    lib().oracle_topk(_p(d.view(np.uint32)), _p(out), ns, n, int(k), 1 if largest else 0)
+    return out.view(np.float32)
 
 
 def half_to_double(bits: np.ndarray) -> np.ndarray:

@@ -43,6 +43,8 @@ _SIGS = {
                                                                  C.POINTER(C.c_size_t)]),
     "felix_flash_attn_fwd": (C.c_int, [C.c_void_p] * 5 + [C.c_uint32] * 4 + [C.c_float,
                                                                             C.c_void_p]),
+    "felix_topk_select": (C.c_int, [C.c_void_p, C.c_void_p] + [C.c_uint32] * 3 +
+                          [C.c_int, C.c_void_p]),
     "felix_watchdog_status": (C.c_int, [C.POINTER(C.c_uint), C.c_int]),
     "felix_watchdog_probe": (C.c_int, [C.c_uint32, C.c_void_p]),
     "felix_num_sms": (C.c_int, [C.POINTER(C.c_int)]),
@@ -156,6 +158,14 @@ def flash_attn_fwd(Q, K, V, O, lse=None, scale=0.0, stream=None):
     check(lib().felix_flash_attn_fwd(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(lse), H, B, S, D,
                                      float(scale), _stream(stream)))
     return O
+
+
+def topk_select(data, out, k, largest=True, stream=None):
+    """data [num_slices, slice_size] fp32 -> out [num_slices]: k-th largest/smallest."""
+    num_slices, slice_size = data.shape
+    check(lib().felix_topk_select(_ptr(data), _ptr(out), num_slices, slice_size, k,
+                                  1 if largest else 0, _stream(stream)))
+    return out
 
 
 def watchdog_status(clear=True) -> int:

@@ -142,6 +142,12 @@ FelixStatus sm100_hgemm_nt(uint32_t M, uint32_t N, uint32_t K, float alpha, cons
   return from_c(felix_hgemm(M, N, K, alpha, A, B, beta, C, FELIX_B_NK, stream));
 }
 
+// --- top-k (k-th value per slice)
+FelixStatus sm100_topk(float const* data, float* out, uint32_t num_slices, uint32_t slice_size,
+                       uint32_t k, bool largest, cudaStream_t stream) {
+  return from_c(felix_topk_select(data, out, num_slices, slice_size, k, largest ? 1 : 0, stream));
+}
+
 // --- flash attention launchers
 template <int D>
 FelixStatus sm100_flash_attn(half* Q, half* K, half* V, half* O, uint32_t heads,
@@ -232,6 +238,9 @@ FELIX_REG(cute_hgemm_128x128_nn, HGEMM, "cute_hgemm_128x128_nn", &felix::sm100_h
 FELIX_REG(cute_hgemm_128x128_nt, HGEMM, "cute_hgemm_128x128_nt", &felix::sm100_hgemm_nt, true);
 FELIX_REG(sm100_hgemm_nn, HGEMM, "sm100_hgemm_nn", &felix::sm100_hgemm_nn, true);
 FELIX_REG(sm100_hgemm_nt, HGEMM, "sm100_hgemm_nt", &felix::sm100_hgemm_nt, true);
+
+FELIX_REG(sorting_radix_select, TopK, "sorting_radix_select", &felix::sm100_topk, true);
+FELIX_REG(sm100_topk, TopK, "sm100_topk", &felix::sm100_topk, true);
 
 FELIX_REG(fa64_ampere_name, FlashAttn_64, "ampere_flash_attn_mma16168_64_1D_warp_tiling",
           &felix::sm100_flash_attn<64>, true);

@@ -312,6 +312,12 @@ int felix_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, f
                                   static_cast<cudaStream_t>(stream)));
 }
 
+int felix_topk_select(const float* data, float* out, uint32_t num_slices, uint32_t slice_size,
+                      uint32_t k, int largest, void* stream) {
+  return finish(topk_select_launch(data, out, num_slices, slice_size, k, largest != 0,
+                                   static_cast<cudaStream_t>(stream)));
+}
+
 int felix_watchdog_status(unsigned* code, int clear) {
   DeviceInfo* d = current_device_info();
   if (!d) return launch_error(cudaGetLastError(), "no device").type;

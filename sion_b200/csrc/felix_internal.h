@@ -91,6 +91,9 @@ FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, _
                             float* lse, uint32_t heads, uint32_t batch, uint32_t seqlen,
                             uint32_t head_dim, float scale, cudaStream_t stream);
 
+FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
+                             uint32_t slice_size, uint32_t k, bool largest, cudaStream_t stream);
+
 FelixCode watchdog_probe_launch(uint32_t limit_us, cudaStream_t stream);
 
 }  // namespace felix_impl

@@ -1,0 +1,267 @@
+// k-th value selection per slice (top-k radix select) for sm_100a.
+// out[s] = the k-th largest (largest != 0) or k-th smallest value of
+// data[s * slice_size .. (s + 1) * slice_size), fp32.
+// Replaces felix::sorting_radix_select_launch / "sorting_radix_select"
+// (reference: include/felix/felix.hpp:17-20,
+// src/felix/topk/sorting_radix_select_kernel_launch.cu:7-38,
+// kernels/sorting_radix_select.cuh:153-213), with the same ordering: floats are
+// mapped to order-preserving uint32 keys (negative values bit-inverted, others
+// with the sign bit set; NaN compares above +inf), and the key found maps back
+// to the exact value bits (so -0.0 and +0.0 are distinct, -0.0 < +0.0).
+//
+// Design (HBM-bound integer work, no tensor cores):
+//   * the k-th largest is the (n - k)-th smallest (0-based rank), so one
+//     ascending select serves both directions;
+//   * four passes over 8-bit digits, most significant first; each pass builds
+//     a 256-bin histogram of the keys that still match the chosen prefix and
+//     picks the digit where the running count passes the rank;
+//   * many slices: one CTA per slice; slices up to 48K values are staged once
+//     into shared memory (so HBM is read once), per-warp sub-histograms limit
+//     atomic contention;
+//   * few large slices: every pass is a grid-wide histogram kernel over all
+//     SMs plus a one-warp digit pick per slice, with the histograms and the
+//     per-slice (prefix, rank) state in library scratch.
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "felix_internal.h"
+
+namespace felix_sm100 {
+namespace topk {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr uint32_t kSmemKeys = 48 * 1024;  // staged keys per slice (192 KB)
+
+__device__ __forceinline__ uint32_t to_key(float v) {
+  const uint32_t x = __float_as_uint(v);
+  if (v != v) return 0xffffffffu;  // NaN above everything
+  return x ^ ((x & 0x80000000u) ? 0xffffffffu : 0x80000000u);
+}
+__device__ __forceinline__ float from_key(uint32_t k) {
+  return __uint_as_float(k ^ ((k & 0x80000000u) ? 0x80000000u : 0xffffffffu));
+}
+
+// Digit whose cumulative count first exceeds `rank` (counts of one pass), and
+// the count of keys below it. Executed by one full warp.
+__device__ __forceinline__ void pick_digit(const uint32_t* hist, uint32_t rank, uint32_t& digit,
+                                          uint32_t& below) {
+  const uint32_t lane = threadIdx.x & 31u;
+  uint32_t c[8], sum = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c[i] = hist[lane * 8 + i];
+    sum += c[i];
+  }
+  // exclusive prefix of the 32 lane sums
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= uint32_t(o)) incl += v;
+  }
+  const uint32_t excl = incl - sum;
+  const bool mine = rank >= excl && rank < incl;
+  const uint32_t who = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+  uint32_t d = 0, b = 0;
+  if (lane == who) {
+    uint32_t run = excl;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (rank < run + c[i]) {
+        d = lane * 8 + i;
+        b = run;
+        break;
+      }
+      run += c[i];
+    }
+  }
+  digit = __shfl_sync(0xffffffffu, d, who);
+  below = __shfl_sync(0xffffffffu, b, who);
+}
+
+// One CTA per slice.
+__global__ void __launch_bounds__(kThreads) select_per_slice_kernel(const float* __restrict__ data,
+                                                                  float* __restrict__ out,
+                                                                  uint32_t slice_size, uint32_t k,
+                                                                  int largest, int staged) {
+  extern __shared__ uint32_t keys[];                  // [slice_size] when staged
+  __shared__ uint32_t hist[kWarps][256];
+  __shared__ uint32_t merged[256];
+  __shared__ uint32_t s_prefix, s_rank;
+  const uint32_t t = threadIdx.x, w = t / 32;
+  const float* src = data + size_t(blockIdx.x) * slice_size;
+  if (staged) {
+    for (uint32_t i = t; i < slice_size; i += kThreads) keys[i] = to_key(__ldg(src + i));
+  }
+  if (t == 0) {
+    s_prefix = 0;
+    s_rank = largest ? slice_size - k : k - 1;
+  }
+  uint32_t mask = 0;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (uint32_t i = t; i < kWarps * 256; i += kThreads) (&hist[0][0])[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix;
+    for (uint32_t i = t; i < slice_size; i += kThreads) {
+      const uint32_t key = staged ? keys[i] : to_key(__ldg(src + i));
+      if ((key & mask) == prefix) atomicAdd(&hist[w][(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    for (uint32_t b = t; b < 256; b += kThreads) {
+      uint32_t s = 0;
+#pragma unroll
+      for (int ww = 0; ww < kWarps; ++ww) s += hist[ww][b];
+      merged[b] = s;
+    }
+    __syncthreads();
+    if (w == 0) {
+      uint32_t d, below;
+      pick_digit(merged, s_rank, d, below);
+      if (t == 0) {
+        s_rank -= below;
+        s_prefix = prefix | (d << shift);
+      }
+    }
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  if (t == 0) out[blockIdx.x] = from_key(s_prefix);
+}
+
+// Grid-wide pass for few large slices: histogram of the digit at `shift` of
+// the keys of slice blockIdx.y that match state.prefix under `mask`.
+struct SliceState {
+  uint32_t prefix;
+  uint32_t rank;
+};
+
+__global__ void __launch_bounds__(kThreads) histogram_pass_kernel(const float* __restrict__ data,
+                                                                  uint32_t slice_size, int shift,
+                                                                  uint32_t mask,
+                                                                  const SliceState* state,
+                                                                  uint32_t* __restrict__ hist) {
+  __shared__ uint32_t h[kWarps][256];
+  const uint32_t t = threadIdx.x, w = t / 32;
+  for (uint32_t i = t; i < kWarps * 256; i += kThreads) (&h[0][0])[i] = 0;
+  __syncthreads();
+  const uint32_t slice = blockIdx.y;
+  const uint32_t prefix = state[slice].prefix;
+  const float* src = data + size_t(slice) * slice_size;
+  const uint32_t n4 = (slice_size & 3u) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0
+                          ? slice_size / 4
+                          : 0;
+  const uint32_t stride = gridDim.x * kThreads;
+  for (uint32_t i = blockIdx.x * kThreads + t; i < n4; i += stride) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(src) + i);
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t key = to_key(vv[j]);
+      if ((key & mask) == prefix) atomicAdd(&h[w][(key >> shift) & 255u], 1u);
+    }
+  }
+  for (uint32_t i = n4 * 4 + blockIdx.x * kThreads + t; i < slice_size; i += stride) {
+    const uint32_t key = to_key(__ldg(src + i));
+    if ((key & mask) == prefix) atomicAdd(&h[w][(key >> shift) & 255u], 1u);
+  }
+  __syncthreads();
+  for (uint32_t b = t; b < 256; b += kThreads) {
+    uint32_t s = 0;
+#pragma unroll
+    for (int ww = 0; ww < kWarps; ++ww) s += h[ww][b];
+    if (s) atomicAdd(&hist[size_t(slice) * 256 + b], s);
+  }
+}
+
+// One warp per slice: choose the digit, update (prefix, rank), clear the
+// histogram for the next pass; after the last pass write the value.
+__global__ void pick_pass_kernel(uint32_t* hist, SliceState* state, int shift, int last,
+                                 float* out) {
+  const uint32_t slice = blockIdx.x;
+  uint32_t* hs = hist + size_t(slice) * 256;
+  uint32_t d, below;
+  pick_digit(hs, state[slice].rank, d, below);
+  __syncwarp();
+  for (uint32_t b = threadIdx.x; b < 256; b += 32) hs[b] = 0;
+  if (threadIdx.x == 0) {
+    state[slice].rank -= below;
+    state[slice].prefix |= d << shift;
+    if (last) out[slice] = from_key(state[slice].prefix);
+  }
+}
+
+__global__ void init_state_kernel(SliceState* state, uint32_t num_slices, uint32_t slice_size,
+                                  uint32_t k, int largest) {
+  const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s < num_slices) {
+    state[s].prefix = 0;
+    state[s].rank = largest ? slice_size - k : k - 1;
+  }
+}
+
+}  // namespace topk
+}  // namespace felix_sm100
+
+namespace felix_impl {
+
+using namespace felix_sm100::topk;
+
+FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
+                             uint32_t slice_size, uint32_t k, bool largest,
+                             cudaStream_t stream) {
+  // Argument rules of the reference launcher (sorting_radix_select_kernel_launch.cu:12-25).
+  if (num_slices == 0) return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  if (!data || !out) return api_error("topk: data/out must be non-null");
+  if (slice_size == 0 || k == 0 || k > slice_size)
+    return api_error("topk: k must be in [1, slice_size] and slice_size > 0");
+  if (num_slices > 65535u * 1024u) return api_error("topk: too many slices");
+  DeviceInfo* dev = current_device_info();
+  if (!dev) return launch_error(cudaGetLastError(), "topk: no CUDA device");
+
+  // Few slices, each far larger than one CTA streams quickly: spread every
+  // pass over the whole GPU.
+  const bool grid_wide = num_slices < uint32_t(dev->num_sms) / 2 && slice_size >= (1u << 20) &&
+                         num_slices <= 65535u;
+  cudaError_t e;
+  if (!grid_wide) {
+    const int staged = slice_size <= kSmemKeys ? 1 : 0;
+    const size_t smem = staged ? size_t(slice_size) * 4 : 0;
+    static bool configured[64] = {false};
+    if (!configured[dev->ordinal]) {
+      e = cudaFuncSetAttribute(select_per_slice_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               int(kSmemKeys * 4));
+      if (e != cudaSuccess) return FelixCode{FELIX_API_ERROR, e};
+      configured[dev->ordinal] = true;
+    }
+    select_per_slice_kernel<<<num_slices, kThreads, smem, stream>>>(data, out, slice_size, k,
+                                                                    largest ? 1 : 0, staged);
+  } else {
+    const size_t need = kWsCounterBytes + size_t(num_slices) * (256 * 4 + sizeof(SliceState));
+    uint8_t* ws = static_cast<uint8_t*>(library_workspace(dev, stream, need));
+    if (!ws) return launch_error(cudaErrorMemoryAllocation, "topk: workspace");
+    uint32_t* hist = reinterpret_cast<uint32_t*>(ws + kWsCounterBytes);
+    SliceState* state = reinterpret_cast<SliceState*>(hist + size_t(num_slices) * 256);
+    e = cudaMemsetAsync(hist, 0, size_t(num_slices) * 256 * 4, stream);
+    if (e != cudaSuccess) return launch_error(e, "topk: clearing histograms");
+    init_state_kernel<<<(num_slices + 255) / 256, 256, 0, stream>>>(state, num_slices, slice_size,
+                                                                    k, largest ? 1 : 0);
+    const uint32_t per_slice = (uint32_t(dev->num_sms) * 2 + num_slices - 1) / num_slices;
+    const uint32_t max_blocks = (slice_size + kThreads * 4 - 1) / (kThreads * 4);
+    const dim3 grid(per_slice < max_blocks ? per_slice : max_blocks, num_slices);
+    uint32_t mask = 0;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      histogram_pass_kernel<<<grid, kThreads, 0, stream>>>(data, slice_size, shift, mask, state,
+                                                           hist);
+      pick_pass_kernel<<<num_slices, 32, 0, stream>>>(hist, state, shift, pass == 3 ? 1 : 0, out);
+      mask |= 255u << shift;
+    }
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return launch_error(e, "topk: launch failed");
+  return FelixCode{FELIX_SUCCESS, cudaSuccess};
+}
+
+}  // namespace felix_impl

@@ -65,3 +65,25 @@ def test_half_conversions_exhaustive():
 
 def test_golden_fixtures_present():
     assert len(glob.glob(os.path.join(GOLD, "*.npz"))) == 6
+
+
+def test_topk_oracle_matches_numpy_ordering():
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((5, 101)).astype(np.float32)
+    x[0, :10] = np.float32(0.5)           # duplicates
+    x[1, 3] = -0.0
+    x[1, 4] = 0.0
+    x[2, 7] = np.inf
+    x[2, 8] = -np.inf
+    for k in (1, 2, 50, 101):
+        for largest in (True, False):
+            got = oracle.topk(x, k, largest)
+            srt = np.sort(x, axis=1)  # numpy sorts -0.0 == 0.0: compare values
+            want = srt[:, -k] if largest else srt[:, k - 1]
+            np.testing.assert_array_equal(got, want)
+    # NaN is the largest key
+    y = np.array([[1.0, np.nan, 3.0]], np.float32)
+    assert np.isnan(oracle.topk(y, 1, True)[0]) and oracle.topk(y, 2, True)[0] == 3.0
+    # -0.0 orders below +0.0 (bit-exact result)
+    z = np.array([[0.0, -0.0]], np.float32)
+    assert oracle.topk(z, 1, False).view(np.uint32)[0] == np.float32(-0.0).view(np.uint32)

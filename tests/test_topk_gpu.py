@@ -1,0 +1,58 @@
+"""k-th value per slice (felix_topk_select, the reference's sorting_radix_select)
+through the C ABI against the CPU oracle: bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(felix, x, k, largest):
+    out = torch.empty(x.shape[0], device="cuda")
+    felix.topk_select(torch.from_numpy(x).cuda(), out, k, largest)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32),
+                                  oracle.topk(x, k, largest).view(np.uint32))
+
+
+@pytest.mark.parametrize("largest", [True, False])
+@pytest.mark.parametrize("ns,n,k", [(1, 1, 1), (7, 100, 1), (7, 100, 100), (300, 1000, 17),
+                                    (64, 49152, 1000), (3, 49153, 5), (2, 200000, 77777)])
+def test_topk_random(felix, ns, n, k, largest):
+    rng = np.random.default_rng(ns * 7 + n)
+    _check(felix, rng.standard_normal((ns, n)).astype(np.float32), k, largest)
+
+
+@pytest.mark.parametrize("largest", [True, False])
+def test_topk_special_values(felix, largest):
+    rng = np.random.default_rng(5)
+    x = rng.integers(-3, 4, size=(16, 5000)).astype(np.float32)  # heavy duplicates
+    x[0, :100] = np.nan
+    x[1, :50] = -0.0
+    x[2, :50] = np.inf
+    x[3, :50] = -np.inf
+    x[4, :] = 0.0
+    x[5, ::2] = -0.0
+    for k in (1, 2, 50, 101, 2500, 5000):
+        _check(felix, x, k, largest)
+
+
+@pytest.mark.parametrize("largest", [True, False])
+def test_topk_few_huge_slices_grid_wide(felix, largest):
+    # few slices of >= 1M values take the grid-wide path
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((2, 3_000_001)).astype(np.float32)
+    x[1, :1000] = 7.0
+    for k in (1, 1000, 1500000):
+        _check(felix, x, k, largest)
+
+
+def test_topk_argument_errors(felix):
+    x = torch.zeros(2, 10, device="cuda")
+    out = torch.empty(2, device="cuda")
+    for k in (0, 11):
+        with pytest.raises(felix.FelixError) as e:
+            felix.topk_select(x, out, k)
+        assert e.value.code == felix.API_ERROR
