@@ -188,7 +188,7 @@ class AttnRunner:
                                                                             cfg.D).contiguous()
                        for t in (Q, K, V)]
             self.work_fraction = (s1 - s0) / (cfg.B * cfg.H)
-            cfg = W.AttnConfig(cfg.name, 1, s1 - s0, cfg.S, cfg.D, cfg.seed)
+            cfg = W.AttnConfig(cfg.name, 1, s1 - s0, cfg.S, cfg.D, cfg.seed, cfg.causal)
             self.cfg = cfg
         self.h = [t.pin_memory() for t in (Q, K, V)]
         self.d = [t.to(device) for t in self.h]
@@ -199,7 +199,8 @@ class AttnRunner:
         self.launches_per_step = 1
 
     def step(self):
-        self.abi.flash_attn_fwd(self.d[0], self.d[1], self.d[2], self.dO, self.dL)
+        self.abi.flash_attn_fwd(self.d[0], self.d[1], self.d[2], self.dO, self.dL,
+                                causal=self.cfg.causal)
 
     def step_e2e(self):
         for d, h in zip(self.d, self.h):

@@ -34,11 +34,12 @@ FelixStatus ampere_flash_attn_launch(half* Q, half* K, half* V, half* O, uint32_
                                          "ampere_flash_attn_mma16168_64_1D_warp_tiling");
 
 // new: same operator with the fp32 natural-log LSE of every query row
-// ([batch, heads, seqlen]; lse may be nullptr).
+// ([batch, heads, seqlen]; lse may be nullptr) and an optional causal mask
+// (query i attends to keys 0..i).
 template <int HEAD_DIM, int Bc = 64>
 FelixStatus flash_attn_fwd_lse_launch(half* Q, half* K, half* V, half* O, float* lse,
                                       uint32_t heads, uint32_t batch_size, uint32_t QKV_seqlen,
-                                      cudaStream_t stream);
+                                      cudaStream_t stream, bool causal = false);
 
 // new: reads (and clears) the device watchdog word; KERNEL_RUNTIME_ERROR when a
 // bounded wait inside a kernel gave up. Synchronises the device.

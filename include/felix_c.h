@@ -135,6 +135,17 @@ int felix_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, f
                          float scale, void* stream);
 
 /*
+ * Flash-attention forward with an optional causal mask (causal != 0: query i
+ * attends to keys 0..i, queries and keys aligned at position 0, as
+ * scaled_dot_product_attention(is_causal=True) with equal lengths). Otherwise
+ * identical to felix_flash_attn_fwd. No reference counterpart: the reference
+ * kernel supports no mask (reference README.md:23).
+ */
+int felix_flash_attn_fwd_ex(const void* Q, const void* K, const void* V, void* O, float* lse,
+                            uint32_t heads, uint32_t batch, uint32_t seqlen, uint32_t head_dim,
+                            float scale, int causal, void* stream);
+
+/*
  * k-th value per slice (radix select): out[s] = the k-th largest (largest != 0)
  * or k-th smallest value of data[s * slice_size, (s + 1) * slice_size), fp32,
  * returned bit-exactly (order: NaN above +inf, -0.0 below +0.0).

@@ -13,9 +13,13 @@ torch::Tensor hgemm(const torch::Tensor& A, const torch::Tensor& B, float alpha,
 torch::Tensor hgemm_nt(const torch::Tensor& A, const torch::Tensor& B, float alpha, float beta);
 torch::Tensor gemm(const torch::Tensor& A, const torch::Tensor& B, float alpha, float beta);
 
+// new: causal-mask variant (query i attends to keys 0..i)
+torch::Tensor flash_attention(const torch::Tensor& query, const torch::Tensor& key,
+                              const torch::Tensor& value, bool causal);
 // new: (O, LSE) with LSE fp32 [B, H, S]
 std::tuple<torch::Tensor, torch::Tensor> flash_attention_lse(const torch::Tensor& query,
                                                              const torch::Tensor& key,
-                                                             const torch::Tensor& value);
+                                                             const torch::Tensor& value,
+                                                             bool causal = false);
 
 }  // namespace sion

@@ -36,7 +36,7 @@ def lib() -> C.CDLL:
         L.oracle_sgemm.argtypes = [C.c_int64] * 3 + [C.c_double, P, P, C.c_double, P, P]
         L.oracle_hgemm.argtypes = [C.c_int64] * 3 + [C.c_double, P, P, C.c_int, C.c_double, P, P]
         L.oracle_attention_rows.argtypes = [C.c_int64] * 4 + [P, P, P, C.c_double, P, C.c_int64,
-                                                              P, P]
+                                                              P, P, C.c_int]
         L.oracle_half_to_double.restype = C.c_double
         L.oracle_half_to_double.argtypes = [C.c_uint16]
         L.oracle_double_to_half.restype = C.c_uint16
@@ -94,9 +94,9 @@ def hgemm(A, B, nt: bool, alpha=1.0, beta=0.0, C0=None) -> np.ndarray:
     return out
 
 
-def attention(Q, K, V, scale=0.0, rows=None):
+def attention(Q, K, V, scale=0.0, rows=None, causal=False):
     """Q, K, V fp16 [B, H, S, D]. Returns (O [B,H,R,D] f64, LSE [B,H,R] f64) for the
-    query rows `rows` (all rows when None)."""
+    query rows `rows` (all rows when None); causal: query i sees keys 0..i."""
     Q, K, V = _half_bits(Q), _half_bits(K), _half_bits(V)
     Bn, H, S, D = Q.shape
     r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int64)
@@ -104,7 +104,7 @@ def attention(Q, K, V, scale=0.0, rows=None):
     O = np.empty((Bn, H, R, D), np.float64)
     L = np.empty((Bn, H, R), np.float64)
     lib().oracle_attention_rows(Bn, H, S, D, _p(Q), _p(K), _p(V), float(scale), _p(r),
-                                0 if r is None else len(r), _p(O), _p(L))
+                                0 if r is None else len(r), _p(O), _p(L), 1 if causal else 0)
     return O, L
 
 

@@ -60,12 +60,12 @@ def gemm(A, B, alpha: float = 1.0, beta: float = 0.0):
     return _load_ext().gemm(A, B, alpha, beta)
 
 
-def flash_attention(query, key, value):
-    return _load_ext().flash_attention(query, key, value)
+def flash_attention(query, key, value, causal: bool = False):
+    return _load_ext().flash_attention(query, key, value, causal)
 
 
-def flash_attention_lse(query, key, value):
-    return _load_ext().flash_attention_lse(query, key, value)
+def flash_attention_lse(query, key, value, causal: bool = False):
+    return _load_ext().flash_attention_lse(query, key, value, causal)
 
 
 __all__ = ["sgemm", "hgemm", "hgemm_nt", "gemm", "flash_attention", "flash_attention_lse",

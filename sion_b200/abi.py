@@ -45,6 +45,8 @@ _SIGS = {
                                                                             C.c_void_p]),
     "felix_topk_select": (C.c_int, [C.c_void_p, C.c_void_p] + [C.c_uint32] * 3 +
                           [C.c_int, C.c_void_p]),
+    "felix_flash_attn_fwd_ex": (C.c_int, [C.c_void_p] * 5 + [C.c_uint32] * 4 +
+                                [C.c_float, C.c_int, C.c_void_p]),
     "felix_watchdog_status": (C.c_int, [C.POINTER(C.c_uint), C.c_int]),
     "felix_watchdog_probe": (C.c_int, [C.c_uint32, C.c_void_p]),
     "felix_num_sms": (C.c_int, [C.POINTER(C.c_int)]),
@@ -153,10 +155,14 @@ def sgemm_workspace_size(M, N, K, split_k=0) -> int:
     return n.value
 
 
-def flash_attn_fwd(Q, K, V, O, lse=None, scale=0.0, stream=None):
+def flash_attn_fwd(Q, K, V, O, lse=None, scale=0.0, causal=False, stream=None):
     B, H, S, D = Q.shape
-    check(lib().felix_flash_attn_fwd(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(lse), H, B, S, D,
-                                     float(scale), _stream(stream)))
+    if causal:
+        check(lib().felix_flash_attn_fwd_ex(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(lse), H, B,
+                                            S, D, float(scale), 1, _stream(stream)))
+    else:
+        check(lib().felix_flash_attn_fwd(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(lse), H, B, S,
+                                         D, float(scale), _stream(stream)))
     return O
 
 

@@ -197,17 +197,19 @@ FelixStatus ampere_flash_attn_launch<128, 64>(half* Q, half* K, half* V, half* O
 template <>
 FelixStatus flash_attn_fwd_lse_launch<64, 64>(half* Q, half* K, half* V, half* O, float* lse,
                                               uint32_t heads, uint32_t batch_size,
-                                              uint32_t QKV_seqlen, cudaStream_t stream) {
-  return from_c(felix_flash_attn_fwd(Q, K, V, O, lse, heads, batch_size, QKV_seqlen, 64, 0.0f,
-                                     stream));
+                                              uint32_t QKV_seqlen, cudaStream_t stream,
+                                              bool causal) {
+  return from_c(felix_flash_attn_fwd_ex(Q, K, V, O, lse, heads, batch_size, QKV_seqlen, 64, 0.0f,
+                                        causal ? 1 : 0, stream));
 }
 
 template <>
 FelixStatus flash_attn_fwd_lse_launch<128, 64>(half* Q, half* K, half* V, half* O, float* lse,
                                                uint32_t heads, uint32_t batch_size,
-                                               uint32_t QKV_seqlen, cudaStream_t stream) {
-  return from_c(felix_flash_attn_fwd(Q, K, V, O, lse, heads, batch_size, QKV_seqlen, 128, 0.0f,
-                                     stream));
+                                               uint32_t QKV_seqlen, cudaStream_t stream,
+                                               bool causal) {
+  return from_c(felix_flash_attn_fwd_ex(Q, K, V, O, lse, heads, batch_size, QKV_seqlen, 128,
+                                        0.0f, causal ? 1 : 0, stream));
 }
 
 FelixStatus check_watchdog() {

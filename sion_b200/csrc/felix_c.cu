@@ -308,7 +308,16 @@ int felix_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, f
                          float scale, void* stream) {
   return finish(flash_attn_launch(static_cast<const __half*>(Q), static_cast<const __half*>(K),
                                   static_cast<const __half*>(V), static_cast<__half*>(O), lse,
-                                  heads, batch, seqlen, head_dim, scale,
+                                  heads, batch, seqlen, head_dim, scale, false,
+                                  static_cast<cudaStream_t>(stream)));
+}
+
+int felix_flash_attn_fwd_ex(const void* Q, const void* K, const void* V, void* O, float* lse,
+                            uint32_t heads, uint32_t batch, uint32_t seqlen, uint32_t head_dim,
+                            float scale, int causal, void* stream) {
+  return finish(flash_attn_launch(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                  static_cast<const __half*>(V), static_cast<__half*>(O), lse,
+                                  heads, batch, seqlen, head_dim, scale, causal != 0,
                                   static_cast<cudaStream_t>(stream)));
 }
 

@@ -89,7 +89,7 @@ FelixCode sgemm_noalloc_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, 
 
 FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, __half* O,
                             float* lse, uint32_t heads, uint32_t batch, uint32_t seqlen,
-                            uint32_t head_dim, float scale, cudaStream_t stream);
+                            uint32_t head_dim, float scale, bool causal, cudaStream_t stream);
 
 FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
                              uint32_t slice_size, uint32_t k, bool largest, cudaStream_t stream);

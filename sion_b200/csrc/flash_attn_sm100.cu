@@ -75,6 +75,7 @@ struct Params {
   uint32_t n_kv;     // KV blocks
   uint32_t q_tiles;  // CTA groups per (b, h) along the query axis
   float scale_log2;  // scale * log2(e)
+  uint32_t causal;   // 1: query i attends to keys 0..i only
   unsigned* status;
 };
 
@@ -206,8 +207,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
   const uint32_t grp = blockIdx.x / CG;
   const uint32_t bh = grp / p.q_tiles;
-  const uint32_t q0 = (grp % p.q_tiles) * (2 * kBlockQ * CG) + rank * (2 * kBlockQ);
-  const uint32_t n = p.n_kv;
+  // Causal: the longest query tiles first (they bound the tail of the grid).
+  const uint32_t qt = p.causal ? p.q_tiles - 1 - grp % p.q_tiles : grp % p.q_tiles;
+  const uint32_t grp_q0 = qt * (2 * kBlockQ * CG);
+  const uint32_t q0 = grp_q0 + rank * (2 * kBlockQ);
+  // KV blocks this CTA (group) streams: all, or (causal) up to the block that
+  // holds the group's last query row. Every role of the group uses the same n.
+  const uint32_t n =
+      p.causal ? min(p.n_kv, (grp_q0 + 2 * kBlockQ * CG - 1) / kBlockKV + 1) : p.n_kv;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -430,8 +437,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_ld_wait();
       if (lane == 0 && q == 0) FA_TRACE(t, j, 2);
-      const uint32_t valid = p.S - j * kBlockKV;  // keys left in this block
-      if (valid < uint32_t(kBlockKV)) {
+      // keys of this block the row may see: the ragged tail of the sequence
+      // and, when causal, keys past the row's own position are masked
+      uint32_t valid = p.S - j * kBlockKV;
+      if (p.causal) {
+        const uint32_t qrow = q0 + t * kBlockQ + row;
+        const uint32_t upto = qrow + 1 > j * kBlockKV ? qrow + 1 - j * kBlockKV : 0u;
+        valid = min(valid, upto);
+      }
+      if (__any_sync(0xffffffffu, valid < uint32_t(kBlockKV))) {
 #pragma unroll
         for (int i = 0; i < kBlockKV; ++i)
           if (uint32_t(i) >= valid) s[i] = -INFINITY;
@@ -614,7 +628,7 @@ cudaError_t launch(uint64_t groups, const CUtensorMap& tq, const CUtensorMap& tk
 
 FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, __half* O,
                             float* lse, uint32_t heads, uint32_t batch, uint32_t seqlen,
-                            uint32_t head_dim, float scale, cudaStream_t stream) {
+                            uint32_t head_dim, float scale, bool causal, cudaStream_t stream) {
   if (head_dim != 64 && head_dim != 128)
     return api_error("flash_attn: head_dim must be 64 or 128");
   if (heads == 0 || batch == 0 || seqlen == 0) return FelixCode{FELIX_SUCCESS, cudaSuccess};
@@ -640,6 +654,7 @@ FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, _
   p.lse = lse;
   p.S = seqlen;
   p.n_kv = (seqlen + kBlockKV - 1) / kBlockKV;
+  p.causal = causal ? 1u : 0u;
   p.q_tiles = (seqlen + 2 * kBlockQ * cg - 1) / (2 * kBlockQ * cg);
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf(float(head_dim));
   p.scale_log2 = sc * 1.4426950408889634f;

@@ -8,7 +8,8 @@
 //   * C is zero-filled when beta != 0 (the reference reads uninitialised
 //     torch::empty memory there, sgemm.cpp:19,27);
 //   * flash_attention accepts any seqlen (the reference requires seqlen % 64);
-//   * flash_attention_lse also returns the fp32 log-sum-exp;
+//   * flash_attention_lse also returns the fp32 log-sum-exp; both take an
+//     optional causal mask;
 //   * the Python functions take named arguments (python/binding.cpp:6-11 has none).
 #include <sion/sion.hpp>
 
@@ -109,7 +110,8 @@ void check_attn_inputs(const torch::Tensor& Q, const torch::Tensor& K, const tor
 
 std::tuple<torch::Tensor, torch::Tensor> attn_impl(const torch::Tensor& query,
                                                    const torch::Tensor& key,
-                                                   const torch::Tensor& value, bool want_lse) {
+                                                   const torch::Tensor& value, bool want_lse,
+                                                   bool causal) {
   check_attn_inputs(query, key, value);
   const c10::cuda::CUDAGuard guard(query.device());
   auto Q = query.contiguous(), K = key.contiguous(), V = value.contiguous();
@@ -126,15 +128,18 @@ std::tuple<torch::Tensor, torch::Tensor> attn_impl(const torch::Tensor& query,
   felix::FelixStatus status;
   switch (D) {
     case 64:
-      status = want_lse ? felix::flash_attn_fwd_lse_launch<64, 64>(q, k, v, o, l, uint32_t(H),
-                                                                   uint32_t(B), uint32_t(S), stream)
+      status = (want_lse || causal)
+                   ? felix::flash_attn_fwd_lse_launch<64, 64>(q, k, v, o, l, uint32_t(H),
+                                                              uint32_t(B), uint32_t(S), stream,
+                                                              causal)
                         : felix::ampere_flash_attn_launch<64, 64>(q, k, v, o, uint32_t(H),
                                                                   uint32_t(B), uint32_t(S), stream);
       break;
     case 128:
-      status = want_lse
+      status = (want_lse || causal)
                    ? felix::flash_attn_fwd_lse_launch<128, 64>(q, k, v, o, l, uint32_t(H),
-                                                               uint32_t(B), uint32_t(S), stream)
+                                                               uint32_t(B), uint32_t(S), stream,
+                                                               causal)
                    : felix::ampere_flash_attn_launch<128, 64>(q, k, v, o, uint32_t(H),
                                                               uint32_t(B), uint32_t(S), stream);
       break;
@@ -147,13 +152,19 @@ std::tuple<torch::Tensor, torch::Tensor> attn_impl(const torch::Tensor& query,
 
 torch::Tensor flash_attention(const torch::Tensor& query, const torch::Tensor& key,
                               const torch::Tensor& value) {
-  return std::get<0>(attn_impl(query, key, value, false));
+  return std::get<0>(attn_impl(query, key, value, false, false));
+}
+
+torch::Tensor flash_attention(const torch::Tensor& query, const torch::Tensor& key,
+                              const torch::Tensor& value, bool causal) {
+  return std::get<0>(attn_impl(query, key, value, false, causal));
 }
 
 std::tuple<torch::Tensor, torch::Tensor> flash_attention_lse(const torch::Tensor& query,
                                                              const torch::Tensor& key,
-                                                             const torch::Tensor& value) {
-  return attn_impl(query, key, value, true);
+                                                             const torch::Tensor& value,
+                                                             bool causal) {
+  return attn_impl(query, key, value, true, causal);
 }
 
 }  // namespace sion
@@ -169,9 +180,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("alpha") = 1.0f, py::arg("beta") = 0.0f);
   m.def("gemm", &sion::gemm, "GEMM dispatching on dtype (fp32 -> sgemm, fp16 -> hgemm)",
         py::arg("A"), py::arg("B"), py::arg("alpha") = 1.0f, py::arg("beta") = 0.0f);
-  m.def("flash_attention", &sion::flash_attention, "flash attention forward, no mask",
-        py::arg("query"), py::arg("key"), py::arg("value"));
+  m.def("flash_attention",
+        py::overload_cast<const torch::Tensor&, const torch::Tensor&, const torch::Tensor&, bool>(
+            &sion::flash_attention),
+        "flash attention forward (causal=True: query i sees keys 0..i)", py::arg("query"),
+        py::arg("key"), py::arg("value"), py::arg("causal") = false);
   m.def("flash_attention_lse", &sion::flash_attention_lse,
         "flash attention forward returning (O, fp32 LSE)", py::arg("query"), py::arg("key"),
-        py::arg("value"));
+        py::arg("value"), py::arg("causal") = false);
 }

@@ -42,11 +42,14 @@ class AttnConfig:
     S: int
     D: int
     seed: int
+    causal: bool = False
 
     @property
     def flops(self) -> float:
-        # reference convention (bench/flash_attention/fa_bench.cpp:93-95): 4*B*H*S^2*D
-        return 4.0 * self.B * self.H * self.S * self.S * self.D
+        # reference convention (bench/flash_attention/fa_bench.cpp:93-95): 4*B*H*S^2*D;
+        # a causal mask halves the work actually required
+        f = 4.0 * self.B * self.H * self.S * self.S * self.D
+        return f / 2 if self.causal else f
 
     @property
     def io_bytes(self) -> int:
@@ -59,10 +62,13 @@ HGEMM_4096 = GemmConfig("hgemm_f16_4096_nt", 4096, 4096, 4096, "f16", "nk", "uni
 HGEMM_SKINNY = GemmConfig("hgemm_f16_128x8192x16384_nt", 128, 8192, 16384, "f16", "nk",
                           "normal", 0.02, 2)
 FA_8192 = AttnConfig("flash_attn_fwd_f16_4x32x8192x128", 4, 32, 8192, 128, 3)
+FA_8192_CAUSAL = AttnConfig("flash_attn_fwd_causal_f16_4x32x8192x128", 4, 32, 8192, 128, 3,
+                            causal=True)
 HGEMM_16384 = GemmConfig("hgemm_f16_16384_nt", 16384, 16384, 16384, "f16", "nk", "uniform", 1.0,
                          4)
 
-CONFIGS = {c.name: c for c in (SGEMM_1024, HGEMM_4096, HGEMM_SKINNY, FA_8192, HGEMM_16384)}
+CONFIGS = {c.name: c for c in (SGEMM_1024, HGEMM_4096, HGEMM_SKINNY, FA_8192, HGEMM_16384,
+                               FA_8192_CAUSAL)}
 
 
 def _draw(gen: torch.Generator, shape, dist: str, std: float) -> torch.Tensor:

@@ -42,14 +42,17 @@ def hgemm_case(name, M, N, K, nt, alpha, beta, seed):
                         C0=C0.numpy(), nt=nt, alpha=alpha, beta=beta, ref=ref.numpy())
 
 
-def attn_case(name, Bn, H, S, D, seed):
+def attn_case(name, Bn, H, S, D, seed, causal=False):
     g = torch.Generator().manual_seed(seed)
     Q = torch.randn(Bn, H, S, D, generator=g).half()
     K = torch.randn(Bn, H, S, D, generator=g).half()
     V = torch.randn(Bn, H, S, D, generator=g).half()
     q, k, v = Q.double(), K.double(), V.double()
-    O = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=None, dropout_p=0.0)
+    O = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=None, dropout_p=0.0,
+                                                         is_causal=causal)
     scores = (q @ k.transpose(-1, -2)) / (D ** 0.5)
+    if causal:
+        scores = scores.masked_fill(torch.ones(S, S, dtype=torch.bool).triu(1), float("-inf"))
     lse = torch.logsumexp(scores, dim=-1)
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"), Q=Q.numpy(), K=K.numpy(),
                         V=V.numpy(), O=O.numpy(), lse=lse.numpy())
@@ -62,6 +65,7 @@ def main():
     hgemm_case("hgemm_nn_200x136x72", 200, 136, 72, False, 0.5, 0.25, 13)
     attn_case("attn_1x2x80x64", 1, 2, 80, 64, 14)
     attn_case("attn_1x1x130x128", 1, 1, 130, 128, 15)
+    attn_case("attn_causal_1x2x150x64", 1, 2, 150, 64, 16, causal=True)
 
 
 if __name__ == "__main__":

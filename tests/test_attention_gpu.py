@@ -100,3 +100,40 @@ def test_attention_rejects_bad_head_dim(felix):
     with pytest.raises(felix.FelixError) as e:
         felix.flash_attn_fwd(Q, Q, Q, torch.empty_like(Q))
     assert e.value.code == felix.API_ERROR
+
+
+def _run_causal(felix, B, H, S, D, seed, rows=None):
+    Q, K, V = _inputs(B, H, S, D, seed)
+    O = torch.empty(B, H, S, D, dtype=torch.half, device="cuda")
+    L = torch.empty(B, H, S, device="cuda")
+    felix.flash_attn_fwd(Q.cuda(), K.cuda(), V.cuda(), O, L, causal=True)
+    torch.cuda.synchronize()
+    Oref, Lref = oracle.attention(Q.numpy(), K.numpy(), V.numpy(), rows=rows, causal=True)
+    o = O.cpu().numpy().astype(np.float64)
+    l = L.cpu().numpy().astype(np.float64)
+    if rows is not None:
+        o, l = o[:, :, rows], l[:, :, rows]
+    return Oref, Lref, o, l
+
+
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("S", [1, 100, 128, 129, 256, 300, 512, 777, 1024])
+def test_attention_causal(felix, S, D):
+    _check(*_run_causal(felix, 2, 2, S, D, seed=S + D), ctx=f"causal S={S} D={D}")
+
+
+def test_attention_causal_long_sampled(felix):
+    rows = np.r_[0, 1, 127, 128, 255, 256, 4095, 8000, 8191]
+    _check(*_run_causal(felix, 1, 2, 8192, 128, seed=4, rows=rows), ctx="causal 8192")
+
+
+def test_sion_module_causal_matches_c_abi(felix):
+    import sion_b200 as sion
+    Q, K, V = [t.cuda() for t in _inputs(1, 3, 333, 128, 8)]
+    O1, L1 = sion.flash_attention_lse(Q, K, V, causal=True)
+    O2 = torch.empty_like(Q)
+    L2 = torch.empty(1, 3, 333, device="cuda")
+    felix.flash_attn_fwd(Q, K, V, O2, L2, causal=True)
+    torch.cuda.synchronize()
+    assert torch.equal(O1, O2) and torch.equal(L1, L2)
+    assert torch.equal(sion.flash_attention(Q, K, V, causal=True), O1)

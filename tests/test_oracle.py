@@ -38,6 +38,13 @@ def test_attention_oracle_matches_golden(name):
     np.testing.assert_allclose(L, g["lse"], rtol=1e-12, atol=1e-12)
 
 
+def test_attention_causal_oracle_matches_golden():
+    g = _load("attn_causal_1x2x150x64")
+    O, L = oracle.attention(g["Q"], g["K"], g["V"], causal=True)
+    np.testing.assert_allclose(O, g["O"], rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(L, g["lse"], rtol=1e-12, atol=1e-12)
+
+
 def test_attention_oracle_row_subset():
     g = _load("attn_1x1x130x128")
     rows = np.array([0, 5, 129], np.int64)
@@ -64,7 +71,7 @@ def test_half_conversions_exhaustive():
 
 
 def test_golden_fixtures_present():
-    assert len(glob.glob(os.path.join(GOLD, "*.npz"))) == 6
+    assert len(glob.glob(os.path.join(GOLD, "*.npz"))) == 7
 
 
 def test_topk_oracle_matches_numpy_ordering():
