@@ -146,6 +146,24 @@ int felix_flash_attn_fwd_ex(const void* Q, const void* K, const void* V, void* O
                             float scale, int causal, void* stream);
 
 /*
+ * Flash-attention backward (no reference counterpart; the reference has a
+ * forward kernel only): given Q, K, V, the forward output O, its gradient dO
+ * (all fp16 [batch, heads, seqlen, head_dim]) and the forward's fp32
+ * natural-log LSE [batch, heads, seqlen], writes dQ, dK, dV (fp16, same
+ * shape). scale <= 0 selects 1/sqrt(head_dim); causal as in
+ * felix_flash_attn_fwd_ex. workspace: NULL = library-owned scratch, else at
+ * least felix_flash_attn_bwd_workspace_size() bytes (fp32 dQ accumulator and
+ * the per-row dO.O sums; its contents need no initialisation).
+ */
+int felix_flash_attn_bwd(const void* Q, const void* K, const void* V, const void* O,
+                         const void* dO, const float* lse, void* dQ, void* dK, void* dV,
+                         uint32_t heads, uint32_t batch, uint32_t seqlen, uint32_t head_dim,
+                         float scale, int causal, void* workspace, size_t workspace_bytes,
+                         void* stream);
+int felix_flash_attn_bwd_workspace_size(uint32_t heads, uint32_t batch, uint32_t seqlen,
+                                        uint32_t head_dim, size_t* bytes);
+
+/*
  * k-th value per slice (radix select): out[s] = the k-th largest (largest != 0)
  * or k-th smallest value of data[s * slice_size, (s + 1) * slice_size), fp32,
  * returned bit-exactly (order: NaN above +inf, -0.0 below +0.0).

@@ -43,6 +43,8 @@ def lib() -> C.CDLL:
         L.oracle_double_to_half.argtypes = [C.c_double]
         L.oracle_half_to_double_array.argtypes = [P, P, C.c_int64]
         L.oracle_double_to_half_array.argtypes = [P, P, C.c_int64]
+        L.oracle_attention_bwd.argtypes = [C.c_int64] * 4 + [P, P, P, P, C.c_double, C.c_int,
+                                                             P, P, P]
         L.oracle_topk.argtypes = [P, P, C.c_int64, C.c_int64, C.c_int64, C.c_int]
         L.oracle_set_threads.argtypes = [C.c_int]
         L.oracle_get_threads.restype = C.c_int
@@ -106,6 +108,16 @@ def attention(Q, K, V, scale=0.0, rows=None, causal=False):
     lib().oracle_attention_rows(Bn, H, S, D, _p(Q), _p(K), _p(V), float(scale), _p(r),
                                 0 if r is None else len(r), _p(O), _p(L), 1 if causal else 0)
     return O, L
+
+
+def attention_bwd(Q, K, V, dO, scale=0.0, causal=False):
+    """fp16 [B, H, S, D] inputs -> (dQ, dK, dV) float64 of softmax(Q K^T scale) V."""
+    Q, K, V, dO = _half_bits(Q), _half_bits(K), _half_bits(V), _half_bits(dO)
+    Bn, H, S, D = Q.shape
+    dQ, dK, dV = (np.empty((Bn, H, S, D), np.float64) for _ in range(3))
+    lib().oracle_attention_bwd(Bn, H, S, D, _p(Q), _p(K), _p(V), _p(dO), float(scale),
+                               1 if causal else 0, _p(dQ), _p(dK), _p(dV))
+    return dQ, dK, dV
 
 
 def topk(data: np.ndarray, k: int, largest: bool = True) -> np.ndarray:

@@ -43,6 +43,9 @@ _SIGS = {
                                                                  C.POINTER(C.c_size_t)]),
     "felix_flash_attn_fwd": (C.c_int, [C.c_void_p] * 5 + [C.c_uint32] * 4 + [C.c_float,
                                                                             C.c_void_p]),
+    "felix_flash_attn_bwd": (C.c_int, [C.c_void_p] * 9 + [C.c_uint32] * 4 +
+                             [C.c_float, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "felix_flash_attn_bwd_workspace_size": (C.c_int, [C.c_uint32] * 4 + [C.POINTER(C.c_size_t)]),
     "felix_topk_select": (C.c_int, [C.c_void_p, C.c_void_p] + [C.c_uint32] * 3 +
                           [C.c_int, C.c_void_p]),
     "felix_flash_attn_fwd_ex": (C.c_int, [C.c_void_p] * 5 + [C.c_uint32] * 4 +
@@ -164,6 +167,17 @@ def flash_attn_fwd(Q, K, V, O, lse=None, scale=0.0, causal=False, stream=None):
         check(lib().felix_flash_attn_fwd(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(lse), H, B, S,
                                          D, float(scale), _stream(stream)))
     return O
+
+
+def flash_attn_bwd(Q, K, V, O, dO, lse, dQ, dK, dV, scale=0.0, causal=False, workspace=None,
+                   stream=None):
+    B, H, S, D = Q.shape
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().felix_flash_attn_bwd(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(dO), _ptr(lse),
+                                     _ptr(dQ), _ptr(dK), _ptr(dV), H, B, S, D, float(scale),
+                                     1 if causal else 0, _ptr(workspace), ws_bytes,
+                                     _stream(stream)))
+    return dQ, dK, dV
 
 
 def topk_select(data, out, k, largest=True, stream=None):

@@ -25,7 +25,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
 CU_SOURCES = ["felix_c.cu", "sgemm_sm100.cu", "hgemm_sm100.cu", "flash_attn_sm100.cu",
-              "topk_sm100.cu"]
+              "topk_sm100.cu", "flash_attn_bwd_sm100.cu"]
 CPP_SOURCES = ["felix_api.cpp"]
 HEADERS = ["sm100_ptx.cuh", "felix_internal.h"]
 

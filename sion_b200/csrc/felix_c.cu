@@ -321,6 +321,25 @@ int felix_flash_attn_fwd_ex(const void* Q, const void* K, const void* V, void* O
                                   static_cast<cudaStream_t>(stream)));
 }
 
+int felix_flash_attn_bwd(const void* Q, const void* K, const void* V, const void* O,
+                         const void* dO, const float* lse, void* dQ, void* dK, void* dV,
+                         uint32_t heads, uint32_t batch, uint32_t seqlen, uint32_t head_dim,
+                         float scale, int causal, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  return finish(flash_attn_bwd_launch(
+      static_cast<const __half*>(Q), static_cast<const __half*>(K), static_cast<const __half*>(V),
+      static_cast<const __half*>(O), static_cast<const __half*>(dO), lse,
+      static_cast<__half*>(dQ), static_cast<__half*>(dK), static_cast<__half*>(dV), heads, batch,
+      seqlen, head_dim, scale, causal != 0, workspace, workspace_bytes,
+      static_cast<cudaStream_t>(stream)));
+}
+
+int felix_flash_attn_bwd_workspace_size(uint32_t heads, uint32_t batch, uint32_t seqlen,
+                                        uint32_t head_dim, size_t* bytes) {
+  if (bytes) *bytes = flash_attn_bwd_workspace_bytes(heads, batch, seqlen, head_dim);
+  return FELIX_SUCCESS;
+}
+
 int felix_topk_select(const float* data, float* out, uint32_t num_slices, uint32_t slice_size,
                       uint32_t k, int largest, void* stream) {
   return finish(topk_select_launch(data, out, num_slices, slice_size, k, largest != 0,

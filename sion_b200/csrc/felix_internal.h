@@ -91,6 +91,14 @@ FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, _
                             float* lse, uint32_t heads, uint32_t batch, uint32_t seqlen,
                             uint32_t head_dim, float scale, bool causal, cudaStream_t stream);
 
+size_t flash_attn_bwd_workspace_bytes(uint32_t heads, uint32_t batch, uint32_t seqlen,
+                                      uint32_t head_dim);
+FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* V,
+                                const __half* O, const __half* dO, const float* lse, __half* dQ,
+                                __half* dK, __half* dV, uint32_t heads, uint32_t batch,
+                                uint32_t seqlen, uint32_t head_dim, float scale, bool causal,
+                                void* workspace, size_t ws_bytes, cudaStream_t stream);
+
 FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
                              uint32_t slice_size, uint32_t k, bool largest, cudaStream_t stream);
 

@@ -1,0 +1,469 @@
+// Flash-attention backward for sm_100a, fp16 in/out, fp32 accumulation:
+//   given Q, K, V, O, dO and the forward's natural-log LSE, computes
+//   dQ, dK, dV of O = softmax(Q K^T * scale) V (optionally causal).
+// No reference counterpart (the reference has a forward kernel only); the
+// backward of its operator is listed as the next attention feature.
+//
+// Math (per (b, h)): P = exp(scale * Q K^T - LSE), dV = P^T dO,
+// dP = dO V^T, Delta = rowsum(dO * O), dS = P * (dP - Delta),
+// dK = scale * dS^T Q, dQ = scale * dS K.
+//
+// Kernel layout: one CTA per (b, h) and 128-key block j, looping over the
+// 128-query blocks i (from the diagonal block when causal). Everything is
+// computed in the "transposed" orientation so that TMEM lanes are keys:
+//   S^T  = K_j Q_i^T        (SS MMA)              -> TMEM cols [0, 128)
+//   dP^T = V_j dO_i^T       (SS MMA)              -> TMEM cols [128, 256)
+//   P^T, dS^T (fp16) overwrite the first halves of those regions (TMEM A
+//   operands); dS is also written to shared memory as an MN-major tile;
+//   dV_j += P^T dO_i        (TS MMA)              -> TMEM cols [256, 256 + D)
+//   dK_j += dS^T Q_i        (TS MMA)              -> TMEM cols [384, 384 + D)
+//   dQ_i  = dS K_j          (SS MMA, A MN-major)  -> TMEM cols [0, D)
+// dQ_i is reduced into an fp32 buffer with 16-byte vector reductions; a small
+// kernel scales and converts it to fp16 at the end. MMAs of a CTA execute in
+// issue order, so dQ_i may overwrite the P^T columns right behind the dV MMA
+// that reads them. Warps: 0 TMA loader, 1 MMA issuer, 4-7 one warpgroup of
+// element-wise work (one key row per thread).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "felix_internal.h"
+#include "sm100_ptx.cuh"
+
+namespace felix_sm100 {
+namespace attn_bwd {
+
+constexpr int kBlk = 128;  // keys per CTA, queries per loop step
+constexpr int kThreads = 256;
+
+template <int D>
+struct Cfg {
+  static constexpr int kChunks = D / 64;
+  static constexpr int kTile = kBlk * D * 2;  // one 128 x D fp16 tile
+  static constexpr int kKOff = 0;
+  static constexpr int kVOff = kKOff + kTile;
+  static constexpr int kQOff = kVOff + kTile;
+  static constexpr int kDOOff = kQOff + kTile;
+  static constexpr int kDSOff = kDOOff + kTile;       // dS: 128 queries x 128 keys fp16
+  // lse2[2][128], delta[2][128]: double-buffered by step parity
+  static constexpr int kVecOff = kDSOff + kBlk * kBlk * 2;
+  static constexpr int kBarOff = kVecOff + 4 * kBlk * 4;
+  static constexpr int kSmemBytes = kBarOff + 256 + 1024;
+};
+
+struct Params {
+  const float* lse;     // [BH, S] natural log (forward output)
+  const float* delta;   // [BH, S] rowsum(dO * O)
+  float* dq_acc;        // [BH, S, D] fp32, zeroed
+  __half* dK;
+  __half* dV;
+  uint32_t S, n_blk;
+  float scale, scale_log2;
+  uint32_t causal;
+  unsigned* status;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int ROWS>
+__device__ __forceinline__ uint64_t kmajor(uint32_t tile, int k) {
+  return make_sdesc_sw128(tile + (uint32_t(k) >> 2) * (ROWS * 128) + (uint32_t(k) & 3u) * 32, 16,
+                          1024);
+}
+// MN-major operand made of 64-column chunks of 128 rows (16 KB each), K step k.
+__device__ __forceinline__ uint64_t mnmajor(uint32_t tile, int k) {
+  return make_sdesc_sw128(tile + uint32_t(k) * 2048, kBlk * 128, 1024);
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                          const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV,
+                          const __grid_constant__ CUtensorMap tmDO, const Params p) {
+  using C_ = Cfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  float* s_vec = reinterpret_cast<float*>(smem + C_::kVecOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
+  uint64_t* kv_full = bars;        // K_j, V_j landed
+  uint64_t* qdo_full = bars + 1;   // Q_i, dO_i landed
+  uint64_t* qdo_empty = bars + 2;  // MMAs of step i done with Q_i, dO_i, dS
+  uint64_t* st_full = bars + 3;    // S^T, dP^T in TMEM
+  uint64_t* p_ready = bars + 4;    // P^T, dS^T in TMEM, dS in smem (4 warp arrivals)
+  uint64_t* dq_full = bars + 5;    // dQ_i in TMEM
+  uint64_t* dq_free = bars + 6;    // dQ_i read out (4 warp arrivals)
+  uint64_t* done = bars + 7;       // every MMA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t bh = blockIdx.x / p.n_blk;
+  const uint32_t j = blockIdx.x % p.n_blk;  // key block
+  const uint32_t i0 = p.causal ? j : 0;     // first query block
+  const uint32_t n_i = p.n_blk - i0;
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 8; ++b) mbar_init(&bars[b], (b == 4 || b == 6) ? 4 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- loader
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * C_::kTile);
+#pragma unroll
+      for (int c = 0; c < C_::kChunks; ++c) {
+        tma_load_3d(smem + C_::kKOff + c * (kBlk * 128), &tmK, kv_full, 64 * c, int(j * kBlk),
+                    int(bh));
+        tma_load_3d(smem + C_::kVOff + c * (kBlk * 128), &tmV, kv_full, 64 * c, int(j * kBlk),
+                    int(bh));
+      }
+      uint32_t filled = 0;
+      for (uint32_t s = 0; s < n_i; ++s) {
+        const uint32_t i = i0 + s;
+        if (!mbar_wait(qdo_empty, (s & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
+        mbar_arrive_expect_tx(qdo_full, 2 * C_::kTile);
+#pragma unroll
+        for (int c = 0; c < C_::kChunks; ++c) {
+          tma_load_3d(smem + C_::kQOff + c * (kBlk * 128), &tmQ, qdo_full, 64 * c, int(i * kBlk),
+                      int(bh));
+          tma_load_3d(smem + C_::kDOOff + c * (kBlk * 128), &tmDO, qdo_full, 64 * c,
+                      int(i * kBlk), int(bh));
+        }
+        ++filled;
+      }
+      int dummy = 0;
+      mbar_wait(kv_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
+      if (filled) mbar_wait(qdo_full, (filled - 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_st = make_idesc_f16_f32(kBlk, kBlk, false, false);  // S^T, dP^T
+      const uint32_t id_acc = make_idesc_f16_f32(kBlk, D, false, true);     // dV, dK
+      const uint32_t id_dq = make_idesc_f16_f32(kBlk, D, true, true);       // dQ
+      const uint32_t sK = smem_u32(smem + C_::kKOff), sV = smem_u32(smem + C_::kVOff);
+      const uint32_t sQ = smem_u32(smem + C_::kQOff), sDO = smem_u32(smem + C_::kDOOff);
+      const uint32_t sDS = smem_u32(smem + C_::kDSOff);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kWdAttnMma);
+      for (uint32_t s = 0; ok && s < n_i; ++s) {
+        const uint32_t ph = s & 1u;
+        if (!(ok = mbar_wait(qdo_full, ph, abort_flag, p.status, kWdAttnMma))) break;
+        // the dQ of the previous step must have been read out of cols [0, D)
+        if (s > 0 && !(ok = mbar_wait(dq_free, ph ^ 1u, abort_flag, p.status, kWdAttnMma))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16_ss(tmem + kColS, kmajor<kBlk>(sK, k), kmajor<kBlk>(sQ, k), id_st,
+                      k > 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16_ss(tmem + kColDP, kmajor<kBlk>(sV, k), kmajor<kBlk>(sDO, k), id_st,
+                      k > 0 ? 1u : 0u);
+        umma_commit(st_full);
+        if (!(ok = mbar_wait(p_ready, ph, abort_flag, p.status, kWdAttnMma))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kBlk / 16; ++k)
+          umma_f16_ts(tmem + kColDV, tmem + kColS + k * 8, mnmajor(sDO, k), id_acc,
+                      (s > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < kBlk / 16; ++k)
+          umma_f16_ts(tmem + kColDK, tmem + kColDP + k * 8, mnmajor(sQ, k), id_acc,
+                      (s > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < kBlk / 16; ++k)
+          umma_f16_ss(tmem + kColS, mnmajor(sDS, k), mnmajor(sK, k), id_dq, k > 0 ? 1u : 0u);
+        umma_commit(qdo_empty);
+        umma_commit(dq_full);
+      }
+      umma_commit(done);
+      int dummy = 0;
+      mbar_wait(done, 0, &dummy, p.status, kWdDrain, 100000000ull);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- element-wise
+    const uint32_t q4 = warp & 3u;
+    const uint32_t r = q4 * 32 + lane;  // key row of this CTA (TMEM lane)
+    const uint32_t key = j * kBlk + r;
+    const uint32_t la = (q4 * 32u) << 16;
+    const uint32_t tid = threadIdx.x - 128;
+    uint8_t* sDS = smem + C_::kDSOff;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (uint32_t s = 0; ok && s < n_i; ++s) {
+      const uint32_t ph = s & 1u;
+      const uint32_t i = i0 + s;
+      // per-query vectors of this step (queries past S: P = 0 through lse = +inf);
+      // double-buffered by step parity, so slower threads may still read the
+      // previous step's copy while this one is written
+      float* s_lse2 = s_vec + ph * (2 * kBlk);
+      float* s_delta = s_lse2 + kBlk;
+      {
+        const uint32_t q = i * kBlk + tid;
+        s_lse2[tid] = q < p.S ? __ldg(p.lse + size_t(bh) * p.S + q) * 1.4426950408889634f
+                              : INFINITY;
+        s_delta[tid] = q < p.S ? __ldg(p.delta + size_t(bh) * p.S + q) : 0.f;
+      }
+      named_barrier_sync(1, 128);
+      if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, kWdAttnSoftmax))) break;
+      tc_fence_after();
+      const bool key_ok = key < p.S;
+#pragma unroll 1
+      for (int c = 0; c < kBlk; c += 32) {
+        uint32_t sr[32], dr[32];
+        tmem_ld_32x32b_x32(tmem + la + kColS + c, sr);
+        tmem_ld_32x32b_x32(tmem + la + kColDP + c, dr);
+        tmem_ld_wait();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t qi = uint32_t(c + e + h);
+            const uint32_t q = i * kBlk + qi;
+            float pr = ex2(fmaf(__uint_as_float(sr[e + h]), sl2, -s_lse2[qi]));
+            if (!key_ok || (p.causal && q < key)) pr = 0.f;
+            pv[h] = pr;
+            dv[h] = pr * (__uint_as_float(dr[e + h]) - s_delta[qi]);
+          }
+          pk[e / 2] = pack_half2(pv[0], pv[1]);
+          dk[e / 2] = pack_half2(dv[0], dv[1]);
+        }
+        tmem_st_32x32b_x16(tmem + la + kColS + c / 2, pk);
+        tmem_st_32x32b_x16(tmem + la + kColDP + c / 2, dk);
+        // dS (queries x keys) as an MN-major A tile: query chunk c / 64, row = key r,
+        // 16-byte units swizzled with the row (128-byte swizzle)
+        uint8_t* row = sDS + (c / 64) * (kBlk * 128) + r * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t unit = uint32_t((c % 64) / 8 + u);
+          *reinterpret_cast<uint4*>(row + ((unit ^ (r & 7u)) * 16)) =
+              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+        }
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      // dQ_i rows (lane = query) -> fp32 accumulation buffer
+      if (!(ok = mbar_wait(dq_full, ph, abort_flag, p.status, kWdAttnSoftmax))) break;
+      tc_fence_after();
+      const uint32_t q = i * kBlk + r;
+      float* dst = p.dq_acc + (size_t(bh) * p.S + q) * D;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + la + kColS + c, v);
+        tmem_ld_wait();
+        if (q < p.S) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            red_add_v4(dst + c + e, __uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                       __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+    // dK_j, dV_j (lane = key) -> fp16
+    if (ok && mbar_wait(done, 0, abort_flag, p.status, kWdAttnSoftmax)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t col = which ? kColDK : kColDV;
+        const float mul = which ? p.scale : 1.f;
+        __half* out = (which ? p.dK : p.dV) + (size_t(bh) * p.S + key) * D;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + la + col + c, v);
+          tmem_ld_wait();
+          if (key < p.S) {
+            uint4 o4[4];
+            uint32_t* o = reinterpret_cast<uint32_t*>(o4);
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              o[e] = pack_half2(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(out + c)[e] = o4[e];
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Delta[row] = sum_d dO[row, d] * O[row, d] (fp32), one warp per row.
+__global__ void delta_kernel(const __half* __restrict__ O, const __half* __restrict__ dO,
+                             float* __restrict__ delta, uint64_t rows, uint32_t D) {
+  const uint64_t row = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+  const uint32_t lane = threadIdx.x % 32;
+  if (row >= rows) return;
+  const __half2* o = reinterpret_cast<const __half2*>(O + row * D);
+  const __half2* g = reinterpret_cast<const __half2*>(dO + row * D);
+  float acc = 0.f;
+  for (uint32_t k = lane; k < D / 2; k += 32) {
+    const float2 a = __half22float2(o[k]), b = __half22float2(g[k]);
+    acc = fmaf(a.x, b.x, fmaf(a.y, b.y, acc));
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) delta[row] = acc;
+}
+
+__global__ void dq_convert_kernel(const float* __restrict__ acc, __half* __restrict__ dQ, size_t n,
+                                  float scale) {
+  for (size_t i = (blockIdx.x * size_t(blockDim.x) + threadIdx.x) * 4; i < n;
+       i += size_t(gridDim.x) * blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(acc + i);
+    reinterpret_cast<__half2*>(dQ + i)[0] = __floats2half2_rn(v.x * scale, v.y * scale);
+    reinterpret_cast<__half2*>(dQ + i)[1] = __floats2half2_rn(v.z * scale, v.w * scale);
+  }
+}
+
+}  // namespace attn_bwd
+}  // namespace felix_sm100
+
+namespace felix_impl {
+
+using namespace felix_sm100::attn_bwd;
+
+namespace {
+template <int D>
+int configure_bwd(int device) {
+  static int done[64] = {0};
+  if (device < 0 || device >= 64) return -1;
+  if (!done[device]) {
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_bwd_kernel<D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<D>::kSmemBytes);
+    if (e != cudaSuccess) return int(e);
+    done[device] = 1;
+  }
+  return 0;
+}
+}  // namespace
+
+size_t flash_attn_bwd_workspace_bytes(uint32_t heads, uint32_t batch, uint32_t seqlen,
+                                      uint32_t head_dim) {
+  const size_t rows = size_t(heads) * batch * seqlen;
+  return kWsCounterBytes + rows * 4 + 16 + rows * head_dim * 4;
+}
+
+FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* V,
+                                const __half* O, const __half* dO, const float* lse, __half* dQ,
+                                __half* dK, __half* dV, uint32_t heads, uint32_t batch,
+                                uint32_t seqlen, uint32_t head_dim, float scale, bool causal,
+                                void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128)
+    return api_error("flash_attn_bwd: head_dim must be 64 or 128");
+  if (heads == 0 || batch == 0 || seqlen == 0) return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  if (!Q || !K || !V || !O || !dO || !lse || !dQ || !dK || !dV)
+    return api_error("flash_attn_bwd: null pointer");
+  if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+       reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(O) |
+       reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(dQ) |
+       reinterpret_cast<uintptr_t>(dK) | reinterpret_cast<uintptr_t>(dV)) & 15u)
+    return api_error("flash_attn_bwd: tensors must be 16-byte aligned");
+  const uint64_t bh = uint64_t(heads) * batch;
+  if (bh > (1u << 31) || seqlen > (1u << 30)) return api_error("flash_attn_bwd: too large");
+  DeviceInfo* dev = current_device_info();
+  if (!dev) return launch_error(cudaGetLastError(), "flash_attn_bwd: no CUDA device");
+
+  const size_t rows = size_t(bh) * seqlen;
+  const size_t need = flash_attn_bwd_workspace_bytes(heads, batch, seqlen, head_dim);
+  if (!workspace) {
+    workspace = library_workspace(dev, stream, need);
+    if (!workspace) return launch_error(cudaErrorMemoryAllocation, "flash_attn_bwd: workspace");
+  } else if (ws_bytes < need) {
+    return api_error("flash_attn_bwd: workspace too small");
+  }
+  float* delta = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
+  float* dq_acc = delta + rows;  // 16-byte aligned: rows * 4 bytes after a 16 KiB block
+  if ((reinterpret_cast<uintptr_t>(dq_acc) & 15u) != 0) {
+    dq_acc = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(dq_acc) + 15) & ~uintptr_t(15));
+  }
+
+  CUtensorMap tq, tk, tv, tdo;
+  auto enc = [&](CUtensorMap* m, const void* base) {
+    return encode_tmap_3d_f16(m, base, head_dim, seqlen, bh, uint64_t(head_dim) * 2,
+                              uint64_t(seqlen) * head_dim * 2, 64, kBlk, 1);
+  };
+  if (enc(&tq, Q) || enc(&tk, K) || enc(&tv, V) || enc(&tdo, dO))
+    return api_error("flash_attn_bwd: cuTensorMapEncodeTiled failed");
+
+  cudaError_t e = cudaMemsetAsync(dq_acc, 0, rows * head_dim * 4, stream);
+  if (e != cudaSuccess) return launch_error(e, "flash_attn_bwd: clearing dQ accumulator");
+  delta_kernel<<<unsigned((rows * 32 + 255) / 256), 256, 0, stream>>>(O, dO, delta, rows,
+                                                                     head_dim);
+
+  Params p{};
+  p.lse = lse;
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.dK = dK;
+  p.dV = dV;
+  p.S = seqlen;
+  p.n_blk = (seqlen + kBlk - 1) / kBlk;
+  p.scale = scale > 0.f ? scale : 1.0f / sqrtf(float(head_dim));
+  p.scale_log2 = p.scale * 1.4426950408889634f;
+  p.causal = causal ? 1u : 0u;
+  p.status = dev->status_word;
+  const uint64_t grid = bh * p.n_blk;
+  if (grid > 0x7fffffffull) return api_error("flash_attn_bwd: grid too large");
+  int rc;
+  if (head_dim == 128) {
+    if ((rc = configure_bwd<128>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    flash_attn_bwd_kernel<128><<<unsigned(grid), kThreads, Cfg<128>::kSmemBytes, stream>>>(
+        tq, tk, tv, tdo, p);
+  } else {
+    if ((rc = configure_bwd<64>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    flash_attn_bwd_kernel<64><<<unsigned(grid), kThreads, Cfg<64>::kSmemBytes, stream>>>(
+        tq, tk, tv, tdo, p);
+  }
+  dq_convert_kernel<<<592, 256, 0, stream>>>(dq_acc, dQ, rows * head_dim, p.scale);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return launch_error(e, "flash_attn_bwd: launch failed");
+  return FelixCode{FELIX_SUCCESS, cudaSuccess};
+}
+
+}  // namespace felix_impl

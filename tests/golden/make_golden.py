@@ -58,6 +58,18 @@ def attn_case(name, Bn, H, S, D, seed, causal=False):
                         V=V.numpy(), O=O.numpy(), lse=lse.numpy())
 
 
+def attn_bwd_case(name, Bn, H, S, D, seed, causal):
+    # gradients of SDPA by torch autograd in float64
+    g = torch.Generator().manual_seed(seed)
+    Q, K, V, dO = [torch.randn(Bn, H, S, D, generator=g).half() for _ in range(4)]
+    q, k, v = [t.double().requires_grad_(True) for t in (Q, K, V)]
+    O = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=causal)
+    O.backward(dO.double())
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), Q=Q.numpy(), K=K.numpy(),
+                        V=V.numpy(), dO=dO.numpy(), dQ=q.grad.numpy(), dK=k.grad.numpy(),
+                        dV=v.grad.numpy(), causal=causal)
+
+
 def main():
     sgemm_case("sgemm_67x45x33", 67, 45, 33, 0.7, 0.3, 10)
     sgemm_case("sgemm_128x128x128", 128, 128, 128, 1.0, 0.0, 11)
@@ -66,6 +78,8 @@ def main():
     attn_case("attn_1x2x80x64", 1, 2, 80, 64, 14)
     attn_case("attn_1x1x130x128", 1, 1, 130, 128, 15)
     attn_case("attn_causal_1x2x150x64", 1, 2, 150, 64, 16, causal=True)
+    attn_bwd_case("attn_bwd_1x2x70x64", 1, 2, 70, 64, 17, causal=False)
+    attn_bwd_case("attn_bwd_causal_1x1x90x128", 1, 1, 90, 128, 18, causal=True)
 
 
 if __name__ == "__main__":

@@ -45,6 +45,14 @@ def test_attention_causal_oracle_matches_golden():
     np.testing.assert_allclose(L, g["lse"], rtol=1e-12, atol=1e-12)
 
 
+@pytest.mark.parametrize("name", ["attn_bwd_1x2x70x64", "attn_bwd_causal_1x1x90x128"])
+def test_attention_bwd_oracle_matches_golden(name):
+    g = _load(name)
+    dQ, dK, dV = oracle.attention_bwd(g["Q"], g["K"], g["V"], g["dO"], causal=bool(g["causal"]))
+    for got, want in ((dQ, g["dQ"]), (dK, g["dK"]), (dV, g["dV"])):
+        np.testing.assert_allclose(got, want, rtol=1e-9, atol=1e-11)
+
+
 def test_attention_oracle_row_subset():
     g = _load("attn_1x1x130x128")
     rows = np.array([0, 5, 129], np.int64)
@@ -71,7 +79,7 @@ def test_half_conversions_exhaustive():
 
 
 def test_golden_fixtures_present():
-    assert len(glob.glob(os.path.join(GOLD, "*.npz"))) == 7
+    assert len(glob.glob(os.path.join(GOLD, "*.npz"))) == 9
 
 
 def test_topk_oracle_matches_numpy_ordering():
