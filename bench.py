@@ -14,7 +14,11 @@ A step is one operator call on one synthetic batch. Each rank runs its own
 copy of the workload (independent units, no data-path collective: weak
 scaling). Steps are timed one by one with CUDA events on the launching stream;
 between steps a 512 MiB buffer is written to flush the 126 MB L2 (outside the
-events). The reported time is the max over ranks of the mean step time.
+events). Workloads whose inputs are larger than the L2 also read a 256 MiB
+buffer after that write, so that the L2 holds clean lines: a streaming kernel
+would otherwise be charged the write-back of the flush buffer (measured: the
+skinny HGEMM 74 us after the write alone, 64 us after write + read). The
+reported time is the max over ranks of the mean step time.
 
 `e2e` times the same call through the C ABI with pinned HOST buffers: the
 host-to-device copy of the inputs, the kernel and the device-to-host copy of
@@ -46,6 +50,36 @@ from sion_b200 import workloads as W  # noqa: E402
 DEFAULT_WORKLOAD = W.HGEMM_4096.name
 METRIC = "HGEMM/FlashAttn/SGEMM TFLOPS per B200 and % of peak; 1/2/4/8-GPU aggregate"
 L2_FLUSH_BYTES = 512 << 20
+L2_CLEAN_BYTES = 256 << 20
+
+
+L2_BYTES = 126 * 10**6
+
+
+class L2Flush:
+    """Evicts the L2 between timed steps: a write larger than the L2; with
+    clean=True also a read larger than the L2 after it, so that the next step
+    starts from cold, clean lines."""
+
+    def __init__(self, device, clean: bool = False):
+        import torch
+        self.w = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+        self.r = torch.zeros(L2_CLEAN_BYTES // 4, dtype=torch.float32, device=device) \
+            if clean else None
+        self.acc = torch.zeros((), dtype=torch.float32, device=device)
+
+    def __call__(self, i):
+        import torch
+        self.w.fill_(float(i))
+        if self.r is not None:
+            torch.sum(self.r, dim=0, out=self.acc)
+
+    @property
+    def description(self) -> str:
+        if self.r is None:
+            return "flushed between steps (512 MiB write outside the timed events)"
+        return ("inputs larger than L2; flushed between steps (512 MiB write, then 256 MiB "
+                "read so the L2 holds clean lines, outside the timed events)")
 
 
 def _peaks():
@@ -188,7 +222,8 @@ class AttnRunner:
                                                                             cfg.D).contiguous()
                        for t in (Q, K, V)]
             self.work_fraction = (s1 - s0) / (cfg.B * cfg.H)
-            cfg = W.AttnConfig(cfg.name, 1, s1 - s0, cfg.S, cfg.D, cfg.seed, cfg.causal)
+            cfg = W.AttnConfig(cfg.name, 1, s1 - s0, cfg.S, cfg.D, cfg.seed, cfg.causal,
+                               cfg.backward)
             self.cfg = cfg
         self.h = [t.pin_memory() for t in (Q, K, V)]
         self.d = [t.to(device) for t in self.h]
@@ -197,8 +232,27 @@ class AttnRunner:
         self.hO = torch.empty_like(self.h[0]).pin_memory()
         self.hL = torch.empty(cfg.B, cfg.H, cfg.S).pin_memory()
         self.launches_per_step = 1
+        if cfg.backward:
+            # forward outputs and the incoming gradient are inputs of the step
+            abi.flash_attn_fwd(self.d[0], self.d[1], self.d[2], self.dO, self.dL,
+                               causal=cfg.causal)
+            g = W.attn_grad_input(W.CONFIGS[cfg.name])
+            if shard_rank is not None:
+                g = g.reshape(-1, cfg.S, cfg.D)[s0:s1].reshape(self.d[0].shape).contiguous()
+            self.h += [self.dO.cpu().pin_memory(), self.dL.cpu().pin_memory(), g.pin_memory()]
+            self.d += [self.dO, self.dL, g.to(device)]
+            self.grads = [torch.empty_like(self.d[0]) for _ in range(3)]
+            self.hgrads = [torch.empty_like(self.h[0]).pin_memory() for _ in range(3)]
+            self.ws = torch.empty(abi.flash_attn_bwd_workspace_size(cfg.H, cfg.B, cfg.S, cfg.D),
+                                  dtype=torch.uint8, device=device)
+            self.launches_per_step = 3  # Delta, backward, dQ conversion
 
     def step(self):
+        if self.cfg.backward:
+            Q, K, V, O, L, dO = self.d
+            self.abi.flash_attn_bwd(Q, K, V, O, dO, L, *self.grads, causal=self.cfg.causal,
+                                    workspace=self.ws)
+            return
         self.abi.flash_attn_fwd(self.d[0], self.d[1], self.d[2], self.dO, self.dL,
                                 causal=self.cfg.causal)
 
@@ -206,6 +260,10 @@ class AttnRunner:
         for d, h in zip(self.d, self.h):
             d.copy_(h, non_blocking=True)
         self.step()
+        if self.cfg.backward:
+            for h, d in zip(self.hgrads, self.grads):
+                h.copy_(d, non_blocking=True)
+            return
         self.hO.copy_(self.dO, non_blocking=True)
         self.hL.copy_(self.dL, non_blocking=True)
 
@@ -215,6 +273,8 @@ class AttnRunner:
 
     @property
     def d2h_bytes(self):
+        if self.cfg.backward:
+            return sum(t.numel() * t.element_size() for t in self.hgrads)
         return self.hO.numel() * 2 + self.hL.numel() * 4
 
     def algorithmic(self):
@@ -243,6 +303,18 @@ def cpu_sample(cfg, budget_s: float = 10.0):
             return p @ v
         desc = (f"naive fp32 softmax(QK^T/sqrt(D))V, {rows} query rows x {cfg.S} keys of one "
                 f"(b,h) per call, torch CPU, repeated for ~{budget_s:.0f} s")
+        if cfg.backward:
+            g = torch.randn(rows, cfg.D, generator=torch.Generator().manual_seed(cfg.seed))
+            flops_per = 10.0 * rows * cfg.S * cfg.D
+            def fn():  # noqa: F811
+                p = torch.softmax((q[:rows] @ k.t()) / (cfg.D ** 0.5), dim=-1)
+                dv = p.t() @ g
+                dp = g @ v.t()
+                ds = p * (dp - (dp * p).sum(-1, keepdim=True))
+                return ds @ k, ds.t() @ q[:rows], dv
+            desc = (f"naive fp32 attention backward (P recomputed; dV, dP, dS, dQ, dK), "
+                    f"{rows} query rows x {cfg.S} keys of one (b,h) per call, torch CPU, "
+                    f"repeated for ~{budget_s:.0f} s")
     else:
         rows = min(cfg.M, 512)
         A, B = W.gemm_inputs(cfg, M=rows)
@@ -301,6 +373,8 @@ def reference_gpu_timing(cfg, steps: int, warmup: int):
     if not (ref.available() and torch.cuda.is_available()):
         return None
     dev = torch.device("cuda", 0)
+    if isinstance(cfg, W.AttnConfig) and (cfg.backward or cfg.causal):
+        return {"unavailable": "the reference has no backward or masked attention kernel"}
     if isinstance(cfg, W.AttnConfig):
         Q, K, V = [t.to(dev) for t in W.attn_inputs(cfg)]
         O = torch.empty_like(Q)
@@ -313,12 +387,12 @@ def reference_gpu_timing(cfg, steps: int, warmup: int):
         else:
             C = torch.empty(cfg.M, cfg.N, dtype=torch.half, device=dev)
             step = lambda: ref.hgemm(A, B, C, nt=cfg.b_layout == "nk")  # noqa: E731
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(dev, clean=cfg.io_bytes > L2_BYTES)
     for _ in range(warmup):
         step()
     times = []
     for i in range(steps):
-        flush.fill_(float(i))
+        flush(i)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         step()
@@ -387,7 +461,7 @@ def main():
     torch.cuda.set_device(device)
     runner = make_runner(args.workload, device, rank if args.shard else None, world)
     full_cfg = W.CONFIGS[args.workload]
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    flush = L2Flush(device, clean=full_cfg.io_bytes > L2_BYTES)
     stream = torch.cuda.current_stream()
 
     for _ in range(args.warmup):
@@ -403,7 +477,7 @@ def main():
         time.sleep(0.25)
         t_wall = time.perf_counter()
         for i in range(args.steps):
-            flush.fill_(float(i))
+            flush(i)
             starts[i].record(stream)
             runner.step()
             ends[i].record(stream)
@@ -464,7 +538,7 @@ def main():
         par = (f"shards x{world} (N-column / (b,h) blocks, no collective)" if args.shard
                else f"replicas x{world} (independent units)")
         conf = {"workload": cfg.name, "parallelism": par,
-                "l2": "flushed between steps (512 MiB write outside the timed events)"}
+                "l2": flush.description}
         if isinstance(cfg, W.GemmConfig):
             conf.update({"M": cfg.M, "N": cfg.N, "K": cfg.K, "b_layout": cfg.b_layout})
         else:

@@ -180,6 +180,12 @@ def flash_attn_bwd(Q, K, V, O, dO, lse, dQ, dK, dV, scale=0.0, causal=False, wor
     return dQ, dK, dV
 
 
+def flash_attn_bwd_workspace_size(heads, batch, seqlen, head_dim) -> int:
+    n = C.c_size_t(0)
+    check(lib().felix_flash_attn_bwd_workspace_size(heads, batch, seqlen, head_dim, C.byref(n)))
+    return n.value
+
+
 def topk_select(data, out, k, largest=True, stream=None):
     """data [num_slices, slice_size] fp32 -> out [num_slices]: k-th largest/smallest."""
     num_slices, slice_size = data.shape

@@ -147,6 +147,22 @@ int encode_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint6
   return r == CUDA_SUCCESS ? 0 : int(r);
 }
 
+int encode_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer1,
+                       uint64_t outer2, uint64_t pitch1, uint64_t pitch2, uint32_t bi,
+                       uint32_t bo1, uint32_t bo2) {
+  std::call_once(g_encode_once, load_encode);
+  if (!g_encode) return -1;
+  cuuint64_t dims[3] = {inner, outer1, outer2};
+  cuuint64_t strides[2] = {pitch1, pitch2};
+  cuuint32_t box[3] = {bi, bo1, bo2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : int(r);
+}
+
 int encode_tmap_2d_f16_noswizzle(CUtensorMap* map, const void* base, uint64_t inner,
                                  uint64_t outer, uint64_t pitch, uint32_t bi, uint32_t bo) {
   return encode_2d(map, base, inner, outer, pitch, bi, bo, CU_TENSOR_MAP_SWIZZLE_NONE);

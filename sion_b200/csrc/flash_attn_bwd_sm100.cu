@@ -13,16 +13,20 @@
 // computed in the "transposed" orientation so that TMEM lanes are keys:
 //   S^T  = K_j Q_i^T        (SS MMA)              -> TMEM cols [0, 128)
 //   dP^T = V_j dO_i^T       (SS MMA)              -> TMEM cols [128, 256)
-//   P^T, dS^T (fp16) overwrite the first halves of those regions (TMEM A
-//   operands); dS is also written to shared memory as an MN-major tile;
+//   P^T, dS^T (fp16) overwrite the first half of each 64-column half of
+//   those regions (TMEM A operands); dS is also written to shared memory as
+//   an MN-major tile;
 //   dV_j += P^T dO_i        (TS MMA)              -> TMEM cols [256, 256 + D)
 //   dK_j += dS^T Q_i        (TS MMA)              -> TMEM cols [384, 384 + D)
 //   dQ_i  = dS K_j          (SS MMA, A MN-major)  -> TMEM cols [0, D)
-// dQ_i is reduced into an fp32 buffer with 16-byte vector reductions; a small
-// kernel scales and converts it to fp16 at the end. MMAs of a CTA execute in
-// issue order, so dQ_i may overwrite the P^T columns right behind the dV MMA
-// that reads them. Warps: 0 TMA loader, 1 MMA issuer, 4-7 one warpgroup of
-// element-wise work (one key row per thread).
+// dQ_i is read out of TMEM in 32 x 32 fp32 boxes, staged in shared memory
+// (128-byte swizzle) and added into an fp32 buffer [BH][S][D] with TMA tensor
+// reductions (cp.reduce.async.bulk.tensor ... add), which run asynchronously and
+// clip rows past S; a small kernel scales and converts the buffer to fp16 at
+// the end. MMAs of a CTA execute in issue order, so dQ_i may overwrite the P^T
+// columns right behind the dV MMA that reads them. Warps: 0 TMA loader, 1 MMA
+// issuer, 4-11 two warpgroups of element-wise work (one key row per thread,
+// each warpgroup one half of the query columns / of D).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -31,11 +35,21 @@
 #include "felix_internal.h"
 #include "sm100_ptx.cuh"
 
+// Timing experiments only (results are wrong when set): skip the dQ
+// reductions / the exponentials.
+#ifndef FELIX_FA_BWD_EXP_NO_DQRED
+#define FELIX_FA_BWD_EXP_NO_DQRED 0
+#endif
+#ifndef FELIX_FA_BWD_EXP_NO_EW
+#define FELIX_FA_BWD_EXP_NO_EW 0
+#endif
+
 namespace felix_sm100 {
 namespace attn_bwd {
 
 constexpr int kBlk = 128;  // keys per CTA, queries per loop step
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
+constexpr int kEwWarps = 8;  // element-wise warps (two warpgroups)
 
 template <int D>
 struct Cfg {
@@ -48,14 +62,16 @@ struct Cfg {
   static constexpr int kDSOff = kDOOff + kTile;       // dS: 128 queries x 128 keys fp16
   // lse2[2][128], delta[2][128]: double-buffered by step parity
   static constexpr int kVecOff = kDSOff + kBlk * kBlk * 2;
-  static constexpr int kBarOff = kVecOff + 4 * kBlk * 4;
+  // second dQ staging box (32 x 32 fp32) per element-wise warp; the first one
+  // is the 4 KB of the dS tile that the same warp writes
+  static constexpr int kStgOff = kVecOff + 4 * kBlk * 4;
+  static constexpr int kBarOff = kStgOff + kEwWarps * 4096;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;
 };
 
 struct Params {
   const float* lse;     // [BH, S] natural log (forward output)
   const float* delta;   // [BH, S] rowsum(dO * O)
-  float* dq_acc;        // [BH, S, D] fp32, zeroed
   __half* dK;
   __half* dV;
   uint32_t S, n_blk;
@@ -70,6 +86,12 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// TMEM column (relative to the S^T / dP^T region) of packed fp16 query
+// column q: queries [64h, 64h + 64) are packed into columns [64h, 64h + 32).
+__device__ __forceinline__ uint32_t packed_col(int q) {
+  return uint32_t(q & ~63) + uint32_t(q & 63) / 2;
+}
+
 template <int ROWS>
 __device__ __forceinline__ uint64_t kmajor(uint32_t tile, int k) {
   return make_sdesc_sw128(tile + (uint32_t(k) >> 2) * (ROWS * 128) + (uint32_t(k) & 3u) * 32, 16,
@@ -80,18 +102,13 @@ __device__ __forceinline__ uint64_t mnmajor(uint32_t tile, int k) {
   return make_sdesc_sw128(tile + uint32_t(k) * 2048, kBlk * 128, 1024);
 }
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
-               "f"(c), "f"(d)
-               : "memory");
-}
-
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV,
-                          const __grid_constant__ CUtensorMap tmDO, const Params p) {
+                          const __grid_constant__ CUtensorMap tmDO,
+                          const __grid_constant__ CUtensorMap tmDQ, const Params p) {
   using C_ = Cfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -102,9 +119,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* qdo_full = bars + 1;   // Q_i, dO_i landed
   uint64_t* qdo_empty = bars + 2;  // MMAs of step i done with Q_i, dO_i, dS
   uint64_t* st_full = bars + 3;    // S^T, dP^T in TMEM
-  uint64_t* p_ready = bars + 4;    // P^T, dS^T in TMEM, dS in smem (4 warp arrivals)
+  uint64_t* p_ready = bars + 4;    // P^T, dS^T in TMEM, dS in smem (8 warp arrivals)
   uint64_t* dq_full = bars + 5;    // dQ_i in TMEM
-  uint64_t* dq_free = bars + 6;    // dQ_i read out (4 warp arrivals)
+  uint64_t* dq_free = bars + 6;    // dQ_i read out (8 warp arrivals)
   uint64_t* done = bars + 7;       // every MMA complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -116,13 +133,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t n_i = p.n_blk - i0;
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 8; ++b) mbar_init(&bars[b], (b == 4 || b == 6) ? 4 : 1);
+    for (int b = 0; b < 8; ++b) mbar_init(&bars[b], (b == 4 || b == 6) ? kEwWarps : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmDQ);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -192,11 +210,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kBlk / 16; ++k)
-          umma_f16_ts(tmem + kColDV, tmem + kColS + k * 8, mnmajor(sDO, k), id_acc,
+          umma_f16_ts(tmem + kColDV, tmem + kColS + packed_col(16 * k), mnmajor(sDO, k), id_acc,
                       (s > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < kBlk / 16; ++k)
-          umma_f16_ts(tmem + kColDK, tmem + kColDP + k * 8, mnmajor(sQ, k), id_acc,
+          umma_f16_ts(tmem + kColDK, tmem + kColDP + packed_col(16 * k), mnmajor(sQ, k), id_acc,
                       (s > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < kBlk / 16; ++k)
@@ -210,12 +228,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- element-wise
-    const uint32_t q4 = warp & 3u;
-    const uint32_t r = q4 * 32 + lane;  // key row of this CTA (TMEM lane)
+    const uint32_t q4 = warp & 3u;         // TMEM lane quadrant
+    const uint32_t ew = warp - 4;          // 0..7
+    const uint32_t g = ew >> 2;            // column half handled by this warpgroup
+    const uint32_t r = q4 * 32 + lane;     // key row of this CTA (TMEM lane)
     const uint32_t key = j * kBlk + r;
     const uint32_t la = (q4 * 32u) << 16;
     const uint32_t tid = threadIdx.x - 128;
     uint8_t* sDS = smem + C_::kDSOff;
+    // dQ staging: box 0 is this warp's own 4 KB of the dS tile (free once the
+    // dQ MMA has read it), box 1 a dedicated 4 KB
+    uint8_t* stg0 = sDS + (g * 4 + q4) * 4096;
+    uint8_t* stg1 = smem + C_::kStgOff + ew * 4096;
     const float sl2 = p.scale_log2;
     bool ok = true;
     for (uint32_t s = 0; ok && s < n_i; ++s) {
@@ -226,18 +250,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       // previous step's copy while this one is written
       float* s_lse2 = s_vec + ph * (2 * kBlk);
       float* s_delta = s_lse2 + kBlk;
-      {
+      if (tid < kBlk) {
         const uint32_t q = i * kBlk + tid;
         s_lse2[tid] = q < p.S ? __ldg(p.lse + size_t(bh) * p.S + q) * 1.4426950408889634f
                               : INFINITY;
         s_delta[tid] = q < p.S ? __ldg(p.delta + size_t(bh) * p.S + q) : 0.f;
       }
-      named_barrier_sync(1, 128);
+      // the dS writes below reuse staging box 0: its last reduction must have
+      // been read out of shared memory
+      if (lane == 0) bulk_wait_group_read<0>();
+      named_barrier_sync(1, kEwWarps * 32);
       if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, kWdAttnSoftmax))) break;
       tc_fence_after();
       const bool key_ok = key < p.S;
 #pragma unroll 1
-      for (int c = 0; c < kBlk; c += 32) {
+      for (int c = int(g) * 64; c < int(g) * 64 + 64; c += 32) {
         uint32_t sr[32], dr[32];
         tmem_ld_32x32b_x32(tmem + la + kColS + c, sr);
         tmem_ld_32x32b_x32(tmem + la + kColDP + c, dr);
@@ -250,7 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int h = 0; h < 2; ++h) {
             const uint32_t qi = uint32_t(c + e + h);
             const uint32_t q = i * kBlk + qi;
-            float pr = ex2(fmaf(__uint_as_float(sr[e + h]), sl2, -s_lse2[qi]));
+            float pr = FELIX_FA_BWD_EXP_NO_EW
+                           ? __uint_as_float(sr[e + h])
+                           : ex2(fmaf(__uint_as_float(sr[e + h]), sl2, -s_lse2[qi]));
             if (!key_ok || (p.causal && q < key)) pr = 0.f;
             pv[h] = pr;
             dv[h] = pr * (__uint_as_float(dr[e + h]) - s_delta[qi]);
@@ -258,8 +287,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk[e / 2] = pack_half2(pv[0], pv[1]);
           dk[e / 2] = pack_half2(dv[0], dv[1]);
         }
-        tmem_st_32x32b_x16(tmem + la + kColS + c / 2, pk);
-        tmem_st_32x32b_x16(tmem + la + kColDP + c / 2, dk);
+        // packed fp16 P^T / dS^T: each warpgroup packs its 64 query columns into
+        // the first 32 of them, so it never overwrites columns the other one
+        // is still reading
+        tmem_st_32x32b_x16(tmem + la + kColS + packed_col(c), pk);
+        tmem_st_32x32b_x16(tmem + la + kColDP + packed_col(c), dk);
         // dS (queries x keys) as an MN-major A tile: query chunk c / 64, row = key r,
         // 16-byte units swizzled with the row (128-byte swizzle)
         uint8_t* row = sDS + (c / 64) * (kBlk * 128) + r * 128;
@@ -275,28 +307,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
-      // dQ_i rows (lane = query) -> fp32 accumulation buffer
+      // dQ_i rows (lane = query), columns [g * D / 2, (g + 1) * D / 2) -> staged
+      // 32 x 32 boxes -> TMA reduction into the fp32 accumulator
       if (!(ok = mbar_wait(dq_full, ph, abort_flag, p.status, kWdAttnSoftmax))) break;
       tc_fence_after();
-      const uint32_t q = i * kBlk + r;
-      float* dst = p.dq_acc + (size_t(bh) * p.S + q) * D;
-#pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
+      const uint32_t q0 = i * kBlk + q4 * 32;
+      constexpr int kDqBoxes = D / 64;
+#pragma unroll
+      for (int b = 0; b < kDqBoxes; ++b) {
+        const int c = int(g) * (D / 2) + b * 32;
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem + la + kColS + c, v);
         tmem_ld_wait();
-        if (q < p.S) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            red_add_v4(dst + c + e, __uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                       __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+        if (b == kDqBoxes - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dq_free);
         }
+        uint8_t* stg = b == 0 ? stg0 : stg1;
+        if (b > 0) {
+          // box 1's previous reduction (one step ago) must have been read
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((u ^ (lane & 7u)) * 16)) =
+              make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && q0 < p.S && !FELIX_FA_BWD_EXP_NO_DQRED) {
+          tma_reduce_add_3d(&tmDQ, stg, c, int(q0), int(bh));
+        }
+        if (lane == 0) bulk_commit_group();
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
     }
-    // dK_j, dV_j (lane = key) -> fp16
+    // dK_j, dV_j (lane = key) -> fp16, columns [g * D / 2, (g + 1) * D / 2)
     if (ok && mbar_wait(done, 0, abort_flag, p.status, kWdAttnSoftmax)) {
       tc_fence_after();
 #pragma unroll 1
@@ -305,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mul = which ? p.scale : 1.f;
         __half* out = (which ? p.dK : p.dV) + (size_t(bh) * p.S + key) * D;
 #pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
+        for (int c = int(g) * (D / 2); c < int(g + 1) * (D / 2); c += 32) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem + la + col + c, v);
           tmem_ld_wait();
@@ -321,6 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // every staged reduction complete before the shared memory goes away
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -423,12 +472,14 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
     dq_acc = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(dq_acc) + 15) & ~uintptr_t(15));
   }
 
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   auto enc = [&](CUtensorMap* m, const void* base) {
     return encode_tmap_3d_f16(m, base, head_dim, seqlen, bh, uint64_t(head_dim) * 2,
                               uint64_t(seqlen) * head_dim * 2, 64, kBlk, 1);
   };
-  if (enc(&tq, Q) || enc(&tk, K) || enc(&tv, V) || enc(&tdo, dO))
+  if (enc(&tq, Q) || enc(&tk, K) || enc(&tv, V) || enc(&tdo, dO) ||
+      encode_tmap_3d_f32(&tdq, dq_acc, head_dim, seqlen, bh, uint64_t(head_dim) * 4,
+                         uint64_t(seqlen) * head_dim * 4, 32, 32, 1))
     return api_error("flash_attn_bwd: cuTensorMapEncodeTiled failed");
 
   cudaError_t e = cudaMemsetAsync(dq_acc, 0, rows * head_dim * 4, stream);
@@ -439,7 +490,6 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
   Params p{};
   p.lse = lse;
   p.delta = delta;
-  p.dq_acc = dq_acc;
   p.dK = dK;
   p.dV = dV;
   p.S = seqlen;
@@ -454,11 +504,11 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
   if (head_dim == 128) {
     if ((rc = configure_bwd<128>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
     flash_attn_bwd_kernel<128><<<unsigned(grid), kThreads, Cfg<128>::kSmemBytes, stream>>>(
-        tq, tk, tv, tdo, p);
+        tq, tk, tv, tdo, tdq, p);
   } else {
     if ((rc = configure_bwd<64>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
     flash_attn_bwd_kernel<64><<<unsigned(grid), kThreads, Cfg<64>::kSmemBytes, stream>>>(
-        tq, tk, tv, tdo, p);
+        tq, tk, tv, tdo, tdq, p);
   }
   dq_convert_kernel<<<592, 256, 0, stream>>>(dq_acc, dQ, rows * head_dim, p.scale);
   e = cudaGetLastError();

@@ -43,17 +43,23 @@ class AttnConfig:
     D: int
     seed: int
     causal: bool = False
+    backward: bool = False
 
     @property
     def flops(self) -> float:
-        # reference convention (bench/flash_attention/fa_bench.cpp:93-95): 4*B*H*S^2*D;
-        # a causal mask halves the work actually required
-        f = 4.0 * self.B * self.H * self.S * self.S * self.D
+        # reference convention (bench/flash_attention/fa_bench.cpp:93-95): 4*B*H*S^2*D
+        # for the forward (QK^T and PV). The backward does five such products
+        # (S recomputed, dP, dV, dK, dQ): 10*B*H*S^2*D. A causal mask halves the
+        # work actually required.
+        f = (10.0 if self.backward else 4.0) * self.B * self.H * self.S * self.S * self.D
         return f / 2 if self.causal else f
 
     @property
     def io_bytes(self) -> int:
-        return 2 * 4 * self.B * self.H * self.S * self.D + 4 * self.B * self.H * self.S
+        t = 2 * self.B * self.H * self.S * self.D
+        rows = 4 * self.B * self.H * self.S
+        # backward: reads Q, K, V, O, dO, LSE; writes dQ, dK, dV
+        return 8 * t + rows if self.backward else 4 * t + rows
 
 
 # The five configurations of the headline metric.
@@ -64,11 +70,13 @@ HGEMM_SKINNY = GemmConfig("hgemm_f16_128x8192x16384_nt", 128, 8192, 16384, "f16"
 FA_8192 = AttnConfig("flash_attn_fwd_f16_4x32x8192x128", 4, 32, 8192, 128, 3)
 FA_8192_CAUSAL = AttnConfig("flash_attn_fwd_causal_f16_4x32x8192x128", 4, 32, 8192, 128, 3,
                             causal=True)
+FA_BWD_8192 = AttnConfig("flash_attn_bwd_f16_4x32x8192x128", 4, 32, 8192, 128, 3,
+                         backward=True)
 HGEMM_16384 = GemmConfig("hgemm_f16_16384_nt", 16384, 16384, 16384, "f16", "nk", "uniform", 1.0,
                          4)
 
 CONFIGS = {c.name: c for c in (SGEMM_1024, HGEMM_4096, HGEMM_SKINNY, FA_8192, HGEMM_16384,
-                               FA_8192_CAUSAL)}
+                               FA_8192_CAUSAL, FA_BWD_8192)}
 
 
 def _draw(gen: torch.Generator, shape, dist: str, std: float) -> torch.Tensor:
@@ -97,3 +105,9 @@ def attn_inputs(cfg: AttnConfig):
     K = torch.randn(*shape, generator=gen, dtype=torch.float32).half()
     V = torch.randn(*shape, generator=gen, dtype=torch.float32).half()
     return Q, K, V
+
+
+def attn_grad_input(cfg: AttnConfig):
+    """dO for a backward config: drawn after Q, K, V from the same seed."""
+    gen = torch.Generator().manual_seed(cfg.seed + 1000)
+    return torch.randn(cfg.B, cfg.H, cfg.S, cfg.D, generator=gen, dtype=torch.float32).half()
