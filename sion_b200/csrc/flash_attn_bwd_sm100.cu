@@ -57,16 +57,17 @@ struct Cfg {
   static constexpr int kTile = kBlk * D * 2;  // one 128 x D fp16 tile
   static constexpr int kKOff = 0;
   static constexpr int kVOff = kKOff + kTile;
-  static constexpr int kQOff = kVOff + kTile;
-  static constexpr int kDOOff = kQOff + kTile;
-  static constexpr int kDSOff = kDOOff + kTile;       // dS: 128 queries x 128 keys fp16
+  static constexpr int kQOff = kVOff + kTile;         // Q_i, two stages
+  static constexpr int kDOOff = kQOff + 2 * kTile;    // dO_i, two stages
+  // dS: 128 queries x 128 keys fp16; after the dQ MMA has read it, each
+  // element-wise warp's 4 KB of it is that warp's dQ staging box
+  static constexpr int kDSOff = kDOOff + 2 * kTile;
   // lse2[2][128], delta[2][128]: double-buffered by step parity
   static constexpr int kVecOff = kDSOff + kBlk * kBlk * 2;
-  // second dQ staging box (32 x 32 fp32) per element-wise warp; the first one
-  // is the 4 KB of the dS tile that the same warp writes
-  static constexpr int kStgOff = kVecOff + 4 * kBlk * 4;
-  static constexpr int kBarOff = kStgOff + kEwWarps * 4096;
-  static constexpr int kSmemBytes = kBarOff + 256 + 1024;
+  static constexpr int kBarOff = kVecOff + 4 * kBlk * 4;
+  // No alignment slack (D = 128 needs all but 768 B of the 227 KB): the
+  // kernel checks that the dynamic shared memory starts 1024-byte aligned.
+  static constexpr int kSmemBytes = kBarOff + 256;
 };
 
 struct Params {
@@ -111,19 +112,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tmDQ, const Params p) {
   using C_ = Cfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_raw;
+  if (smem_u32(smem) & 1023u) {  // uniform over the CTA: nobody touches a barrier
+    if (threadIdx.x == 0) atomicCAS(p.status, 0u, unsigned(kWdSmemAlign));
+    return;
+  }
   float* s_vec = reinterpret_cast<float*>(smem + C_::kVecOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
   uint64_t* kv_full = bars;        // K_j, V_j landed
-  uint64_t* qdo_full = bars + 1;   // Q_i, dO_i landed
-  uint64_t* qdo_empty = bars + 2;  // MMAs of step i done with Q_i, dO_i, dS
-  uint64_t* st_full = bars + 3;    // S^T, dP^T in TMEM
-  uint64_t* p_ready = bars + 4;    // P^T, dS^T in TMEM, dS in smem (8 warp arrivals)
-  uint64_t* dq_full = bars + 5;    // dQ_i in TMEM
-  uint64_t* dq_free = bars + 6;    // dQ_i read out (8 warp arrivals)
-  uint64_t* done = bars + 7;       // every MMA complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* st_full = bars + 1;    // S^T, dP^T in TMEM
+  uint64_t* p_ready = bars + 2;    // P^T, dS^T in TMEM, dS in smem (8 warp arrivals)
+  uint64_t* dq_full = bars + 3;    // dQ_i in TMEM
+  uint64_t* dq_free = bars + 4;    // dQ_i read out (8 warp arrivals)
+  uint64_t* done = bars + 5;       // every MMA complete
+  uint64_t* qdo_full = bars + 6;   // [2] Q_i, dO_i landed in stage i % 2
+  uint64_t* qdo_empty = bars + 8;  // [2] MMAs of step i done with stage i % 2
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -133,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t n_i = p.n_blk - i0;
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 8; ++b) mbar_init(&bars[b], (b == 4 || b == 6) ? kEwWarps : 1);
+    for (int b = 0; b < 10; ++b) mbar_init(&bars[b], (b == 2 || b == 4) ? kEwWarps : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -166,20 +170,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t filled = 0;
       for (uint32_t s = 0; s < n_i; ++s) {
         const uint32_t i = i0 + s;
-        if (!mbar_wait(qdo_empty, (s & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * C_::kTile);
+        const uint32_t st = s & 1u, use = s >> 1;
+        if (!mbar_wait(qdo_empty + st, (use & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
+        mbar_arrive_expect_tx(qdo_full + st, 2 * C_::kTile);
 #pragma unroll
         for (int c = 0; c < C_::kChunks; ++c) {
-          tma_load_3d(smem + C_::kQOff + c * (kBlk * 128), &tmQ, qdo_full, 64 * c, int(i * kBlk),
-                      int(bh));
-          tma_load_3d(smem + C_::kDOOff + c * (kBlk * 128), &tmDO, qdo_full, 64 * c,
-                      int(i * kBlk), int(bh));
+          tma_load_3d(smem + C_::kQOff + st * C_::kTile + c * (kBlk * 128), &tmQ, qdo_full + st,
+                      64 * c, int(i * kBlk), int(bh));
+          tma_load_3d(smem + C_::kDOOff + st * C_::kTile + c * (kBlk * 128), &tmDO,
+                      qdo_full + st, 64 * c, int(i * kBlk), int(bh));
         }
         ++filled;
       }
+      // drain: the last load of each stage has landed
       int dummy = 0;
       mbar_wait(kv_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
-      if (filled) mbar_wait(qdo_full, (filled - 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
+      for (uint32_t s = filled > 2 ? filled - 2 : 0; s < filled; ++s)
+        mbar_wait(qdo_full + (s & 1u), (s >> 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -188,12 +195,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_acc = make_idesc_f16_f32(kBlk, D, false, true);     // dV, dK
       const uint32_t id_dq = make_idesc_f16_f32(kBlk, D, true, true);       // dQ
       const uint32_t sK = smem_u32(smem + C_::kKOff), sV = smem_u32(smem + C_::kVOff);
-      const uint32_t sQ = smem_u32(smem + C_::kQOff), sDO = smem_u32(smem + C_::kDOOff);
       const uint32_t sDS = smem_u32(smem + C_::kDSOff);
       bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kWdAttnMma);
       for (uint32_t s = 0; ok && s < n_i; ++s) {
         const uint32_t ph = s & 1u;
-        if (!(ok = mbar_wait(qdo_full, ph, abort_flag, p.status, kWdAttnMma))) break;
+        const uint32_t st = s & 1u, use = s >> 1;
+        const uint32_t sQ = smem_u32(smem + C_::kQOff + st * C_::kTile);
+        const uint32_t sDO = smem_u32(smem + C_::kDOOff + st * C_::kTile);
+        if (!(ok = mbar_wait(qdo_full + st, use & 1u, abort_flag, p.status, kWdAttnMma))) break;
         // the dQ of the previous step must have been read out of cols [0, D)
         if (s > 0 && !(ok = mbar_wait(dq_free, ph ^ 1u, abort_flag, p.status, kWdAttnMma))) break;
         tc_fence_after();
@@ -219,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < kBlk / 16; ++k)
           umma_f16_ss(tmem + kColS, mnmajor(sDS, k), mnmajor(sK, k), id_dq, k > 0 ? 1u : 0u);
-        umma_commit(qdo_empty);
+        umma_commit(qdo_empty + st);
         umma_commit(dq_full);
       }
       umma_commit(done);
@@ -229,17 +238,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- element-wise
     const uint32_t q4 = warp & 3u;         // TMEM lane quadrant
-    const uint32_t ew = warp - 4;          // 0..7
-    const uint32_t g = ew >> 2;            // column half handled by this warpgroup
+    const uint32_t g = (warp - 4) >> 2;    // column half handled by this warpgroup
     const uint32_t r = q4 * 32 + lane;     // key row of this CTA (TMEM lane)
     const uint32_t key = j * kBlk + r;
     const uint32_t la = (q4 * 32u) << 16;
     const uint32_t tid = threadIdx.x - 128;
     uint8_t* sDS = smem + C_::kDSOff;
-    // dQ staging: box 0 is this warp's own 4 KB of the dS tile (free once the
-    // dQ MMA has read it), box 1 a dedicated 4 KB
-    uint8_t* stg0 = sDS + (g * 4 + q4) * 4096;
-    uint8_t* stg1 = smem + C_::kStgOff + ew * 4096;
+    // dQ staging box: this warp's own 4 KB of the dS tile (free once the dQ
+    // MMA has read it)
+    uint8_t* stg = sDS + (g * 4 + q4) * 4096;
     const float sl2 = p.scale_log2;
     bool ok = true;
     for (uint32_t s = 0; ok && s < n_i; ++s) {
@@ -256,8 +263,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                               : INFINITY;
         s_delta[tid] = q < p.S ? __ldg(p.delta + size_t(bh) * p.S + q) : 0.f;
       }
-      // the dS writes below reuse staging box 0: its last reduction must have
-      // been read out of shared memory
+      // the dS writes below reuse the staging box: its last reduction must
+      // have been read out of shared memory
       if (lane == 0) bulk_wait_group_read<0>();
       named_barrier_sync(1, kEwWarps * 32);
       if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, kWdAttnSoftmax))) break;
@@ -324,10 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(dq_free);
         }
-        uint8_t* stg = b == 0 ? stg0 : stg1;
         if (b > 0) {
-          // box 1's previous reduction (one step ago) must have been read
-          if (lane == 0) bulk_wait_group_read<1>();
+          // the previous box's reduction must have been read
+          if (lane == 0) bulk_wait_group_read<0>();
           __syncwarp();
         }
 #pragma unroll
@@ -381,6 +387,366 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// D = 128: 64-query steps with double-buffered S^T / dP^T, so that the
+// element-wise work and the dQ read-out of one step overlap the MMAs of the
+// neighbouring steps.
+//
+// TMEM (512 columns): buffer b in {0, 1} holds S^T at [128b, 128b + 64) and
+// dP^T at [128b + 64, 128b + 128) (lanes = the CTA's 128 keys, columns = the
+// step's 64 queries); dV at [256, 384), dK at [384, 512). dQ^T = K^T dS^T
+// (lanes = d, columns = queries) overwrites the S^T columns of its own buffer
+// right behind the dV MMA that reads P^T from them, and is read out before the
+// S^T of the step two ahead is written there.
+// MMA issue order: S/dP(0), S/dP(1), then for t = 0, 1, ...:
+//   dV/dK/dQ(t); after odd t also S/dP(t + 1), S/dP(t + 2).
+// so the read-out of dQ(t) runs behind dV/dK/dQ(t + 1) and the element-wise
+// work of step t + 1 behind the MMAs of step t.
+// Warps: 0 TMA loader, 1 MMA issuer, 4-7 dQ read-out (TMEM lane quadrant =
+// warp % 4), 8-15 element-wise (two warpgroups, 32 query columns each).
+namespace q64 {
+
+constexpr int kD = 128;
+constexpr int kBk = 128;  // keys per CTA
+constexpr int kBq = 64;   // queries per step
+constexpr int kThreads = 512;
+constexpr int kEwWarps = 8;
+constexpr int kRdWarps = 4;
+constexpr int kQStages = 3;
+constexpr int kKTile = kBk * kD * 2;   // 32 KB
+constexpr int kQTile = kBq * kD * 2;   // 16 KB
+constexpr int kDsTile = kBk * kBq * 2; // 16 KB: dS, rows = keys, 64 queries per 128-byte row
+constexpr int kKOff = 0;
+constexpr int kVOff = kKOff + kKTile;
+constexpr int kQOff = kVOff + kKTile;                 // [kQStages]
+constexpr int kDOOff = kQOff + kQStages * kQTile;     // [kQStages]
+constexpr int kDSOff = kDOOff + kQStages * kQTile;    // [2]
+constexpr int kStgOff = kDSOff + 2 * kDsTile;         // [kRdWarps] x two 32 x 32 fp32 boxes
+constexpr int kVecOff = kStgOff + kRdWarps * 8192;    // [2] x (lse2[64], delta[64])
+constexpr int kBarOff = kVecOff + 2 * 2 * kBq * 4;
+constexpr int kSmemBytes = kBarOff + 256;  // no alignment slack: checked in the kernel
+static_assert(kSmemBytes <= 232448, "shared memory");
+
+// TMEM column (within a 64-column S^T / dP^T region) of packed fp16 query q:
+// each element-wise warpgroup packs its 32 queries into the first 16 of them.
+__device__ __forceinline__ uint32_t packed_col64(int q) {
+  return uint32_t(q & ~31) + uint32_t(q & 31) / 2;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_attn_bwd_q64_kernel(const __grid_constant__ CUtensorMap tmQ,
+                              const __grid_constant__ CUtensorMap tmK,
+                              const __grid_constant__ CUtensorMap tmV,
+                              const __grid_constant__ CUtensorMap tmDO,
+                              const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (smem_u32(smem) & 1023u) {  // uniform over the CTA: nobody touches a barrier
+    if (threadIdx.x == 0) atomicCAS(p.status, 0u, unsigned(kWdSmemAlign));
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint64_t* kv_full = bars;         // K_j, V_j landed
+  uint64_t* qdo_full = bars + 1;    // [3] Q_i, dO_i landed in stage i % 3
+  uint64_t* qdo_empty = bars + 4;   // [3] MMAs of step i done with stage i % 3
+  uint64_t* st_full = bars + 7;     // [2] S^T, dP^T of step i in buffer i % 2
+  uint64_t* p_ready = bars + 9;     // [2] P^T, dS^T in TMEM, dS in smem (8 warp arrivals)
+  uint64_t* dq_full = bars + 11;    // [2] dQ^T of step i in buffer i % 2
+  uint64_t* dq_free = bars + 13;    // [2] dQ^T read out (4 warp arrivals)
+  uint64_t* done = bars + 15;       // every MMA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_vec = reinterpret_cast<float*>(smem + kVecOff);
+
+  const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t bh = blockIdx.x / p.n_blk;
+  const uint32_t j = blockIdx.x % p.n_blk;          // 128-key block
+  const uint32_t n_q = (p.S + kBq - 1) / kBq;       // 64-query blocks
+  const uint32_t i0 = p.causal ? 2 * j : 0;         // first query block at or after key j*128
+  const uint32_t n = n_q - i0;
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 16; ++b) {
+      uint32_t cnt = 1;
+      if (b == 9 || b == 10) cnt = kEwWarps;
+      if (b == 13 || b == 14) cnt = kRdWarps;
+      mbar_init(&bars[b], cnt);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmDQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t kColDV = 256, kColDK = 384;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- loader
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * kKTile);
+#pragma unroll
+      for (int c = 0; c < kD / 64; ++c) {
+        tma_load_3d(smem + kKOff + c * (kBk * 128), &tmK, kv_full, 64 * c, int(j * kBk), int(bh));
+        tma_load_3d(smem + kVOff + c * (kBk * 128), &tmV, kv_full, 64 * c, int(j * kBk), int(bh));
+      }
+      uint32_t filled = 0;
+      for (uint32_t s = 0; s < n; ++s) {
+        const uint32_t st = s % kQStages, use = s / kQStages;
+        const int q0 = int((i0 + s) * kBq);
+        if (!mbar_wait(qdo_empty + st, (use & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
+        mbar_arrive_expect_tx(qdo_full + st, 2 * kQTile);
+#pragma unroll
+        for (int c = 0; c < kD / 64; ++c) {
+          tma_load_3d(smem + kQOff + st * kQTile + c * (kBq * 128), &tmQ, qdo_full + st, 64 * c,
+                      q0, int(bh));
+          tma_load_3d(smem + kDOOff + st * kQTile + c * (kBq * 128), &tmDO, qdo_full + st,
+                      64 * c, q0, int(bh));
+        }
+        ++filled;
+      }
+      // drain: the last load of every stage has landed
+      int dummy = 0;
+      mbar_wait(kv_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
+      for (uint32_t s = filled > kQStages ? filled - kQStages : 0; s < filled; ++s)
+        mbar_wait(qdo_full + s % kQStages, (s / kQStages) & 1u, &dummy, p.status, kWdDrain,
+                  100000000ull);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_s = make_idesc_f16_f32(kBk, kBq, false, false);  // S^T, dP^T
+      const uint32_t id_acc = make_idesc_f16_f32(kBk, kD, false, true);  // dV, dK
+      const uint32_t id_dq = make_idesc_f16_f32(kD, kBq, true, true);    // dQ^T
+      const uint32_t sK = smem_u32(smem + kKOff), sV = smem_u32(smem + kVOff);
+      auto kmaj = [](uint32_t tile, int k, int rows) {
+        return make_sdesc_sw128(tile + (uint32_t(k) >> 2) * (rows * 128) + (uint32_t(k) & 3u) * 32,
+                                16, 1024);
+      };
+      // MN-major operand of 64-element chunks `chunk` bytes apart, K step k (16 rows)
+      auto mnmaj = [](uint32_t tile, int k, uint32_t chunk) {
+        return make_sdesc_sw128(tile + uint32_t(k) * 2048, chunk, 1024);
+      };
+      // S^T and dP^T of step s into buffer s % 2
+      auto mma_sdp = [&](uint32_t s) -> bool {
+        const uint32_t st = s % kQStages, b = s & 1u;
+        if (!mbar_wait(qdo_full + st, (s / kQStages) & 1u, abort_flag, p.status, kWdAttnMma))
+          return false;
+        // dQ^T of step s - 2 (same buffer) read out
+        if (s >= 2 && !mbar_wait(dq_free + b, ((s - 2) >> 1) & 1u, abort_flag, p.status,
+                                 kWdAttnMma))
+          return false;
+        tc_fence_after();
+        const uint32_t sQ = smem_u32(smem + kQOff + st * kQTile);
+        const uint32_t sDO = smem_u32(smem + kDOOff + st * kQTile);
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k)
+          umma_f16_ss(tmem + 128 * b, kmaj(sK, k, kBk), kmaj(sQ, k, kBq), id_s, k > 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k)
+          umma_f16_ss(tmem + 128 * b + 64, kmaj(sV, k, kBk), kmaj(sDO, k, kBq), id_s,
+                      k > 0 ? 1u : 0u);
+        umma_commit(st_full + b);
+        return true;
+      };
+      // dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T of step t
+      auto mma_grad = [&](uint32_t t) -> bool {
+        const uint32_t st = t % kQStages, b = t & 1u;
+        if (!mbar_wait(p_ready + b, (t >> 1) & 1u, abort_flag, p.status, kWdAttnMma)) return false;
+        tc_fence_after();
+        const uint32_t sQ = smem_u32(smem + kQOff + st * kQTile);
+        const uint32_t sDO = smem_u32(smem + kDOOff + st * kQTile);
+        const uint32_t sDS = smem_u32(smem + kDSOff + b * kDsTile);
+#pragma unroll
+        for (int k = 0; k < kBq / 16; ++k)
+          umma_f16_ts(tmem + kColDV, tmem + 128 * b + packed_col64(16 * k),
+                      mnmaj(sDO, k, kBq * 128), id_acc, (t > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < kBq / 16; ++k)
+          umma_f16_ts(tmem + kColDK, tmem + 128 * b + 64 + packed_col64(16 * k),
+                      mnmaj(sQ, k, kBq * 128), id_acc, (t > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < kBk / 16; ++k)
+          umma_f16_ss(tmem + 128 * b, mnmaj(sK, k, kBk * 128), mnmaj(sDS, k, kDsTile), id_dq,
+                      k > 0 ? 1u : 0u);
+        umma_commit(qdo_empty + st);
+        umma_commit(dq_full + b);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kWdAttnMma);
+      if (ok) ok = mma_sdp(0);
+      if (ok && n > 1) ok = mma_sdp(1);
+      for (uint32_t t = 0; ok && t < n; ++t) {
+        ok = mma_grad(t);
+        if (ok && (t & 1u)) {
+          if (t + 1 < n) ok = mma_sdp(t + 1);
+          if (ok && t + 2 < n) ok = mma_sdp(t + 2);
+        }
+      }
+      umma_commit(done);
+      int dummy = 0;
+      mbar_wait(done, 0, &dummy, p.status, kWdDrain, 100000000ull);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------------------------------------------------------- dQ read-out
+    const uint32_t q4 = warp & 3u;  // d in [32 q4, 32 q4 + 32)
+    const uint32_t la = (q4 * 32u) << 16;
+    uint8_t* stg = smem + kStgOff + q4 * 8192;
+    bool ok = true;
+    for (uint32_t t = 0; ok && t < n; ++t) {
+      const uint32_t b = t & 1u;
+      if (!(ok = mbar_wait(dq_full + b, (t >> 1) & 1u, abort_flag, p.status, kWdAttnSoftmax)))
+        break;
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld_32x32b_x32(tmem + la + 128 * b, v0);
+      tmem_ld_32x32b_x32(tmem + la + 128 * b + 32, v1);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free + b);
+      // the boxes of the previous step must have been read by their reductions
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+      // box h: rows = queries 32h .. 32h + 31, columns = this warp's 32 d
+      // (128-byte rows, 16-byte units swizzled with the row)
+      const uint32_t ub = lane >> 2, wb = (lane & 3u) * 4;
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        *reinterpret_cast<uint32_t*>(stg + q * 128 + ((ub ^ (uint32_t(q) & 7u)) * 16) + wb) = v0[q];
+        *reinterpret_cast<uint32_t*>(stg + 4096 + q * 128 + ((ub ^ (uint32_t(q) & 7u)) * 16) +
+                                     wb) = v1[q];
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t y = (i0 + t) * kBq;
+        if (!FELIX_FA_BWD_EXP_NO_DQRED) {
+          if (y < p.S) tma_reduce_add_3d(&tmDQ, stg, int(32 * q4), int(y), int(bh));
+          if (y + 32 < p.S) tma_reduce_add_3d(&tmDQ, stg + 4096, int(32 * q4), int(y + 32), int(bh));
+        }
+        bulk_commit_group();
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------------- element-wise
+    const uint32_t q4 = warp & 3u;          // TMEM lane quadrant
+    const uint32_t g = (warp - 8) >> 2;     // queries [32g, 32g + 32) of each step
+    const uint32_t r = q4 * 32 + lane;      // key row of this CTA (TMEM lane)
+    const uint32_t key = j * kBk + r;
+    const uint32_t la = (q4 * 32u) << 16;
+    const uint32_t tid = threadIdx.x - 256;
+    const bool key_ok = key < p.S;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (uint32_t s = 0; ok && s < n; ++s) {
+      const uint32_t b = s & 1u;
+      const uint32_t qb = (i0 + s) * kBq;
+      float* s_lse2 = s_vec + b * (2 * kBq);
+      float* s_delta = s_lse2 + kBq;
+      if (tid < kBq) {
+        const uint32_t q = qb + tid;
+        s_lse2[tid] = q < p.S ? __ldg(p.lse + size_t(bh) * p.S + q) * 1.4426950408889634f
+                              : INFINITY;
+      } else if (tid < 2 * kBq) {
+        const uint32_t q = qb + tid - kBq;
+        s_delta[tid - kBq] = q < p.S ? __ldg(p.delta + size_t(bh) * p.S + q) : 0.f;
+      }
+      named_barrier_sync(1, kEwWarps * 32);
+      // st_full(s) also covers every earlier MMA, so dS buffer b (last read by
+      // the dQ MMA of step s - 2) is free
+      if (!(ok = mbar_wait(st_full + b, (s >> 1) & 1u, abort_flag, p.status, kWdAttnSoftmax)))
+        break;
+      tc_fence_after();
+      uint8_t* dsrow = smem + kDSOff + b * kDsTile + r * 128;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = int(g) * 32 + h * 16;  // 16 queries
+        uint32_t sr[16], dr[16];
+        tmem_ld_32x32b_x16(tmem + la + 128 * b + c, sr);
+        tmem_ld_32x32b_x16(tmem + la + 128 * b + 64 + c, dr);
+        tmem_ld_wait();
+        uint32_t pk[8], dk[8];
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const uint32_t qi = uint32_t(c + e + x);
+            float pr = FELIX_FA_BWD_EXP_NO_EW
+                           ? __uint_as_float(sr[e + x])
+                           : ex2(fmaf(__uint_as_float(sr[e + x]), sl2, -s_lse2[qi]));
+            if (!key_ok || (p.causal && qb + qi < key)) pr = 0.f;
+            pv[x] = pr;
+            dv[x] = pr * (__uint_as_float(dr[e + x]) - s_delta[qi]);
+          }
+          pk[e / 2] = pack_half2(pv[0], pv[1]);
+          dk[e / 2] = pack_half2(dv[0], dv[1]);
+        }
+        tmem_st_32x32b_x8(tmem + la + 128 * b + packed_col64(c), pk);
+        tmem_st_32x32b_x8(tmem + la + 128 * b + 64 + packed_col64(c), dk);
+        // dS row (key r): queries c .. c + 15 = 16-byte units c / 8, c / 8 + 1
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint32_t unit = uint32_t(c / 8 + u);
+          *reinterpret_cast<uint4*>(dsrow + ((unit ^ (r & 7u)) * 16)) =
+              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+        }
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready + b);
+    }
+    // dK_j, dV_j (lane = key) -> fp16, columns [64g, 64g + 64)
+    if (ok && mbar_wait(done, 0, abort_flag, p.status, kWdAttnSoftmax)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t col = which ? kColDK : kColDV;
+        const float mul = which ? p.scale : 1.f;
+        __half* out = (which ? p.dK : p.dV) + (size_t(bh) * p.S + key) * kD;
+#pragma unroll 1
+        for (int c = int(g) * 64; c < int(g) * 64 + 64; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + la + col + c, v);
+          tmem_ld_wait();
+          if (key_ok) {
+            uint4 o4[4];
+            uint32_t* o = reinterpret_cast<uint32_t*>(o4);
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              o[e] = pack_half2(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(out + c)[e] = o4[e];
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace q64
+
 // Delta[row] = sum_d dO[row, d] * O[row, d] (fp32), one warp per row.
 __global__ void delta_kernel(const __half* __restrict__ O, const __half* __restrict__ dO,
                              float* __restrict__ delta, uint64_t rows, uint32_t D) {
@@ -417,6 +783,19 @@ namespace felix_impl {
 using namespace felix_sm100::attn_bwd;
 
 namespace {
+int configure_bwd_q64(int device) {
+  static int done[64] = {0};
+  if (device < 0 || device >= 64) return -1;
+  if (!done[device]) {
+    cudaError_t e = cudaFuncSetAttribute(q64::flash_attn_bwd_q64_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         q64::kSmemBytes);
+    if (e != cudaSuccess) return int(e);
+    done[device] = 1;
+  }
+  return 0;
+}
+
 template <int D>
 int configure_bwd(int device) {
   static int done[64] = {0};
@@ -473,11 +852,14 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
   }
 
   CUtensorMap tq, tk, tv, tdo, tdq;
-  auto enc = [&](CUtensorMap* m, const void* base) {
+  // D = 128 runs the 64-query-step kernel: Q and dO are loaded 64 rows at a time
+  const bool q64 = head_dim == 128;
+  auto enc = [&](CUtensorMap* m, const void* base, uint32_t rows) {
     return encode_tmap_3d_f16(m, base, head_dim, seqlen, bh, uint64_t(head_dim) * 2,
-                              uint64_t(seqlen) * head_dim * 2, 64, kBlk, 1);
+                              uint64_t(seqlen) * head_dim * 2, 64, rows, 1);
   };
-  if (enc(&tq, Q) || enc(&tk, K) || enc(&tv, V) || enc(&tdo, dO) ||
+  const uint32_t qrows = q64 ? uint32_t(q64::kBq) : uint32_t(kBlk);
+  if (enc(&tq, Q, qrows) || enc(&tk, K, kBlk) || enc(&tv, V, kBlk) || enc(&tdo, dO, qrows) ||
       encode_tmap_3d_f32(&tdq, dq_acc, head_dim, seqlen, bh, uint64_t(head_dim) * 4,
                          uint64_t(seqlen) * head_dim * 4, 32, 32, 1))
     return api_error("flash_attn_bwd: cuTensorMapEncodeTiled failed");
@@ -501,7 +883,11 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
   const uint64_t grid = bh * p.n_blk;
   if (grid > 0x7fffffffull) return api_error("flash_attn_bwd: grid too large");
   int rc;
-  if (head_dim == 128) {
+  if (q64) {
+    if ((rc = configure_bwd_q64(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    q64::flash_attn_bwd_q64_kernel<<<unsigned(grid), q64::kThreads, q64::kSmemBytes, stream>>>(
+        tq, tk, tv, tdo, tdq, p);
+  } else if (head_dim == 128) {
     if ((rc = configure_bwd<128>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
     flash_attn_bwd_kernel<128><<<unsigned(grid), kThreads, Cfg<128>::kSmemBytes, stream>>>(
         tq, tk, tv, tdo, tdq, p);

@@ -31,6 +31,7 @@ enum WatchdogSite : unsigned {
   kWdAttnMma = 8,
   kWdAttnSoftmax = 9,
   kWdAttnCorrection = 10,
+  kWdSmemAlign = 11,  // dynamic shared memory not 1024-byte aligned: kernel did nothing
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
