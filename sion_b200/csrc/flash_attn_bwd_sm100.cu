@@ -43,6 +43,28 @@
 #ifndef FELIX_FA_BWD_EXP_NO_EW
 #define FELIX_FA_BWD_EXP_NO_EW 0
 #endif
+// bit mask of MMA groups left out of the D = 128 kernel: 1 S^T, 2 dP^T, 4 dV,
+// 8 dK, 16 dQ^T (their commits stay, so the barrier protocol is unchanged)
+#ifndef FELIX_FA_BWD_EXP_SKIP
+#define FELIX_FA_BWD_EXP_SKIP 0
+#endif
+
+// Timing experiments only: per-role cycle counters around the waits of the
+// D = 128 kernel, summed over all CTAs (read with felix_debug_bwd_trace, which
+// exists only in such builds).
+#ifndef FELIX_FA_BWD_TRACE
+#define FELIX_FA_BWD_TRACE 0
+#endif
+#if FELIX_FA_BWD_TRACE
+__device__ unsigned long long g_bwd_trace[16];
+#define BWD_TR_BEGIN(v) const long long v = clock64()
+#define BWD_TR_ACC(acc, v) acc += clock64() - v
+#define BWD_TR_FLUSH(slot, acc) atomicAdd(&g_bwd_trace[slot], (unsigned long long)(acc))
+#else
+#define BWD_TR_BEGIN(v)
+#define BWD_TR_ACC(acc, v)
+#define BWD_TR_FLUSH(slot, acc)
+#endif
 
 namespace felix_sm100 {
 namespace attn_bwd {
@@ -388,57 +410,51 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// D = 128: 64-query steps with double-buffered S^T / dP^T, so that the
-// element-wise work and the dQ read-out of one step overlap the MMAs of the
-// neighbouring steps.
+// D = 128: 128-query steps (every MMA N = 128: narrower MMAs cost as much
+// per instruction on this tensor core) with the work of neighbouring steps
+// interleaved.
 //
-// TMEM (512 columns): buffer b in {0, 1} holds S^T at [128b, 128b + 64) and
-// dP^T at [128b + 64, 128b + 128) (lanes = the CTA's 128 keys, columns = the
-// step's 64 queries); dV at [256, 384), dK at [384, 512). dQ^T = K^T dS^T
-// (lanes = d, columns = queries) overwrites the S^T columns of its own buffer
-// right behind the dV MMA that reads P^T from them, and is read out before the
-// S^T of the step two ahead is written there.
-// MMA issue order: S/dP(0), S/dP(1), then for t = 0, 1, ...:
-//   dV/dK/dQ(t); after odd t also S/dP(t + 1), S/dP(t + 2).
-// so the read-out of dQ(t) runs behind dV/dK/dQ(t + 1) and the element-wise
-// work of step t + 1 behind the MMAs of step t.
-// Warps: 0 TMA loader, 1 MMA issuer, 4-7 dQ read-out (TMEM lane quadrant =
-// warp % 4), 8-15 element-wise (two warpgroups, 32 query columns each).
-namespace q64 {
+// TMEM (512 columns, lanes = the CTA's 128 keys unless noted):
+//   [0, 128)   S^T(i) fp32; P^T(i) fp16 packed into the first 32 columns of
+//              each 64-query half (TS operand of dV)
+//   [128, 256) dP^T(i) fp32; dS^T(i) fp16 packed the same way (TS operand of
+//              dK); then dQ(i) = dS K (lanes = queries, columns = d)
+//   [256, 384) dV, [384, 512) dK
+// MMA issue order per step i:
+//   dV(i) | S^T(i + 1) | dP^T(i) | dK(i) dQ(i)
+// with the waits: P^T(i) ready; Q(i + 1) loaded; dQ(i - 1) read out; dS(i)
+// ready. The element-wise warps run, per step:
+//   dS(i) (needs dP^T(i) and P(i), kept in registers as fp16 pairs) |
+//   P(i + 1) (needs S^T(i + 1)) | read-out of dQ(i) into the fp32 accumulator,
+// so the exponentials of step i + 1 and the dQ read-out overlap dK(i), dQ(i)
+// and dV(i + 1), S^T(i + 2).
+// Warps: 0 TMA loader, 1 MMA issuer, 4-11 element-wise: two warpgroups, each
+// one half of the queries (S/P/dS) and one half of d (dQ, dK, dV).
+namespace pipe {
 
 constexpr int kD = 128;
-constexpr int kBk = 128;  // keys per CTA
-constexpr int kBq = 64;   // queries per step
-constexpr int kThreads = 512;
+constexpr int kB = 128;  // keys per CTA, queries per step
+constexpr int kThreads = 384;
 constexpr int kEwWarps = 8;
-constexpr int kRdWarps = 4;
-constexpr int kQStages = 3;
-constexpr int kKTile = kBk * kD * 2;   // 32 KB
-constexpr int kQTile = kBq * kD * 2;   // 16 KB
-constexpr int kDsTile = kBk * kBq * 2; // 16 KB: dS, rows = keys, 64 queries per 128-byte row
+constexpr int kTile = kB * kD * 2;  // 32 KB
 constexpr int kKOff = 0;
-constexpr int kVOff = kKOff + kKTile;
-constexpr int kQOff = kVOff + kKTile;                 // [kQStages]
-constexpr int kDOOff = kQOff + kQStages * kQTile;     // [kQStages]
-constexpr int kDSOff = kDOOff + kQStages * kQTile;    // [2]
-constexpr int kStgOff = kDSOff + 2 * kDsTile;         // [kRdWarps] x two 32 x 32 fp32 boxes
-constexpr int kVecOff = kStgOff + kRdWarps * 8192;    // [2] x (lse2[64], delta[64])
-constexpr int kBarOff = kVecOff + 2 * 2 * kBq * 4;
+constexpr int kVOff = kKOff + kTile;
+constexpr int kQOff = kVOff + kTile;        // [2]
+constexpr int kDOOff = kQOff + 2 * kTile;   // [2]
+// dS (rows = keys, 64-query 128-byte chunks); after the dQ MMA has read it,
+// each element-wise warp's 4 KB of it is that warp's dQ staging box
+constexpr int kDSOff = kDOOff + 2 * kTile;
+constexpr int kVecOff = kDSOff + kB * kB * 2;  // [2] x (lse2[128], delta[128])
+constexpr int kBarOff = kVecOff + 2 * 2 * kB * 4;
 constexpr int kSmemBytes = kBarOff + 256;  // no alignment slack: checked in the kernel
 static_assert(kSmemBytes <= 232448, "shared memory");
 
-// TMEM column (within a 64-column S^T / dP^T region) of packed fp16 query q:
-// each element-wise warpgroup packs its 32 queries into the first 16 of them.
-__device__ __forceinline__ uint32_t packed_col64(int q) {
-  return uint32_t(q & ~31) + uint32_t(q & 31) / 2;
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
-    flash_attn_bwd_q64_kernel(const __grid_constant__ CUtensorMap tmQ,
-                              const __grid_constant__ CUtensorMap tmK,
-                              const __grid_constant__ CUtensorMap tmV,
-                              const __grid_constant__ CUtensorMap tmDO,
-                              const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+    flash_attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tmQ,
+                               const __grid_constant__ CUtensorMap tmK,
+                               const __grid_constant__ CUtensorMap tmV,
+                               const __grid_constant__ CUtensorMap tmDO,
+                               const __grid_constant__ CUtensorMap tmDQ, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {  // uniform over the CTA: nobody touches a barrier
     if (threadIdx.x == 0) atomicCAS(p.status, 0u, unsigned(kWdSmemAlign));
@@ -446,31 +462,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
   uint64_t* kv_full = bars;         // K_j, V_j landed
-  uint64_t* qdo_full = bars + 1;    // [3] Q_i, dO_i landed in stage i % 3
-  uint64_t* qdo_empty = bars + 4;   // [3] MMAs of step i done with stage i % 3
-  uint64_t* st_full = bars + 7;     // [2] S^T, dP^T of step i in buffer i % 2
-  uint64_t* p_ready = bars + 9;     // [2] P^T, dS^T in TMEM, dS in smem (8 warp arrivals)
-  uint64_t* dq_full = bars + 11;    // [2] dQ^T of step i in buffer i % 2
-  uint64_t* dq_free = bars + 13;    // [2] dQ^T read out (4 warp arrivals)
-  uint64_t* done = bars + 15;       // every MMA complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* qdo_full = bars + 1;    // [2] Q_i, dO_i landed in stage i % 2
+  uint64_t* qdo_empty = bars + 3;   // [2] MMAs of step i done with stage i % 2
+  uint64_t* s_full = bars + 5;      // S^T(i) in TMEM
+  uint64_t* p_ready = bars + 6;     // P^T(i) in TMEM (8 warp arrivals)
+  uint64_t* dp_full = bars + 7;     // dP^T(i) in TMEM
+  uint64_t* ds_ready = bars + 8;    // dS^T(i) in TMEM, dS(i) in smem (8 warp arrivals)
+  uint64_t* dq_full = bars + 9;     // dQ(i) in TMEM
+  uint64_t* dq_free = bars + 10;    // dQ(i) read out of TMEM (8 warp arrivals)
+  uint64_t* done = bars + 11;       // every MMA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_vec = reinterpret_cast<float*>(smem + kVecOff);
 
   const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t bh = blockIdx.x / p.n_blk;
-  const uint32_t j = blockIdx.x % p.n_blk;          // 128-key block
-  const uint32_t n_q = (p.S + kBq - 1) / kBq;       // 64-query blocks
-  const uint32_t i0 = p.causal ? 2 * j : 0;         // first query block at or after key j*128
-  const uint32_t n = n_q - i0;
+  const uint32_t j = blockIdx.x % p.n_blk;  // key block
+  const uint32_t i0 = p.causal ? j : 0;     // first query block
+  const uint32_t n = p.n_blk - i0;
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 16; ++b) {
-      uint32_t cnt = 1;
-      if (b == 9 || b == 10) cnt = kEwWarps;
-      if (b == 13 || b == 14) cnt = kRdWarps;
-      mbar_init(&bars[b], cnt);
-    }
+    for (int b = 0; b < 12; ++b)
+      mbar_init(&bars[b], (b == 6 || b == 8 || b == 10) ? kEwWarps : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -487,227 +500,284 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  constexpr uint32_t kColDV = 256, kColDK = 384;
+  constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
 
   if (warp == 0) {
     // ---------------------------------------------------------------- loader
     if (elect_one()) {
-      mbar_arrive_expect_tx(kv_full, 2 * kKTile);
+      mbar_arrive_expect_tx(kv_full, 2 * kTile);
 #pragma unroll
       for (int c = 0; c < kD / 64; ++c) {
-        tma_load_3d(smem + kKOff + c * (kBk * 128), &tmK, kv_full, 64 * c, int(j * kBk), int(bh));
-        tma_load_3d(smem + kVOff + c * (kBk * 128), &tmV, kv_full, 64 * c, int(j * kBk), int(bh));
+        tma_load_3d(smem + kKOff + c * (kB * 128), &tmK, kv_full, 64 * c, int(j * kB), int(bh));
+        tma_load_3d(smem + kVOff + c * (kB * 128), &tmV, kv_full, 64 * c, int(j * kB), int(bh));
       }
       uint32_t filled = 0;
       for (uint32_t s = 0; s < n; ++s) {
-        const uint32_t st = s % kQStages, use = s / kQStages;
-        const int q0 = int((i0 + s) * kBq);
+        const uint32_t st = s & 1u, use = s >> 1;
         if (!mbar_wait(qdo_empty + st, (use & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
-        mbar_arrive_expect_tx(qdo_full + st, 2 * kQTile);
+        mbar_arrive_expect_tx(qdo_full + st, 2 * kTile);
 #pragma unroll
         for (int c = 0; c < kD / 64; ++c) {
-          tma_load_3d(smem + kQOff + st * kQTile + c * (kBq * 128), &tmQ, qdo_full + st, 64 * c,
-                      q0, int(bh));
-          tma_load_3d(smem + kDOOff + st * kQTile + c * (kBq * 128), &tmDO, qdo_full + st,
-                      64 * c, q0, int(bh));
+          tma_load_3d(smem + kQOff + st * kTile + c * (kB * 128), &tmQ, qdo_full + st, 64 * c,
+                      int((i0 + s) * kB), int(bh));
+          tma_load_3d(smem + kDOOff + st * kTile + c * (kB * 128), &tmDO, qdo_full + st, 64 * c,
+                      int((i0 + s) * kB), int(bh));
         }
         ++filled;
       }
-      // drain: the last load of every stage has landed
+      // drain: the last load of each stage has landed
       int dummy = 0;
       mbar_wait(kv_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
-      for (uint32_t s = filled > kQStages ? filled - kQStages : 0; s < filled; ++s)
-        mbar_wait(qdo_full + s % kQStages, (s / kQStages) & 1u, &dummy, p.status, kWdDrain,
-                  100000000ull);
+      for (uint32_t s = filled > 2 ? filled - 2 : 0; s < filled; ++s)
+        mbar_wait(qdo_full + (s & 1u), (s >> 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t id_s = make_idesc_f16_f32(kBk, kBq, false, false);  // S^T, dP^T
-      const uint32_t id_acc = make_idesc_f16_f32(kBk, kD, false, true);  // dV, dK
-      const uint32_t id_dq = make_idesc_f16_f32(kD, kBq, true, true);    // dQ^T
+      const uint32_t id_st = make_idesc_f16_f32(kB, kB, false, false);  // S^T, dP^T
+      const uint32_t id_acc = make_idesc_f16_f32(kB, kD, false, true);  // dV, dK
+      const uint32_t id_dq = make_idesc_f16_f32(kB, kD, true, true);    // dQ
       const uint32_t sK = smem_u32(smem + kKOff), sV = smem_u32(smem + kVOff);
-      auto kmaj = [](uint32_t tile, int k, int rows) {
-        return make_sdesc_sw128(tile + (uint32_t(k) >> 2) * (rows * 128) + (uint32_t(k) & 3u) * 32,
-                                16, 1024);
-      };
-      // MN-major operand of 64-element chunks `chunk` bytes apart, K step k (16 rows)
-      auto mnmaj = [](uint32_t tile, int k, uint32_t chunk) {
-        return make_sdesc_sw128(tile + uint32_t(k) * 2048, chunk, 1024);
-      };
-      // S^T and dP^T of step s into buffer s % 2
-      auto mma_sdp = [&](uint32_t s) -> bool {
-        const uint32_t st = s % kQStages, b = s & 1u;
-        if (!mbar_wait(qdo_full + st, (s / kQStages) & 1u, abort_flag, p.status, kWdAttnMma))
+      const uint32_t sDS = smem_u32(smem + kDSOff);
+      long long tr_qdo = 0, tr_dqf = 0, tr_pr = 0;
+      (void)tr_qdo; (void)tr_dqf; (void)tr_pr;
+      BWD_TR_BEGIN(tr_total);
+      auto sq = [&](uint32_t s) { return smem_u32(smem + kQOff + (s & 1u) * kTile); };
+      auto sdo = [&](uint32_t s) { return smem_u32(smem + kDOOff + (s & 1u) * kTile); };
+      auto issue_s = [&](uint32_t s) -> bool {
+        BWD_TR_BEGIN(t0);
+        if (!mbar_wait(qdo_full + (s & 1u), (s >> 1) & 1u, abort_flag, p.status, kWdAttnMma))
           return false;
-        // dQ^T of step s - 2 (same buffer) read out
-        if (s >= 2 && !mbar_wait(dq_free + b, ((s - 2) >> 1) & 1u, abort_flag, p.status,
-                                 kWdAttnMma))
-          return false;
+        BWD_TR_ACC(tr_qdo, t0);
         tc_fence_after();
-        const uint32_t sQ = smem_u32(smem + kQOff + st * kQTile);
-        const uint32_t sDO = smem_u32(smem + kDOOff + st * kQTile);
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k)
-          umma_f16_ss(tmem + 128 * b, kmaj(sK, k, kBk), kmaj(sQ, k, kBq), id_s, k > 0 ? 1u : 0u);
+          if (!(FELIX_FA_BWD_EXP_SKIP & 1))
+          umma_f16_ss(tmem + kColS, kmajor<kB>(sK, k), kmajor<kB>(sq(s), k), id_st,
+                      k > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kWdAttnMma) && issue_s(0);
+      for (uint32_t i = 0; ok && i < n; ++i) {
+        BWD_TR_BEGIN(t1);
+        if (!(ok = mbar_wait(p_ready, i & 1u, abort_flag, p.status, kWdAttnMma))) break;
+        BWD_TR_ACC(tr_pr, t1);
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kB / 16; ++k)
+          if (!(FELIX_FA_BWD_EXP_SKIP & 4))
+          umma_f16_ts(tmem + kColDV, tmem + kColS + packed_col(16 * k), mnmajor(sdo(i), k),
+                      id_acc, (i > 0 || k > 0) ? 1u : 0u);
+        if (i + 1 < n && !(ok = issue_s(i + 1))) break;
+        // dQ(i - 1) sits in the dP^T columns until it has been read out
+        BWD_TR_BEGIN(t2);
+        if (i > 0 && !(ok = mbar_wait(dq_free, (i - 1) & 1u, abort_flag, p.status, kWdAttnMma)))
+          break;
+        BWD_TR_ACC(tr_dqf, t2);
+        tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k)
-          umma_f16_ss(tmem + 128 * b + 64, kmaj(sV, k, kBk), kmaj(sDO, k, kBq), id_s,
+          if (!(FELIX_FA_BWD_EXP_SKIP & 2))
+          umma_f16_ss(tmem + kColDP, kmajor<kB>(sV, k), kmajor<kB>(sdo(i), k), id_st,
                       k > 0 ? 1u : 0u);
-        umma_commit(st_full + b);
-        return true;
-      };
-      // dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T of step t
-      auto mma_grad = [&](uint32_t t) -> bool {
-        const uint32_t st = t % kQStages, b = t & 1u;
-        if (!mbar_wait(p_ready + b, (t >> 1) & 1u, abort_flag, p.status, kWdAttnMma)) return false;
+        umma_commit(dp_full);
+        BWD_TR_BEGIN(t3);
+        if (!(ok = mbar_wait(ds_ready, i & 1u, abort_flag, p.status, kWdAttnMma))) break;
+        BWD_TR_ACC(tr_pr, t3);
         tc_fence_after();
-        const uint32_t sQ = smem_u32(smem + kQOff + st * kQTile);
-        const uint32_t sDO = smem_u32(smem + kDOOff + st * kQTile);
-        const uint32_t sDS = smem_u32(smem + kDSOff + b * kDsTile);
 #pragma unroll
-        for (int k = 0; k < kBq / 16; ++k)
-          umma_f16_ts(tmem + kColDV, tmem + 128 * b + packed_col64(16 * k),
-                      mnmaj(sDO, k, kBq * 128), id_acc, (t > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < kB / 16; ++k)
+          if (!(FELIX_FA_BWD_EXP_SKIP & 8))
+          umma_f16_ts(tmem + kColDK, tmem + kColDP + packed_col(16 * k), mnmajor(sq(i), k),
+                      id_acc, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < kBq / 16; ++k)
-          umma_f16_ts(tmem + kColDK, tmem + 128 * b + 64 + packed_col64(16 * k),
-                      mnmaj(sQ, k, kBq * 128), id_acc, (t > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < kBk / 16; ++k)
-          umma_f16_ss(tmem + 128 * b, mnmaj(sK, k, kBk * 128), mnmaj(sDS, k, kDsTile), id_dq,
-                      k > 0 ? 1u : 0u);
-        umma_commit(qdo_empty + st);
-        umma_commit(dq_full + b);
-        return true;
-      };
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kWdAttnMma);
-      if (ok) ok = mma_sdp(0);
-      if (ok && n > 1) ok = mma_sdp(1);
-      for (uint32_t t = 0; ok && t < n; ++t) {
-        ok = mma_grad(t);
-        if (ok && (t & 1u)) {
-          if (t + 1 < n) ok = mma_sdp(t + 1);
-          if (ok && t + 2 < n) ok = mma_sdp(t + 2);
-        }
+        for (int k = 0; k < kB / 16; ++k)
+          if (!(FELIX_FA_BWD_EXP_SKIP & 16))
+          umma_f16_ss(tmem + kColDP, mnmajor(sDS, k), mnmajor(sK, k), id_dq, k > 0 ? 1u : 0u);
+        umma_commit(qdo_empty + (i & 1u));
+        umma_commit(dq_full);
       }
       umma_commit(done);
       int dummy = 0;
       mbar_wait(done, 0, &dummy, p.status, kWdDrain, 100000000ull);
+      long long tr_all = 0;
+      (void)tr_all;
+      BWD_TR_ACC(tr_all, tr_total);
+      BWD_TR_FLUSH(0, tr_qdo);
+      BWD_TR_FLUSH(1, tr_dqf);
+      BWD_TR_FLUSH(2, tr_pr);
+      BWD_TR_FLUSH(3, tr_all);
+      BWD_TR_FLUSH(15, 1);
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ---------------------------------------------------------------- dQ read-out
-    const uint32_t q4 = warp & 3u;  // d in [32 q4, 32 q4 + 32)
-    const uint32_t la = (q4 * 32u) << 16;
-    uint8_t* stg = smem + kStgOff + q4 * 8192;
-    bool ok = true;
-    for (uint32_t t = 0; ok && t < n; ++t) {
-      const uint32_t b = t & 1u;
-      if (!(ok = mbar_wait(dq_full + b, (t >> 1) & 1u, abort_flag, p.status, kWdAttnSoftmax)))
-        break;
-      tc_fence_after();
-      uint32_t v0[32], v1[32];
-      tmem_ld_32x32b_x32(tmem + la + 128 * b, v0);
-      tmem_ld_32x32b_x32(tmem + la + 128 * b + 32, v1);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free + b);
-      // the boxes of the previous step must have been read by their reductions
-      if (lane == 0) bulk_wait_group_read<0>();
-      __syncwarp();
-      // box h: rows = queries 32h .. 32h + 31, columns = this warp's 32 d
-      // (128-byte rows, 16-byte units swizzled with the row)
-      const uint32_t ub = lane >> 2, wb = (lane & 3u) * 4;
-#pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        *reinterpret_cast<uint32_t*>(stg + q * 128 + ((ub ^ (uint32_t(q) & 7u)) * 16) + wb) = v0[q];
-        *reinterpret_cast<uint32_t*>(stg + 4096 + q * 128 + ((ub ^ (uint32_t(q) & 7u)) * 16) +
-                                     wb) = v1[q];
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        const uint32_t y = (i0 + t) * kBq;
-        if (!FELIX_FA_BWD_EXP_NO_DQRED) {
-          if (y < p.S) tma_reduce_add_3d(&tmDQ, stg, int(32 * q4), int(y), int(bh));
-          if (y + 32 < p.S) tma_reduce_add_3d(&tmDQ, stg + 4096, int(32 * q4), int(y + 32), int(bh));
-        }
-        bulk_commit_group();
-      }
-    }
-    if (lane == 0) bulk_wait_group<0>();
-    __syncwarp();
-  } else if (warp >= 8) {
+  } else if (warp >= 4) {
     // ---------------------------------------------------------------- element-wise
-    const uint32_t q4 = warp & 3u;          // TMEM lane quadrant
-    const uint32_t g = (warp - 8) >> 2;     // queries [32g, 32g + 32) of each step
-    const uint32_t r = q4 * 32 + lane;      // key row of this CTA (TMEM lane)
-    const uint32_t key = j * kBk + r;
+    const uint32_t q4 = warp & 3u;        // TMEM lane quadrant
+    const uint32_t g = (warp - 4) >> 2;   // queries [64g, 64g + 64); d [64g, 64g + 64)
+    const uint32_t r = q4 * 32 + lane;    // key row (S/P/dS) or query row (dQ)
+    const uint32_t key = j * kB + r;
     const uint32_t la = (q4 * 32u) << 16;
-    const uint32_t tid = threadIdx.x - 256;
+    const uint32_t tid = threadIdx.x - 128;
     const bool key_ok = key < p.S;
     const float sl2 = p.scale_log2;
+    uint8_t* sDS = smem + kDSOff;
+    uint8_t* stg = sDS + (g * 4 + q4) * 4096;  // this warp's 4 KB of dS = dQ staging box
+    const int c0 = int(g) * 64;
+    // threads 0..127 fetch lse * log2(e), 128..255 Delta, one step ahead
+    auto fetch_vec = [&](uint32_t s) -> float {
+      const uint32_t q = (i0 + s) * kB + (tid & (kB - 1));
+      if (tid < kB)
+        return q < p.S ? __ldg(p.lse + size_t(bh) * p.S + q) * 1.4426950408889634f : INFINITY;
+      return q < p.S ? __ldg(p.delta + size_t(bh) * p.S + q) : 0.f;
+    };
+    float vec_next = fetch_vec(0);
+    uint32_t pk[32];  // P(i) of this thread's key row and 64 queries, fp16 pairs
     bool ok = true;
-    for (uint32_t s = 0; ok && s < n; ++s) {
-      const uint32_t b = s & 1u;
-      const uint32_t qb = (i0 + s) * kBq;
-      float* s_lse2 = s_vec + b * (2 * kBq);
-      float* s_delta = s_lse2 + kBq;
-      if (tid < kBq) {
-        const uint32_t q = qb + tid;
-        s_lse2[tid] = q < p.S ? __ldg(p.lse + size_t(bh) * p.S + q) * 1.4426950408889634f
-                              : INFINITY;
-      } else if (tid < 2 * kBq) {
-        const uint32_t q = qb + tid - kBq;
-        s_delta[tid - kBq] = q < p.S ? __ldg(p.delta + size_t(bh) * p.S + q) : 0.f;
-      }
+    long long tr_bar = 0, tr_st = 0, tr_ld = 0, tr_math = 0, tr_tst = 0, tr_sts = 0;
+    (void)tr_bar; (void)tr_st; (void)tr_ld; (void)tr_math; (void)tr_tst; (void)tr_sts;
+    BWD_TR_BEGIN(tr_total);
+
+    // P(s) = exp2(S^T * scale * log2 e - lse2): registers and TMEM (P^T operand)
+    auto p_phase = [&](uint32_t s) -> bool {
+      const uint32_t qb = (i0 + s) * kB;
+      float* s_lse2 = s_vec + (s & 1u) * (2 * kB);
+      BWD_TR_BEGIN(t0);
+      s_lse2[tid] = vec_next;  // Delta follows lse2 in the same buffer
+      if (s + 1 < n) vec_next = fetch_vec(s + 1);
       named_barrier_sync(1, kEwWarps * 32);
-      // st_full(s) also covers every earlier MMA, so dS buffer b (last read by
-      // the dQ MMA of step s - 2) is free
-      if (!(ok = mbar_wait(st_full + b, (s >> 1) & 1u, abort_flag, p.status, kWdAttnSoftmax)))
-        break;
+      BWD_TR_ACC(tr_bar, t0);
+      BWD_TR_BEGIN(t1);
+      if (!mbar_wait(s_full, s & 1u, abort_flag, p.status, kWdAttnSoftmax)) return false;
+      BWD_TR_ACC(tr_st, t1);
       tc_fence_after();
-      uint8_t* dsrow = smem + kDSOff + b * kDsTile + r * 128;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int c = int(g) * 32 + h * 16;  // 16 queries
-        uint32_t sr[16], dr[16];
-        tmem_ld_32x32b_x16(tmem + la + 128 * b + c, sr);
-        tmem_ld_32x32b_x16(tmem + la + 128 * b + 64 + c, dr);
+        const int c = c0 + 32 * h;
+        uint32_t sr[32];
+        tmem_ld_32x32b_x32(tmem + la + kColS + c, sr);
         tmem_ld_wait();
-        uint32_t pk[8], dk[8];
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          float pv[2], dv[2];
+        for (int e = 0; e < 32; e += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(s_lse2 + c + e);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+          float pv[4];
 #pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            const uint32_t qi = uint32_t(c + e + x);
-            float pr = FELIX_FA_BWD_EXP_NO_EW
-                           ? __uint_as_float(sr[e + x])
-                           : ex2(fmaf(__uint_as_float(sr[e + x]), sl2, -s_lse2[qi]));
-            if (!key_ok || (p.causal && qb + qi < key)) pr = 0.f;
+          for (int x = 0; x < 4; ++x) {
+            float pr = ex2(fmaf(__uint_as_float(sr[e + x]), sl2, -lv[x]));
+            if (!key_ok || (p.causal && qb + uint32_t(c + e + x) < key)) pr = 0.f;
             pv[x] = pr;
-            dv[x] = pr * (__uint_as_float(dr[e + x]) - s_delta[qi]);
           }
-          pk[e / 2] = pack_half2(pv[0], pv[1]);
-          dk[e / 2] = pack_half2(dv[0], dv[1]);
-        }
-        tmem_st_32x32b_x8(tmem + la + 128 * b + packed_col64(c), pk);
-        tmem_st_32x32b_x8(tmem + la + 128 * b + 64 + packed_col64(c), dk);
-        // dS row (key r): queries c .. c + 15 = 16-byte units c / 8, c / 8 + 1
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const uint32_t unit = uint32_t(c / 8 + u);
-          *reinterpret_cast<uint4*>(dsrow + ((unit ^ (r & 7u)) * 16)) =
-              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+          pk[16 * h + e / 2] = pack_half2(pv[0], pv[1]);
+          pk[16 * h + e / 2 + 1] = pack_half2(pv[2], pv[3]);
         }
       }
+      // packed P^T: this warpgroup's 64 queries into its first 32 columns
+      // (columns it has already read)
+      tmem_st_32x32b_x16(tmem + la + kColS + packed_col(c0), *reinterpret_cast<uint32_t(*)[16]>(pk));
+      tmem_st_32x32b_x16(tmem + la + kColS + packed_col(c0) + 16,
+                         *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      return true;
+    };
+
+    ok = p_phase(0);
+    for (uint32_t i = 0; ok && i < n; ++i) {
+      // ---- dS(i) = P(i) * (dP^T(i) - Delta)
+      const float* s_delta = s_vec + (i & 1u) * (2 * kB) + kB;
+      BWD_TR_BEGIN(t1);
+      if (!(ok = mbar_wait(dp_full, i & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
+      BWD_TR_ACC(tr_st, t1);
+      tc_fence_after();
+      // the dS writes reuse the staging box: its reductions must have read it
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+      BWD_TR_BEGIN(t2);
+      uint32_t dk[32];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = c0 + 32 * h;
+        uint32_t dr[32];
+        tmem_ld_32x32b_x32(tmem + la + kColDP + c, dr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const float4 d4 = *reinterpret_cast<const float4*>(s_delta + c + e);
+          const float2 p01 = __half22float2(*reinterpret_cast<const __half2*>(&pk[16 * h + e / 2]));
+          const float2 p23 =
+              __half22float2(*reinterpret_cast<const __half2*>(&pk[16 * h + e / 2 + 1]));
+          dk[16 * h + e / 2] = pack_half2(p01.x * (__uint_as_float(dr[e]) - d4.x),
+                                          p01.y * (__uint_as_float(dr[e + 1]) - d4.y));
+          dk[16 * h + e / 2 + 1] = pack_half2(p23.x * (__uint_as_float(dr[e + 2]) - d4.z),
+                                              p23.y * (__uint_as_float(dr[e + 3]) - d4.w));
+        }
+      }
+      BWD_TR_ACC(tr_math, t2);
+      BWD_TR_BEGIN(t3);
+      tmem_st_32x32b_x16(tmem + la + kColDP + packed_col(c0), *reinterpret_cast<uint32_t(*)[16]>(dk));
+      tmem_st_32x32b_x16(tmem + la + kColDP + packed_col(c0) + 16,
+                         *reinterpret_cast<uint32_t(*)[16]>(dk + 16));
+      // dS (queries x keys) as an MN-major A tile: query chunk g, row = key r,
+      // 16-byte units swizzled with the row (128-byte swizzle)
+      uint8_t* row = sDS + g * (kB * 128) + r * 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4*>(row + ((uint32_t(u) ^ (r & 7u)) * 16)) =
+            make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready + b);
+      BWD_TR_ACC(tr_tst, t3);
+      if (lane == 0) mbar_arrive(ds_ready);
+      // ---- P(i + 1)
+      if (i + 1 < n && !(ok = p_phase(i + 1))) break;
+      // ---- dQ(i) (lane = query, columns d [64g, 64g + 64)) -> staged 32 x 32
+      // boxes -> TMA reduction into the fp32 accumulator
+      BWD_TR_BEGIN(t4);
+      if (!(ok = mbar_wait(dq_full, i & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
+      BWD_TR_ACC(tr_sts, t4);
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld_32x32b_x32(tmem + la + kColDP + c0, v0);
+      tmem_ld_32x32b_x32(tmem + la + kColDP + c0 + 32, v1);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      const uint32_t q0 = (i0 + i) * kB + q4 * 32;
+#pragma unroll
+      for (int bx = 0; bx < 2; ++bx) {
+        const uint32_t(&v)[32] = bx ? v1 : v0;
+        if (bx) {
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((uint32_t(u) ^ (lane & 7u)) * 16)) =
+              make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (q0 < p.S && !FELIX_FA_BWD_EXP_NO_DQRED)
+            tma_reduce_add_3d(&tmDQ, stg, c0 + 32 * bx, int(q0), int(bh));
+          bulk_commit_group();
+        }
+      }
+    }
+    if (lane == 0 && warp == 4) {
+      long long tr_all = 0;
+      (void)tr_all;
+      BWD_TR_ACC(tr_all, tr_total);
+      BWD_TR_FLUSH(4, tr_bar);
+      BWD_TR_FLUSH(5, tr_st);
+      BWD_TR_FLUSH(6, tr_all);
+      BWD_TR_FLUSH(11, tr_math);
+      BWD_TR_FLUSH(12, tr_tst);
+      BWD_TR_FLUSH(13, tr_sts);
     }
     // dK_j, dV_j (lane = key) -> fp16, columns [64g, 64g + 64)
     if (ok && mbar_wait(done, 0, abort_flag, p.status, kWdAttnSoftmax)) {
@@ -718,7 +788,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mul = which ? p.scale : 1.f;
         __half* out = (which ? p.dK : p.dV) + (size_t(bh) * p.S + key) * kD;
 #pragma unroll 1
-        for (int c = int(g) * 64; c < int(g) * 64 + 64; c += 32) {
+        for (int c = c0; c < c0 + 64; c += 32) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem + la + col + c, v);
           tmem_ld_wait();
@@ -734,6 +804,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // every staged reduction complete before the shared memory goes away
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -745,7 +818,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-}  // namespace q64
+}  // namespace pipe
 
 // Delta[row] = sum_d dO[row, d] * O[row, d] (fp32), one warp per row.
 __global__ void delta_kernel(const __half* __restrict__ O, const __half* __restrict__ dO,
@@ -783,13 +856,13 @@ namespace felix_impl {
 using namespace felix_sm100::attn_bwd;
 
 namespace {
-int configure_bwd_q64(int device) {
+int configure_bwd_pipe(int device) {
   static int done[64] = {0};
   if (device < 0 || device >= 64) return -1;
   if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(q64::flash_attn_bwd_q64_kernel,
+    cudaError_t e = cudaFuncSetAttribute(pipe::flash_attn_bwd_pipe_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         q64::kSmemBytes);
+                                         pipe::kSmemBytes);
     if (e != cudaSuccess) return int(e);
     done[device] = 1;
   }
@@ -852,14 +925,12 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
   }
 
   CUtensorMap tq, tk, tv, tdo, tdq;
-  // D = 128 runs the 64-query-step kernel: Q and dO are loaded 64 rows at a time
-  const bool q64 = head_dim == 128;
+  const bool pipelined = head_dim == 128;
   auto enc = [&](CUtensorMap* m, const void* base, uint32_t rows) {
     return encode_tmap_3d_f16(m, base, head_dim, seqlen, bh, uint64_t(head_dim) * 2,
                               uint64_t(seqlen) * head_dim * 2, 64, rows, 1);
   };
-  const uint32_t qrows = q64 ? uint32_t(q64::kBq) : uint32_t(kBlk);
-  if (enc(&tq, Q, qrows) || enc(&tk, K, kBlk) || enc(&tv, V, kBlk) || enc(&tdo, dO, qrows) ||
+  if (enc(&tq, Q, kBlk) || enc(&tk, K, kBlk) || enc(&tv, V, kBlk) || enc(&tdo, dO, kBlk) ||
       encode_tmap_3d_f32(&tdq, dq_acc, head_dim, seqlen, bh, uint64_t(head_dim) * 4,
                          uint64_t(seqlen) * head_dim * 4, 32, 32, 1))
     return api_error("flash_attn_bwd: cuTensorMapEncodeTiled failed");
@@ -883,10 +954,11 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
   const uint64_t grid = bh * p.n_blk;
   if (grid > 0x7fffffffull) return api_error("flash_attn_bwd: grid too large");
   int rc;
-  if (q64) {
-    if ((rc = configure_bwd_q64(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    q64::flash_attn_bwd_q64_kernel<<<unsigned(grid), q64::kThreads, q64::kSmemBytes, stream>>>(
-        tq, tk, tv, tdo, tdq, p);
+  if (pipelined) {
+    if ((rc = configure_bwd_pipe(dev->ordinal)))
+      return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    pipe::flash_attn_bwd_pipe_kernel<<<unsigned(grid), pipe::kThreads, pipe::kSmemBytes,
+                                       stream>>>(tq, tk, tv, tdo, tdq, p);
   } else if (head_dim == 128) {
     if ((rc = configure_bwd<128>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
     flash_attn_bwd_kernel<128><<<unsigned(grid), kThreads, Cfg<128>::kSmemBytes, stream>>>(
@@ -903,3 +975,16 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
 }
 
 }  // namespace felix_impl
+
+#if FELIX_FA_BWD_TRACE
+extern "C" int felix_debug_bwd_trace(unsigned long long* out16, int clear) {
+  if (cudaMemcpyFromSymbol(out16, g_bwd_trace,
+                           sizeof(unsigned long long) * 16) != cudaSuccess)
+    return 1;
+  if (clear) {
+    unsigned long long z[16] = {0};
+    cudaMemcpyToSymbol(g_bwd_trace, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
