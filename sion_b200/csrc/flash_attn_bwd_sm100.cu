@@ -428,21 +428,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   P(i + 1) (needs S^T(i + 1)) | read-out of dQ(i) into the fp32 accumulator,
 // so the exponentials of step i + 1 and the dQ read-out overlap dK(i), dQ(i)
 // and dV(i + 1), S^T(i + 2).
-// dQ(i) leaves TMEM as 32 x 32 fp32 boxes staged in shared memory for TMA
-// reductions: half of them in the dS tile (which the dQ MMA has finished
-// with), half in the dO(i) stage buffer (which dP(i) has finished with); the
-// element-wise warps overwrite dS, and the loader refills that dO stage, only
-// after the read-out warps report that their reductions have read the boxes.
 // Warps: 0 TMA loader, 1 MMA issuer, 4-11 element-wise: two warpgroups, each
-// one half of the queries (S/P/dS) and one half of d (dK, dV); 12-15 dQ
-// read-out (TMEM lane quadrant = warp % 4).
+// one half of the queries (S/P/dS) and one half of d (dQ, dK, dV).
 namespace pipe {
 
 constexpr int kD = 128;
 constexpr int kB = 128;  // keys per CTA, queries per step
-constexpr int kThreads = 512;
+constexpr int kThreads = 384;
 constexpr int kEwWarps = 8;
-constexpr int kRdWarps = 4;
 constexpr int kTile = kB * kD * 2;  // 32 KB
 constexpr int kKOff = 0;
 constexpr int kVOff = kKOff + kTile;
@@ -469,8 +462,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
   uint64_t* kv_full = bars;         // K_j, V_j landed
-  uint64_t* q_full = bars + 1;      // [2] Q_i landed in stage i % 2
-  uint64_t* q_empty = bars + 3;     // [2] MMAs of step i done with Q stage i % 2
+  uint64_t* qdo_full = bars + 1;    // [2] Q_i, dO_i landed in stage i % 2
+  uint64_t* qdo_empty = bars + 3;   // [2] MMAs of step i done with stage i % 2
   uint64_t* s_full = bars + 5;      // S^T(i) in TMEM
   uint64_t* p_ready = bars + 6;     // P^T(i) in TMEM (8 warp arrivals)
   uint64_t* dp_full = bars + 7;     // dP^T(i) in TMEM
@@ -478,11 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_full = bars + 9;     // dQ(i) in TMEM
   uint64_t* dq_free = bars + 10;    // dQ(i) read out of TMEM (8 warp arrivals)
   uint64_t* done = bars + 11;       // every MMA complete
-  uint64_t* do_full = bars + 12;    // [2] dO_i landed in stage i % 2
-  uint64_t* do_free = bars + 14;    // [2] dO stage i % 2 free: MMAs done, staged dQ(i) read
-                                    //     by its reductions (4 read-out warp arrivals)
-  uint64_t* stg_free = bars + 16;   // dQ(i) boxes in the dS tile read (4 read-out warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_vec = reinterpret_cast<float*>(smem + kVecOff);
 
@@ -493,12 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t n = p.n_blk - i0;
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 17; ++b) {
-      uint32_t cnt = 1;
-      if (b == 6 || b == 8) cnt = kEwWarps;                          // p_ready, ds_ready
-      if (b == 10 || b == 14 || b == 15 || b == 16) cnt = kRdWarps;  // dq_free, do_free, stg_free
-      mbar_init(&bars[b], cnt);
-    }
+    for (int b = 0; b < 12; ++b)
+      mbar_init(&bars[b], (b == 6 || b == 8 || b == 10) ? kEwWarps : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -529,30 +514,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t filled = 0;
       for (uint32_t s = 0; s < n; ++s) {
         const uint32_t st = s & 1u, use = s >> 1;
-        if (!mbar_wait(q_empty + st, (use & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
-        mbar_arrive_expect_tx(q_full + st, kTile);
+        if (!mbar_wait(qdo_empty + st, (use & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
+        mbar_arrive_expect_tx(qdo_full + st, 2 * kTile);
 #pragma unroll
-        for (int c = 0; c < kD / 64; ++c)
-          tma_load_3d(smem + kQOff + st * kTile + c * (kB * 128), &tmQ, q_full + st, 64 * c,
+        for (int c = 0; c < kD / 64; ++c) {
+          tma_load_3d(smem + kQOff + st * kTile + c * (kB * 128), &tmQ, qdo_full + st, 64 * c,
                       int((i0 + s) * kB), int(bh));
-        if (!mbar_wait(do_free + st, (use & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) {
-          mbar_wait(q_full + st, use & 1u, abort_flag, p.status, kWdDrain, 100000000ull);
-          break;
+          tma_load_3d(smem + kDOOff + st * kTile + c * (kB * 128), &tmDO, qdo_full + st, 64 * c,
+                      int((i0 + s) * kB), int(bh));
         }
-        mbar_arrive_expect_tx(do_full + st, kTile);
-#pragma unroll
-        for (int c = 0; c < kD / 64; ++c)
-          tma_load_3d(smem + kDOOff + st * kTile + c * (kB * 128), &tmDO, do_full + st, 64 * c,
-                      int((i0 + s) * kB), int(bh));
         ++filled;
       }
-      // drain: the last loads of each stage have landed
+      // drain: the last load of each stage has landed
       int dummy = 0;
       mbar_wait(kv_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
-      for (uint32_t s = filled > 2 ? filled - 2 : 0; s < filled; ++s) {
-        mbar_wait(q_full + (s & 1u), (s >> 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
-        mbar_wait(do_full + (s & 1u), (s >> 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
-      }
+      for (uint32_t s = filled > 2 ? filled - 2 : 0; s < filled; ++s)
+        mbar_wait(qdo_full + (s & 1u), (s >> 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -569,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto sdo = [&](uint32_t s) { return smem_u32(smem + kDOOff + (s & 1u) * kTile); };
       auto issue_s = [&](uint32_t s) -> bool {
         BWD_TR_BEGIN(t0);
-        if (!mbar_wait(q_full + (s & 1u), (s >> 1) & 1u, abort_flag, p.status, kWdAttnMma))
+        if (!mbar_wait(qdo_full + (s & 1u), (s >> 1) & 1u, abort_flag, p.status, kWdAttnMma))
           return false;
         BWD_TR_ACC(tr_qdo, t0);
         tc_fence_after();
@@ -586,11 +563,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         BWD_TR_BEGIN(t1);
         if (!(ok = mbar_wait(p_ready, i & 1u, abort_flag, p.status, kWdAttnMma))) break;
         BWD_TR_ACC(tr_pr, t1);
-        BWD_TR_BEGIN(t1b);
-        if (!(ok = mbar_wait(do_full + (i & 1u), (i >> 1) & 1u, abort_flag, p.status,
-                             kWdAttnMma)))
-          break;
-        BWD_TR_ACC(tr_qdo, t1b);
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kB / 16; ++k)
@@ -623,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < kB / 16; ++k)
           if (!(FELIX_FA_BWD_EXP_SKIP & 16))
           umma_f16_ss(tmem + kColDP, mnmajor(sDS, k), mnmajor(sK, k), id_dq, k > 0 ? 1u : 0u);
-        umma_commit(q_empty + (i & 1u));
+        umma_commit(qdo_empty + (i & 1u));
         umma_commit(dq_full);
       }
       umma_commit(done);
@@ -638,82 +610,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       BWD_TR_FLUSH(3, tr_all);
       BWD_TR_FLUSH(15, 1);
     }
-  } else if (warp >= 12) {
-    // ---------------------------------------------------------------- dQ read-out
-    // lanes = queries 32 q4 .. 32 q4 + 31, all 128 d: four 32 x 32 fp32 boxes,
-    // staged in shared memory (boxes 0, 1 in the dS tile, which the dQ MMA has
-    // finished with; boxes 2, 3 in the dO stage of the step, which dP has
-    // finished with) and added to the fp32 accumulator by TMA reductions
-    const uint32_t q4 = warp & 3u;
-    const uint32_t la = (q4 * 32u) << 16;
-    bool ok = true;
-    long long tr_w = 0, tr_rd = 0;
-    (void)tr_w; (void)tr_rd;
-    for (uint32_t i = 0; ok && i < n; ++i) {
-      BWD_TR_BEGIN(t0);
-      if (!(ok = mbar_wait(dq_full, i & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
-      BWD_TR_ACC(tr_w, t0);
-      BWD_TR_BEGIN(t1);
-      tc_fence_after();
-      const uint32_t q0 = (i0 + i) * kB + q4 * 32;
-#pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        uint32_t v0[32], v1[32];
-        tmem_ld_32x32b_x32(tmem + la + kColDP + 64 * hb, v0);
-        tmem_ld_32x32b_x32(tmem + la + kColDP + 64 * hb + 32, v1);
-        tmem_ld_wait();
-        if (hb == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(dq_free);
-        }
-        uint8_t* base = hb == 0 ? smem + kDSOff : smem + kDOOff + (i & 1u) * kTile;
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const uint32_t(&v)[32] = x ? v1 : v0;
-          uint8_t* box = base + (x * 4 + q4) * 4096;
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            *reinterpret_cast<uint4*>(box + lane * 128 + ((uint32_t(u) ^ (lane & 7u)) * 16)) =
-                make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        if (q0 < p.S && !FELIX_FA_BWD_EXP_NO_DQRED) {
-#pragma unroll
-          for (int b4 = 0; b4 < 4; ++b4) {
-            uint8_t* base = b4 < 2 ? smem + kDSOff : smem + kDOOff + (i & 1u) * kTile;
-            tma_reduce_add_3d(&tmDQ, base + ((b4 & 1) * 4 + q4) * 4096, 32 * b4, int(q0),
-                              int(bh));
-          }
-        }
-        bulk_commit_group();
-        bulk_wait_group_read<0>();
-        mbar_arrive(stg_free);
-        mbar_arrive(do_free + (i & 1u));
-      }
-      __syncwarp();
-      BWD_TR_ACC(tr_rd, t1);
-    }
-    if (lane == 0) bulk_wait_group<0>();
-    __syncwarp();
-    if (lane == 0 && q4 == 0) {
-      BWD_TR_FLUSH(7, tr_w);
-      BWD_TR_FLUSH(14, tr_rd);
-    }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- element-wise
     const uint32_t q4 = warp & 3u;        // TMEM lane quadrant
     const uint32_t g = (warp - 4) >> 2;   // queries [64g, 64g + 64); d [64g, 64g + 64)
-    const uint32_t r = q4 * 32 + lane;    // key row
+    const uint32_t r = q4 * 32 + lane;    // key row (S/P/dS) or query row (dQ)
     const uint32_t key = j * kB + r;
     const uint32_t la = (q4 * 32u) << 16;
     const uint32_t tid = threadIdx.x - 128;
     const bool key_ok = key < p.S;
     const float sl2 = p.scale_log2;
     uint8_t* sDS = smem + kDSOff;
+    uint8_t* stg = sDS + (g * 4 + q4) * 4096;  // this warp's 4 KB of dS = dQ staging box
     const int c0 = int(g) * 64;
     // threads 0..127 fetch lse * log2(e), 128..255 Delta, one step ahead
     auto fetch_vec = [&](uint32_t s) -> float {
@@ -725,14 +633,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float vec_next = fetch_vec(0);
     uint32_t pk[32];  // P(i) of this thread's key row and 64 queries, fp16 pairs
     bool ok = true;
-    long long tr_bar = 0, tr_st = 0, tr_ld = 0, tr_math = 0;
-    (void)tr_bar; (void)tr_st; (void)tr_ld; (void)tr_math;
+    long long tr_bar = 0, tr_st = 0, tr_ld = 0, tr_math = 0, tr_tst = 0, tr_sts = 0;
+    (void)tr_bar; (void)tr_st; (void)tr_ld; (void)tr_math; (void)tr_tst; (void)tr_sts;
     BWD_TR_BEGIN(tr_total);
 
-    // P(s) = exp2(S^T * scale * log2 e - lse2): registers and TMEM (P^T operand).
-    // Packed P^T of this warpgroup's 64 queries goes to its first 32 columns;
-    // the half stored after reading columns [c, c + 32) lands in columns
-    // already read.
+    // P(s) = exp2(S^T * scale * log2 e - lse2): registers and TMEM (P^T operand)
     auto p_phase = [&](uint32_t s) -> bool {
       const uint32_t qb = (i0 + s) * kB;
       float* s_lse2 = s_vec + (s & 1u) * (2 * kB);
@@ -745,7 +650,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(s_full, s & 1u, abort_flag, p.status, kWdAttnSoftmax)) return false;
       BWD_TR_ACC(tr_st, t1);
       tc_fence_after();
-      BWD_TR_BEGIN(t2);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = c0 + 32 * h;
@@ -766,13 +670,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk[16 * h + e / 2] = pack_half2(pv[0], pv[1]);
           pk[16 * h + e / 2 + 1] = pack_half2(pv[2], pv[3]);
         }
-        tmem_st_32x32b_x16(tmem + la + kColS + packed_col(c0) + 16 * h,
-                           *reinterpret_cast<uint32_t(*)[16]>(pk + 16 * h));
       }
+      // packed P^T: this warpgroup's 64 queries into its first 32 columns
+      // (columns it has already read)
+      tmem_st_32x32b_x16(tmem + la + kColS + packed_col(c0), *reinterpret_cast<uint32_t(*)[16]>(pk));
+      tmem_st_32x32b_x16(tmem + la + kColS + packed_col(c0) + 16,
+                         *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      BWD_TR_ACC(tr_ld, t2);
       if (lane == 0) mbar_arrive(p_ready);
       return true;
     };
@@ -783,18 +689,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* s_delta = s_vec + (i & 1u) * (2 * kB) + kB;
       BWD_TR_BEGIN(t1);
       if (!(ok = mbar_wait(dp_full, i & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
-      // the dS tile held dQ(i - 1) staging boxes: their reductions must have read them
-      if (i > 0 && !(ok = mbar_wait(stg_free, (i - 1) & 1u, abort_flag, p.status,
-                                    kWdAttnSoftmax)))
-        break;
       BWD_TR_ACC(tr_st, t1);
       tc_fence_after();
+      // the dS writes reuse the staging box: its reductions must have read it
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
       BWD_TR_BEGIN(t2);
-      uint8_t* row = sDS + g * (kB * 128) + r * 128;
+      uint32_t dk[32];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = c0 + 32 * h;
-        uint32_t dr[32], dk[16];
+        uint32_t dr[32];
         tmem_ld_32x32b_x32(tmem + la + kColDP + c, dr);
         tmem_ld_wait();
 #pragma unroll
@@ -803,28 +708,65 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float2 p01 = __half22float2(*reinterpret_cast<const __half2*>(&pk[16 * h + e / 2]));
           const float2 p23 =
               __half22float2(*reinterpret_cast<const __half2*>(&pk[16 * h + e / 2 + 1]));
-          dk[e / 2] = pack_half2(p01.x * (__uint_as_float(dr[e]) - d4.x),
-                                 p01.y * (__uint_as_float(dr[e + 1]) - d4.y));
-          dk[e / 2 + 1] = pack_half2(p23.x * (__uint_as_float(dr[e + 2]) - d4.z),
-                                     p23.y * (__uint_as_float(dr[e + 3]) - d4.w));
+          dk[16 * h + e / 2] = pack_half2(p01.x * (__uint_as_float(dr[e]) - d4.x),
+                                          p01.y * (__uint_as_float(dr[e + 1]) - d4.y));
+          dk[16 * h + e / 2 + 1] = pack_half2(p23.x * (__uint_as_float(dr[e + 2]) - d4.z),
+                                              p23.y * (__uint_as_float(dr[e + 3]) - d4.w));
         }
-        // packed dS^T (TMEM A operand of dK), into columns already read
-        tmem_st_32x32b_x16(tmem + la + kColDP + packed_col(c0) + 16 * h, dk);
-        // dS (queries x keys) as an MN-major A tile: query chunk g, row = key r,
-        // 16-byte units 4h .. 4h + 3 swizzled with the row (128-byte swizzle)
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(row + ((uint32_t(4 * h + u) ^ (r & 7u)) * 16)) =
-              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
       }
+      BWD_TR_ACC(tr_math, t2);
+      BWD_TR_BEGIN(t3);
+      tmem_st_32x32b_x16(tmem + la + kColDP + packed_col(c0), *reinterpret_cast<uint32_t(*)[16]>(dk));
+      tmem_st_32x32b_x16(tmem + la + kColDP + packed_col(c0) + 16,
+                         *reinterpret_cast<uint32_t(*)[16]>(dk + 16));
+      // dS (queries x keys) as an MN-major A tile: query chunk g, row = key r,
+      // 16-byte units swizzled with the row (128-byte swizzle)
+      uint8_t* row = sDS + g * (kB * 128) + r * 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4*>(row + ((uint32_t(u) ^ (r & 7u)) * 16)) =
+            make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      BWD_TR_ACC(tr_math, t2);
+      BWD_TR_ACC(tr_tst, t3);
       if (lane == 0) mbar_arrive(ds_ready);
       // ---- P(i + 1)
       if (i + 1 < n && !(ok = p_phase(i + 1))) break;
+      // ---- dQ(i) (lane = query, columns d [64g, 64g + 64)) -> staged 32 x 32
+      // boxes -> TMA reduction into the fp32 accumulator
+      BWD_TR_BEGIN(t4);
+      if (!(ok = mbar_wait(dq_full, i & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
+      BWD_TR_ACC(tr_sts, t4);
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld_32x32b_x32(tmem + la + kColDP + c0, v0);
+      tmem_ld_32x32b_x32(tmem + la + kColDP + c0 + 32, v1);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      const uint32_t q0 = (i0 + i) * kB + q4 * 32;
+#pragma unroll
+      for (int bx = 0; bx < 2; ++bx) {
+        const uint32_t(&v)[32] = bx ? v1 : v0;
+        if (bx) {
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((uint32_t(u) ^ (lane & 7u)) * 16)) =
+              make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (q0 < p.S && !FELIX_FA_BWD_EXP_NO_DQRED)
+            tma_reduce_add_3d(&tmDQ, stg, c0 + 32 * bx, int(q0), int(bh));
+          bulk_commit_group();
+        }
+      }
     }
     if (lane == 0 && warp == 4) {
       long long tr_all = 0;
@@ -833,8 +775,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       BWD_TR_FLUSH(4, tr_bar);
       BWD_TR_FLUSH(5, tr_st);
       BWD_TR_FLUSH(6, tr_all);
-      BWD_TR_FLUSH(10, tr_ld);
       BWD_TR_FLUSH(11, tr_math);
+      BWD_TR_FLUSH(12, tr_tst);
+      BWD_TR_FLUSH(13, tr_sts);
     }
     // dK_j, dV_j (lane = key) -> fp16, columns [64g, 64g + 64)
     if (ok && mbar_wait(done, 0, abort_flag, p.status, kWdAttnSoftmax)) {
@@ -861,6 +804,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // every staged reduction complete before the shared memory goes away
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
