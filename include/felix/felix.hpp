@@ -41,6 +41,17 @@ FelixStatus flash_attn_fwd_lse_launch(half* Q, half* K, half* V, half* O, float*
                                       uint32_t heads, uint32_t batch_size, uint32_t QKV_seqlen,
                                       cudaStream_t stream, bool causal = false);
 
+// new: attention backward. Given Q, K, V, the forward output O and its LSE
+// (from flash_attn_fwd_lse_launch) and dO, writes dQ, dK, dV (all fp16
+// [batch, heads, seqlen, HEAD_DIM]). Library-owned fp32 scratch (dQ
+// accumulator, per-row dO.O) is allocated on first use per device and stream.
+// No reference counterpart: the reference has a forward operator only.
+template <int HEAD_DIM>
+FelixStatus flash_attn_bwd_launch(const half* Q, const half* K, const half* V, const half* O,
+                                  const half* dO, const float* lse, half* dQ, half* dK, half* dV,
+                                  uint32_t heads, uint32_t batch_size, uint32_t QKV_seqlen,
+                                  cudaStream_t stream, bool causal = false);
+
 // new: reads (and clears) the device watchdog word; KERNEL_RUNTIME_ERROR when a
 // bounded wait inside a kernel gave up. Synchronises the device.
 FelixStatus check_watchdog();

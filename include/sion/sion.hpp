@@ -21,5 +21,11 @@ std::tuple<torch::Tensor, torch::Tensor> flash_attention_lse(const torch::Tensor
                                                              const torch::Tensor& key,
                                                              const torch::Tensor& value,
                                                              bool causal = false);
+// new: gradients (dQ, dK, dV) of flash_attention given its inputs, the forward
+// output O and LSE (from flash_attention_lse) and the output gradient dO
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> flash_attention_backward(
+    const torch::Tensor& query, const torch::Tensor& key, const torch::Tensor& value,
+    const torch::Tensor& out, const torch::Tensor& lse, const torch::Tensor& grad_out,
+    bool causal = false);
 
 }  // namespace sion

@@ -9,6 +9,8 @@ Python surface (mirrors the reference module ``sion``, python/binding.cpp:6-11):
     gemm(A, B, alpha=1, beta=0)         dispatch on dtype
     flash_attention(Q, K, V)            fp16 [B,H,S,D], D in {64,128}
     flash_attention_lse(Q, K, V)        -> (O, fp32 LSE [B,H,S])
+    flash_attention_backward(Q, K, V, O, LSE, dO) -> (dQ, dK, dV)
+    flash_attention_autograd(Q, K, V)   differentiable forward (torch.autograd)
 
 These come from the native module ``_sion`` (LibTorch C++), which calls the
 felix:: C++ API in ``libfelix_b200.so``. The C ABI of that library
@@ -68,5 +70,43 @@ def flash_attention_lse(query, key, value, causal: bool = False):
     return _load_ext().flash_attention_lse(query, key, value, causal)
 
 
+def flash_attention_backward(query, key, value, out, lse, grad_out, causal: bool = False):
+    """(dQ, dK, dV) of flash_attention given the forward's O and LSE."""
+    return _load_ext().flash_attention_backward(query, key, value, out, lse, grad_out, causal)
+
+
+def _autograd_function():
+    import torch
+
+    class FlashAttentionFunction(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, query, key, value, causal):
+            out, lse = flash_attention_lse(query, key, value, causal)
+            ctx.save_for_backward(query, key, value, out, lse)
+            ctx.causal = causal
+            return out
+
+        @staticmethod
+        def backward(ctx, grad_out):
+            q, k, v, out, lse = ctx.saved_tensors
+            dq, dk, dv = flash_attention_backward(q, k, v, out, lse, grad_out.contiguous(),
+                                                  ctx.causal)
+            return dq, dk, dv, None
+
+    return FlashAttentionFunction
+
+
+_FA_FN = None
+
+
+def flash_attention_autograd(query, key, value, causal: bool = False):
+    """flash_attention that torch.autograd can differentiate (the backward runs
+    the sm_100a backward kernel)."""
+    global _FA_FN
+    if _FA_FN is None:
+        _FA_FN = _autograd_function()
+    return _FA_FN.apply(query, key, value, causal)
+
+
 __all__ = ["sgemm", "hgemm", "hgemm_nt", "gemm", "flash_attention", "flash_attention_lse",
-           "LIB_PATH"]
+           "flash_attention_backward", "flash_attention_autograd", "LIB_PATH"]

@@ -212,6 +212,24 @@ FelixStatus flash_attn_fwd_lse_launch<128, 64>(half* Q, half* K, half* V, half* 
                                         0.0f, causal ? 1 : 0, stream));
 }
 
+template <>
+FelixStatus flash_attn_bwd_launch<64>(const half* Q, const half* K, const half* V, const half* O,
+                                      const half* dO, const float* lse, half* dQ, half* dK,
+                                      half* dV, uint32_t heads, uint32_t batch_size,
+                                      uint32_t QKV_seqlen, cudaStream_t stream, bool causal) {
+  return from_c(felix_flash_attn_bwd(Q, K, V, O, dO, lse, dQ, dK, dV, heads, batch_size,
+                                     QKV_seqlen, 64, 0.0f, causal ? 1 : 0, nullptr, 0, stream));
+}
+
+template <>
+FelixStatus flash_attn_bwd_launch<128>(const half* Q, const half* K, const half* V, const half* O,
+                                       const half* dO, const float* lse, half* dQ, half* dK,
+                                       half* dV, uint32_t heads, uint32_t batch_size,
+                                       uint32_t QKV_seqlen, cudaStream_t stream, bool causal) {
+  return from_c(felix_flash_attn_bwd(Q, K, V, O, dO, lse, dQ, dK, dV, heads, batch_size,
+                                     QKV_seqlen, 128, 0.0f, causal ? 1 : 0, nullptr, 0, stream));
+}
+
 FelixStatus check_watchdog() {
   unsigned code = 0;
   return from_c(felix_watchdog_status(&code, 1));

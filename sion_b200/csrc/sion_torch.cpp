@@ -167,6 +167,46 @@ std::tuple<torch::Tensor, torch::Tensor> flash_attention_lse(const torch::Tensor
   return attn_impl(query, key, value, true, causal);
 }
 
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> flash_attention_backward(
+    const torch::Tensor& query, const torch::Tensor& key, const torch::Tensor& value,
+    const torch::Tensor& out, const torch::Tensor& lse, const torch::Tensor& grad_out,
+    bool causal) {
+  check_attn_inputs(query, key, value);
+  TORCH_CHECK(out.sizes() == query.sizes() && grad_out.sizes() == query.sizes(),
+              "out and grad_out must have the shape of query");
+  TORCH_CHECK(out.dtype() == torch::kHalf && grad_out.dtype() == torch::kHalf,
+              "out and grad_out must be half");
+  TORCH_CHECK(out.is_cuda() && grad_out.is_cuda() && lse.is_cuda(), "All tensors must be CUDA tensors");
+  const int64_t B = query.size(0), H = query.size(1), S = query.size(2), D = query.size(3);
+  TORCH_CHECK(lse.dtype() == torch::kFloat32 && lse.dim() == 3 && lse.size(0) == B &&
+                  lse.size(1) == H && lse.size(2) == S,
+              "lse must be float32 [B, H, S]");
+  const c10::cuda::CUDAGuard guard(query.device());
+  auto Q = query.contiguous(), K = key.contiguous(), V = value.contiguous();
+  auto O = out.contiguous(), G = grad_out.contiguous(), L = lse.contiguous();
+  auto dQ = torch::empty_like(Q), dK = torch::empty_like(Q), dV = torch::empty_like(Q);
+  auto hp = [](const torch::Tensor& t) { return reinterpret_cast<half*>(t.data_ptr<at::Half>()); };
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  felix::FelixStatus status;
+  switch (D) {
+    case 64:
+      status = felix::flash_attn_bwd_launch<64>(hp(Q), hp(K), hp(V), hp(O), hp(G),
+                                                L.data_ptr<float>(), hp(dQ), hp(dK), hp(dV),
+                                                uint32_t(H), uint32_t(B), uint32_t(S), stream,
+                                                causal);
+      break;
+    case 128:
+      status = felix::flash_attn_bwd_launch<128>(hp(Q), hp(K), hp(V), hp(O), hp(G),
+                                                 L.data_ptr<float>(), hp(dQ), hp(dK), hp(dV),
+                                                 uint32_t(H), uint32_t(B), uint32_t(S), stream,
+                                                 causal);
+      break;
+    default: TORCH_CHECK(false, "flash_attention_backward: unsupported head dimension ", D);
+  }
+  TORCH_CHECK(status.ok(), "flash_attention_backward: kernel launch failed: ", status.str());
+  return {dQ, dK, dV};
+}
+
 }  // namespace sion
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -188,4 +228,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attention_lse", &sion::flash_attention_lse,
         "flash attention forward returning (O, fp32 LSE)", py::arg("query"), py::arg("key"),
         py::arg("value"), py::arg("causal") = false);
+  m.def("flash_attention_backward", &sion::flash_attention_backward,
+        "flash attention backward returning (dQ, dK, dV)", py::arg("query"), py::arg("key"),
+        py::arg("value"), py::arg("out"), py::arg("lse"), py::arg("grad_out"),
+        py::arg("causal") = false);
 }

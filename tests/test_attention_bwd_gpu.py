@@ -73,3 +73,26 @@ def test_attention_bwd_deterministic_shapes(felix):
         outs.append(g)
     torch.cuda.synchronize()
     assert torch.equal(outs[0][1], outs[1][1]) and torch.equal(outs[0][2], outs[1][2])
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_autograd_through_sion(causal):
+    """torch.autograd through sion_b200.flash_attention_autograd (sion:: ->
+    felix:: -> C ABI) gives the oracle's gradients."""
+    import sion_b200
+    B, H, S, D = 1, 2, 200, 128
+    Q, K, V, dO = _inputs(B, H, S, D, seed=7)
+    q, k, v = [t.cuda().requires_grad_(True) for t in (Q, K, V)]
+    o = sion_b200.flash_attention_autograd(q, k, v, causal)
+    o.backward(dO.cuda())
+    exact = oracle.attention_bwd(Q.numpy(), K.numpy(), V.numpy(), dO.numpy(), causal=causal)
+    for name, e, t in zip(("dQ", "dK", "dV"), exact, (q.grad, k.grad, v.grad)):
+        m = compare(e, t.float().cpu().numpy().astype(np.float64))
+        assert m["rel_frob"] <= 1e-2, (name, m)
+
+
+def test_attention_backward_rejects_bad_lse():
+    import sion_b200
+    q = torch.zeros(1, 1, 64, 64, dtype=torch.half, device="cuda")
+    with pytest.raises(RuntimeError):
+        sion_b200.flash_attention_backward(q, q, q, q, torch.zeros(1, 1, 32, device="cuda"), q)
