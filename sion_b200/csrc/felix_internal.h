@@ -79,7 +79,8 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
                        void* workspace, size_t ws_bytes, cudaStream_t stream);
 
 struct SgemmOptions {
-  int split_k = 0;  // 0 = auto, 1 = none, n = n-way
+  int split_k = 0;             // 0 = auto, 1 = none, n = n-way
+  bool allow_stream_k = true;  // auto may pick stream-K (workspace grows with the SM count)
 };
 size_t sgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o,
                              int num_sms);

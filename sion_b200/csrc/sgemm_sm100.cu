@@ -14,10 +14,12 @@
 // 28.3 / 42.3; a packed fma.rn.f32x2 inner product was slower (25.0 / 38.7),
 // and so was an 8 x 16 register block with a 128 x 256 tile (16.4 / 33.5). Any M, N, K:
 // loads are predicated with zero fill, stores are bounds-checked; the 128-bit
-// path is used when rows are 16-byte aligned. Small problems are split along K
-// so that the grid covers every SM twice; the last CTA of a tile to finish
-// (atomic ticket) sums the fp32 partials in split order — deterministic, and
-// no CTA waits on another.
+// path is used when rows are 16-byte aligned. When the tiles do not fill one
+// wave of two CTAs per SM (e.g. 1024^3: 64 tiles), the automatic
+// schedule is stream-K: 2 x SMs CTAs take equal runs of (tile, k-tile)
+// iterations; an explicit split count splits along K instead. Either way the
+// last CTA of a tile to finish (atomic ticket) sums the fp32 partials in a
+// fixed order — deterministic, and no CTA waits on another.
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <mutex>
@@ -54,7 +56,9 @@ struct Params {
   const float* B;
   float* C;
   uint32_t splits, k_per_split;  // k_per_split is a multiple of BK
-  float* ws;                     // [tiles][splits][16][256] float4
+  uint64_t sk_iters;             // stream-K: tiles x kt_per_tile (0 = split-K grid)
+  uint32_t kt_per_tile, tiles_n;
+  float* ws;                     // split-K [tiles][splits], stream-K [ctas][2]; 16 x 256 float4 each
   unsigned* counters;            // [tiles]
 };
 
@@ -148,20 +152,41 @@ __device__ __forceinline__ void store_out(const Params& p, uint32_t row, uint32_
   }
 }
 
-template <bool VEC>
-__global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const Params p) {
-  __shared__ __align__(16) float As[2][BK][BM + APAD];
-  __shared__ __align__(16) float Bs[2][BK][BN];
-  __shared__ uint32_t s_last;
+// Partial 128 x 128 tile layout (float4 q of thread t at [q][t]: coalesced).
+__device__ __forceinline__ void write_partial(float4* part, const float (&acc)[8][TN]) {
+  const uint32_t t = threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int g = 0; g < NB; ++g)
+      __stcg(part + (i * NB + g) * 256 + t,
+             make_float4(acc[i][4 * g], acc[i][4 * g + 1], acc[i][4 * g + 2], acc[i][4 * g + 3]));
+}
 
+template <bool VEC>
+__device__ __forceinline__ void store_acc(const Params& p, uint32_t m0, uint32_t n0,
+                                          const float (&acc)[8][TN]) {
   const uint32_t t = threadIdx.x;
   const uint32_t tx = t % 16, ty = t / 16;
-  const uint32_t m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const uint32_t z = blockIdx.z;
-  const uint32_t kbeg = z * p.k_per_split;
-  const uint32_t kend = min(p.K, kbeg + p.k_per_split);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+#pragma unroll
+    for (int g = 0; g < NB; ++g) {
+      const float v[4] = {acc[i][4 * g], acc[i][4 * g + 1], acc[i][4 * g + 2], acc[i][4 * g + 3]};
+      store_out<VEC>(p, row, n0 + 64 * g + tx * 4, v);
+    }
+  }
+}
 
-  float acc[8][TN];
+// acc = A[m0 : m0 + 128, kbeg : kend] * B[kbeg : kend, n0 : n0 + 128]. Ends with
+// a barrier, so the shared-memory tiles may be reused right away.
+template <bool VEC>
+__device__ __forceinline__ void mainloop(const Params& p, uint32_t m0, uint32_t n0, uint32_t kbeg,
+                                         uint32_t kend, float (*As)[BK][BM + APAD],
+                                         float (*Bs)[BK][BN], float (&acc)[8][TN]) {
+  const uint32_t t = threadIdx.x;
+  const uint32_t tx = t % 16, ty = t / 16;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -213,29 +238,103 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
     if (kt + 1 < nk) store_tile(As[cur ^ 1u], Bs[cur ^ 1u], ra, rb);
     __syncthreads();
   }
+}
 
-  if (p.splits == 1) {
+// Stream-K: CTA of iteration x (iterations = tiles x k-tiles, split evenly).
+__device__ __forceinline__ uint32_t sk_cta_of(uint64_t x, uint32_t P, uint64_t I) {
+  return static_cast<uint32_t>(((x + 1) * P - 1) / I);
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const Params p) {
+  __shared__ __align__(16) float As[2][BK][BM + APAD];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+  __shared__ uint32_t s_last;
+  const uint32_t t = threadIdx.x;
+  float acc[8][TN];
+
+  if (p.sk_iters != 0) {
+    // ------------------------------------------------------------ stream-K
+    // CTA c owns iterations [I c / P, I (c + 1) / P) of the (tile, k-tile)
+    // sequence; a tile it covers only in part goes to one of its two partial
+    // slots, and the last of the tile's CTAs to finish sums the slots in CTA
+    // order (deterministic) and writes C.
+    const uint32_t P = gridDim.x, c = blockIdx.x;
+    const uint64_t I = p.sk_iters;
+    const uint32_t KT = p.kt_per_tile;
+    const uint64_t start = I * c / P, end = I * (c + 1) / P;
+    uint64_t it = start;
+    while (it < end) {
+      const uint32_t tile = static_cast<uint32_t>(it / KT);
+      const uint32_t kb0 = static_cast<uint32_t>(it - uint64_t(tile) * KT);
+      const uint64_t left = end - it;
+      const uint32_t kb1 = left < uint64_t(KT - kb0) ? kb0 + static_cast<uint32_t>(left) : KT;
+      const uint32_t m0 = (tile / p.tiles_n) * BM, n0 = (tile % p.tiles_n) * BN;
+      mainloop<VEC>(p, m0, n0, kb0 * BK, min(p.K, kb1 * BK), As, Bs, acc);
+      if (kb0 == 0 && kb1 == KT) {
+        store_acc<VEC>(p, m0, n0, acc);
+      } else {
+        const uint32_t seg = it == start ? 0u : 1u;
+        write_partial(reinterpret_cast<float4*>(p.ws) + (size_t(c) * 2 + seg) * (kPartF4 * 256),
+                      acc);
+        __threadfence();
+        __syncthreads();
+        const uint32_t c_first = sk_cta_of(uint64_t(tile) * KT, P, I);
+        const uint32_t c_last = sk_cta_of(uint64_t(tile + 1) * KT - 1, P, I);
+        if (t == 0) {
+          const unsigned old = atomicAdd(&p.counters[tile], 1u);
+          const uint32_t last = old == c_last - c_first ? 1u : 0u;
+          if (last) atomicExch(&p.counters[tile], 0u);
+          s_last = last;
+        }
+        __syncthreads();
+        if (s_last) {
+          __threadfence();
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+          for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int g = 0; g < NB; ++g) {
-        const float v[4] = {acc[i][4 * g], acc[i][4 * g + 1], acc[i][4 * g + 2], acc[i][4 * g + 3]};
-        store_out<VEC>(p, row, n0 + 64 * g + tx * 4, v);
+            for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+          for (uint32_t cc = c_first; cc <= c_last; ++cc) {
+            // the tile is CTA cc's first segment when cc starts inside it
+            const uint32_t sg = I * cc / P >= uint64_t(tile) * KT ? 0u : 1u;
+            const float4* part =
+                reinterpret_cast<const float4*>(p.ws) + (size_t(cc) * 2 + sg) * (kPartF4 * 256);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+              for (int g = 0; g < NB; ++g) {
+                const float4 x = __ldcg(part + (i * NB + g) * 256 + t);
+                acc[i][4 * g] += x.x;
+                acc[i][4 * g + 1] += x.y;
+                acc[i][4 * g + 2] += x.z;
+                acc[i][4 * g + 3] += x.w;
+              }
+          }
+          store_acc<VEC>(p, m0, n0, acc);
+        }
       }
+      it += kb1 - kb0;
     }
     return;
   }
 
-  // Split-K: publish the partial (float4 q of thread t at [q][t]: coalesced).
+  // -------------------------------------------------------------- split-K
+  const uint32_t m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const uint32_t z = blockIdx.z;
+  const uint32_t kbeg = z * p.k_per_split;
+  const uint32_t kend = min(p.K, kbeg + p.k_per_split);
+  mainloop<VEC>(p, m0, n0, kbeg, kend, As, Bs, acc);
+
+  if (p.splits == 1) {
+    store_acc<VEC>(p, m0, n0, acc);
+    return;
+  }
+
+  // Split-K: publish the partial; the last split of the tile to finish sums
+  // the partials in split order.
   const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
-  float4* part = reinterpret_cast<float4*>(p.ws) + (size_t(tile) * p.splits + z) * (kPartF4 * 256);
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int g = 0; g < NB; ++g)
-      __stcg(part + (i * NB + g) * 256 + t,
-             make_float4(acc[i][4 * g], acc[i][4 * g + 1], acc[i][4 * g + 2], acc[i][4 * g + 3]));
+  write_partial(reinterpret_cast<float4*>(p.ws) + (size_t(tile) * p.splits + z) * (kPartF4 * 256),
+                acc);
   __threadfence();
   __syncthreads();
   if (t == 0) {
@@ -250,8 +349,7 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
   const float4* base =
       reinterpret_cast<const float4*>(p.ws) + size_t(tile) * p.splits * (kPartF4 * 256);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+  for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int g = 0; g < NB; ++g) {
       float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -259,10 +357,12 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
         const float4 x0 = __ldcg(base + zz * (kPartF4 * 256) + (i * NB + g) * 256 + t);
         s0.x += x0.x; s0.y += x0.y; s0.z += x0.z; s0.w += x0.w;
       }
-      const float v[4] = {s0.x, s0.y, s0.z, s0.w};
-      store_out<VEC>(p, row, n0 + 64 * g + tx * 4, v);
+      acc[i][4 * g] = s0.x;
+      acc[i][4 * g + 1] = s0.y;
+      acc[i][4 * g + 2] = s0.z;
+      acc[i][4 * g + 3] = s0.w;
     }
-  }
+  store_acc<VEC>(p, m0, n0, acc);
 }
 
 }  // namespace sgemm
@@ -303,8 +403,27 @@ uint32_t choose_splits(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o
 }
 }  // namespace
 
+// Stream-K grid (0 = use the split-K grid): when the 128 x 128 tiles do not
+// fill one wave of two resident CTAs per SM, spread (tile, k-tile)
+// iterations evenly over 2 x SMs CTAs (each at least 4 k-tiles).
+uint32_t choose_stream_k(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o, int num_sms) {
+  if (o.split_k != 0 || !o.allow_stream_k) return 0;
+  const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const uint32_t kt = (K + BK - 1) / BK;
+  const uint32_t slots = 2u * uint32_t(num_sms);
+  // (with a full wave or more, plain tiles measured as fast: 4096^3 43.9 vs
+  // 43.3 TFLOP/s)
+  if (kt < 8 || tiles >= slots || tiles > kWsMaxCounters) return 0;
+  const uint64_t iters = uint64_t(tiles) * kt;
+  uint64_t P = slots;
+  if (P > iters / 4) P = iters / 4;
+  return P >= 2 ? uint32_t(P) : 0;
+}
+
 size_t sgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o,
                              int num_sms) {
+  const uint32_t P = choose_stream_k(M, N, K, o, num_sms);
+  if (P) return kWsCounterBytes + size_t(P) * 2 * BM * BN * sizeof(float);
   const uint32_t s = choose_splits(M, N, K, o, num_sms);
   if (s <= 1) return 0;
   const size_t tiles = size_t((M + BM - 1) / BM) * ((N + BN - 1) / BN);
@@ -329,6 +448,33 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
   p.A = A;
   p.B = B;
   p.C = C;
+  const uint32_t sk_ctas = choose_stream_k(M, N, K, o, dev->num_sms);
+  const bool vec = (K % 4 == 0) && (N % 4 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
+                     reinterpret_cast<uintptr_t>(C)) &
+                    15u) == 0;
+  if (sk_ctas) {
+    p.tiles_n = (N + BN - 1) / BN;
+    p.kt_per_tile = (K + BK - 1) / BK;
+    p.sk_iters = uint64_t(p.tiles_n) * ((M + BM - 1) / BM) * p.kt_per_tile;
+    p.splits = 1;
+    const size_t need = kWsCounterBytes + size_t(sk_ctas) * 2 * BM * BN * sizeof(float);
+    if (!workspace) {
+      workspace = library_workspace(dev, stream, need);
+      if (!workspace) return launch_error(cudaErrorMemoryAllocation, "sgemm: workspace");
+    } else if (ws_bytes < need) {
+      return api_error("sgemm: workspace too small");
+    }
+    p.counters = static_cast<unsigned*>(workspace);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
+    if (vec)
+      sgemm_kernel<true><<<sk_ctas, kThreads, 0, stream>>>(p);
+    else
+      sgemm_kernel<false><<<sk_ctas, kThreads, 0, stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return launch_error(e, "sgemm: launch failed");
+    return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  }
   p.splits = choose_splits(M, N, K, o, dev->num_sms);
   const uint32_t kblocks = (K + BK - 1) / BK;
   p.k_per_split = ((kblocks + p.splits - 1) / p.splits) * BK;
@@ -348,10 +494,6 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
     p.counters = static_cast<unsigned*>(workspace);
     p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
   }
-  const bool vec = (K % 4 == 0) && (N % 4 == 0) &&
-                   ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
-                     reinterpret_cast<uintptr_t>(C)) &
-                    15u) == 0;
   if (vec)
     sgemm_kernel<true><<<grid, kThreads, 0, stream>>>(p);
   else
@@ -393,6 +535,7 @@ FelixCode sgemm_noalloc_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, 
   if (!dev) return launch_error(cudaGetLastError(), "sgemm_noalloc: no CUDA device");
   SgemmOptions o;
   o.split_k = split_k;
+  o.allow_stream_k = false;  // the static scratch is sized for split-K partials
   size_t need = sgemm_workspace_bytes(M, N, K, o, dev->num_sms);
   if (need > kNoAllocScratchBytes) {
     if (split_k > 0)
