@@ -163,6 +163,21 @@ int encode_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint6
   return r == CUDA_SUCCESS ? 0 : int(r);
 }
 
+int encode_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t pitch, uint32_t bi, uint32_t bo) {
+  std::call_once(g_encode_once, load_encode);
+  if (!g_encode) return -1;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {bi, bo};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : int(r);
+}
+
 int encode_tmap_2d_f16_noswizzle(CUtensorMap* map, const void* base, uint64_t inner,
                                  uint64_t outer, uint64_t pitch, uint32_t bi, uint32_t bo) {
   return encode_2d(map, base, inner, outer, pitch, bi, bo, CU_TENSOR_MAP_SWIZZLE_NONE);

@@ -54,6 +54,9 @@ int encode_tmap_2d_f16_swizzle(CUtensorMap* map, const void* base, uint64_t inne
 int encode_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer1,
                        uint64_t outer2, uint64_t pitch1_bytes, uint64_t pitch2_bytes,
                        uint32_t box_inner, uint32_t box_outer1, uint32_t box_outer2);
+// 2-D fp32 tensor map without swizzle (row pitch in bytes, multiple of 16).
+int encode_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer);
 // 3-D fp32 tensor map, 128-byte swizzle (box_inner * 4 must be <= 128).
 int encode_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer1,
                        uint64_t outer2, uint64_t pitch1_bytes, uint64_t pitch2_bytes,
@@ -81,6 +84,7 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
 struct SgemmOptions {
   int split_k = 0;             // 0 = auto, 1 = none, n = n-way
   bool allow_stream_k = true;  // auto may pick stream-K (workspace grows with the SM count)
+  bool allow_tma = true;       // TMA-fed main loop when rows are 16-byte aligned
 };
 size_t sgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o,
                              int num_sms);

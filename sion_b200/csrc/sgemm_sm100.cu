@@ -20,11 +20,13 @@
 // iterations; an explicit split count splits along K instead. Either way the
 // last CTA of a tile to finish (atomic ticket) sums the fp32 partials in a
 // fixed order — deterministic, and no CTA waits on another.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <mutex>
 
 #include "felix_internal.h"
+#include "sm100_ptx.cuh"
 
 namespace felix_sm100 {
 namespace sgemm {
@@ -58,6 +60,8 @@ struct Params {
   uint32_t splits, k_per_split;  // k_per_split is a multiple of BK
   uint64_t sk_iters;             // stream-K: tiles x kt_per_tile (0 = split-K grid)
   uint32_t kt_per_tile, tiles_n;
+  uint32_t bk;                   // k-tile of the schedule (BK, or 32 with the TMA main loop)
+  unsigned* status;              // watchdog word (TMA main loop waits)
   float* ws;                     // split-K [tiles][splits], stream-K [ctas][2]; 16 x 256 float4 each
   unsigned* counters;            // [tiles]
 };
@@ -240,18 +244,167 @@ __device__ __forceinline__ void mainloop(const Params& p, uint32_t m0, uint32_t 
   }
 }
 
+// ---------------------------------------------------------------- TMA main loop
+// Used when A and B rows are 16-byte aligned (K % 4 == 0, N % 4 == 0). Per
+// stage: the A tile [128 rows][32 k] and the B tile [32 k][128 n], fp32,
+// unswizzled, loaded by TMA (zero fill past M, N, K). Thread 0 issues the
+// loads; each warp releases a stage with one mbarrier arrival, so there is no
+// CTA-wide barrier per k-tile and no register staging of global loads. A stays
+// row-major: a thread reads its 8 rows as 16-byte (4 k) pieces, so one LDS.128
+// feeds 32 FFMAs, as in the transposed layout.
+constexpr int kTmaBk = 32;
+constexpr int kTmaStages = 3;
+constexpr int kTmaATile = BM * kTmaBk * 4;  // 16 KB
+constexpr int kTmaBTile = kTmaBk * BN * 4;  // 16 KB (BN = 128)
+constexpr int kTmaSmem = kTmaStages * (kTmaATile + kTmaBTile) + 2 * kTmaStages * 8 + 16;
+static_assert(BN == 128, "TMA main loop: 128 x 128 tiles");
+
+struct TmaPipe {
+  float* sA;
+  float* sB;
+  uint64_t* full;
+  uint64_t* empty;
+  volatile int* abort_flag;
+  uint32_t kt_load, kt_use;  // k-tiles issued / consumed by this CTA so far
+};
+
+__device__ __forceinline__ bool tma_issue(TmaPipe& q, const CUtensorMap* tmA,
+                                          const CUtensorMap* tmB, const Params& p, uint32_t m0,
+                                          uint32_t n0, uint32_t kb) {
+  const uint32_t st = q.kt_load % kTmaStages, use = q.kt_load / kTmaStages;
+  if (!felix_sm100::mbar_wait(q.empty + st, (use & 1u) ^ 1u, q.abort_flag, p.status,
+                              felix_sm100::kWdProducerEmpty))
+    return false;
+  felix_sm100::mbar_arrive_expect_tx(q.full + st, kTmaATile + kTmaBTile);
+  felix_sm100::tma_load_2d(q.sA + st * (kTmaATile / 4), tmA, q.full + st, int(kb * kTmaBk),
+                           int(m0));
+  felix_sm100::tma_load_2d(q.sB + st * (kTmaBTile / 4), tmB, q.full + st, int(n0),
+                           int(kb * kTmaBk));
+  ++q.kt_load;
+  return true;
+}
+
+// acc = A[m0 : m0 + 128, kbeg : kend] * B[kbeg : kend, n0 : n0 + 128] with
+// kbeg a multiple of 32 (k past kend inside the last k-tile must be past K).
+__device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
+                                             const CUtensorMap* tmB, const Params& p,
+                                             uint32_t m0, uint32_t n0, uint32_t kbeg,
+                                             uint32_t kend, float (&acc)[8][TN]) {
+  const uint32_t t = threadIdx.x, lane = t % 32;
+  const uint32_t tx = t % 16, ty = t / 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+  const uint32_t kb0 = kbeg / kTmaBk;
+  const uint32_t n = kend > kbeg ? (kend - kbeg + kTmaBk - 1) / kTmaBk : 0;
+  bool ok = true;
+  if (t == 0)
+    for (uint32_t j = 0; ok && j < n && j < kTmaStages - 1; ++j)
+      ok = tma_issue(q, tmA, tmB, p, m0, n0, kb0 + j);
+  for (uint32_t j = 0; j < n; ++j) {
+    const uint32_t st = q.kt_use % kTmaStages;
+    if (!felix_sm100::mbar_wait(q.full + st, (q.kt_use / kTmaStages) & 1u, q.abort_flag, p.status,
+                                felix_sm100::kWdMmaFull))
+      return false;
+    const float* a_s = q.sA + st * (kTmaATile / 4);  // [128][32]
+    const float* b_s = q.sB + st * (kTmaBTile / 4);  // [32][128]
+#pragma unroll
+    for (int k4 = 0; k4 < kTmaBk / 4; ++k4) {
+      float4 af[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t row = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
+        af[i] = *reinterpret_cast<const float4*>(a_s + row * kTmaBk + k4 * 4);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int k = k4 * 4 + kk;
+        float b[TN];
+#pragma unroll
+        for (int g = 0; g < NB; ++g) {
+          const float4 bv = *reinterpret_cast<const float4*>(b_s + k * BN + 64 * g + tx * 4);
+          b[4 * g] = bv.x;
+          b[4 * g + 1] = bv.y;
+          b[4 * g + 2] = bv.z;
+          b[4 * g + 3] = bv.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float a = kk == 0 ? af[i].x : kk == 1 ? af[i].y : kk == 2 ? af[i].z : af[i].w;
+#pragma unroll
+          for (int jj = 0; jj < TN; ++jj) acc[i][jj] = fmaf(a, b[jj], acc[i][jj]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) felix_sm100::mbar_arrive(q.empty + st);
+    ++q.kt_use;
+    if (t == 0 && ok && j + kTmaStages - 1 < n)
+      ok = tma_issue(q, tmA, tmB, p, m0, n0, kb0 + j + kTmaStages - 1);
+  }
+  return true;
+}
+
+// Before the CTA exits: every TMA load it issued has landed (a load can still
+// be in flight only after an aborted wait).
+template <bool TMA>
+__device__ __forceinline__ void drain_tma(TmaPipe& q, const Params& p) {
+  if constexpr (TMA) {
+    if (threadIdx.x == 0) {
+      int dummy = 0;
+      for (uint32_t k = q.kt_use; k < q.kt_load; ++k)
+        felix_sm100::mbar_wait(q.full + k % kTmaStages, (k / kTmaStages) & 1u, &dummy, p.status,
+                               felix_sm100::kWdDrain, 100000000ull);
+    }
+  }
+}
+
 // Stream-K: CTA of iteration x (iterations = tiles x k-tiles, split evenly).
 __device__ __forceinline__ uint32_t sk_cta_of(uint64_t x, uint32_t P, uint64_t I) {
   return static_cast<uint32_t>(((x + 1) * P - 1) / I);
 }
 
-template <bool VEC>
-__global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const Params p) {
-  __shared__ __align__(16) float As[2][BK][BM + APAD];
-  __shared__ __align__(16) float Bs[2][BK][BN];
+template <bool VEC, bool TMA>
+__global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
+    sgemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const Params p) {
+  extern __shared__ __align__(1024) uint8_t dsmem[];
   __shared__ uint32_t s_last;
+  __shared__ int s_abort;
   const uint32_t t = threadIdx.x;
   float acc[8][TN];
+  // register-staged main loop: As [2][BK][BM + APAD], Bs [2][BK][BN]
+  auto As = reinterpret_cast<float(*)[BK][BM + APAD]>(dsmem);
+  auto Bs = reinterpret_cast<float(*)[BK][BN]>(dsmem + 2 * BK * (BM + APAD) * 4);
+  // TMA main loop: stages of A and B tiles, then the full / empty barriers
+  TmaPipe q{};
+  if constexpr (TMA) {
+    q.sA = reinterpret_cast<float*>(dsmem);
+    q.sB = reinterpret_cast<float*>(dsmem + kTmaStages * kTmaATile);
+    q.full = reinterpret_cast<uint64_t*>(dsmem + kTmaStages * (kTmaATile + kTmaBTile));
+    q.empty = q.full + kTmaStages;
+    q.abort_flag = &s_abort;
+    if (t == 0) {
+      for (int i = 0; i < kTmaStages; ++i) {
+        felix_sm100::mbar_init(q.full + i, 1);
+        felix_sm100::mbar_init(q.empty + i, kThreads / 32);
+      }
+      s_abort = 0;
+      felix_sm100::fence_mbar_init();
+      felix_sm100::tma_prefetch_desc(&tmA);
+      felix_sm100::tma_prefetch_desc(&tmB);
+    }
+    __syncthreads();
+  }
+  auto run = [&](uint32_t m0, uint32_t n0, uint32_t kbeg, uint32_t kend) -> bool {
+    if constexpr (TMA) {
+      return mainloop_tma(q, &tmA, &tmB, p, m0, n0, kbeg, kend, acc);
+    } else {
+      mainloop<VEC>(p, m0, n0, kbeg, kend, As, Bs, acc);
+      return true;
+    }
+  };
 
   if (p.sk_iters != 0) {
     // ------------------------------------------------------------ stream-K
@@ -270,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
       const uint64_t left = end - it;
       const uint32_t kb1 = left < uint64_t(KT - kb0) ? kb0 + static_cast<uint32_t>(left) : KT;
       const uint32_t m0 = (tile / p.tiles_n) * BM, n0 = (tile % p.tiles_n) * BN;
-      mainloop<VEC>(p, m0, n0, kb0 * BK, min(p.K, kb1 * BK), As, Bs, acc);
+      if (!run(m0, n0, kb0 * p.bk, min(p.K, kb1 * p.bk))) break;
       if (kb0 == 0 && kb1 == KT) {
         store_acc<VEC>(p, m0, n0, acc);
       } else {
@@ -315,6 +468,7 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
       }
       it += kb1 - kb0;
     }
+    drain_tma<TMA>(q, p);
     return;
   }
 
@@ -323,7 +477,9 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB) sgemm_kernel(const
   const uint32_t z = blockIdx.z;
   const uint32_t kbeg = z * p.k_per_split;
   const uint32_t kend = min(p.K, kbeg + p.k_per_split);
-  mainloop<VEC>(p, m0, n0, kbeg, kend, As, Bs, acc);
+  const bool ok = run(m0, n0, kbeg, kend);
+  drain_tma<TMA>(q, p);
+  if (!ok) return;
 
   if (p.splits == 1) {
     store_acc<VEC>(p, m0, n0, acc);
@@ -406,10 +562,11 @@ uint32_t choose_splits(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o
 // Stream-K grid (0 = use the split-K grid): when the 128 x 128 tiles do not
 // fill one wave of two resident CTAs per SM, spread (tile, k-tile)
 // iterations evenly over 2 x SMs CTAs (each at least 4 k-tiles).
-uint32_t choose_stream_k(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o, int num_sms) {
+uint32_t choose_stream_k(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o, int num_sms,
+                         uint32_t bk) {
   if (o.split_k != 0 || !o.allow_stream_k) return 0;
   const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const uint32_t kt = (K + BK - 1) / BK;
+  const uint32_t kt = (K + bk - 1) / bk;
   const uint32_t slots = 2u * uint32_t(num_sms);
   // (with a full wave or more, plain tiles measured as fast: 4096^3 43.9 vs
   // 43.3 TFLOP/s)
@@ -422,7 +579,8 @@ uint32_t choose_stream_k(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions&
 
 size_t sgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o,
                              int num_sms) {
-  const uint32_t P = choose_stream_k(M, N, K, o, num_sms);
+  // (the larger of the two main loops' needs: the k-tile is BK or 32)
+  const uint32_t P = choose_stream_k(M, N, K, o, num_sms, BK);
   if (P) return kWsCounterBytes + size_t(P) * 2 * BM * BN * sizeof(float);
   const uint32_t s = choose_splits(M, N, K, o, num_sms);
   if (s <= 1) return 0;
@@ -448,17 +606,41 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
   p.A = A;
   p.B = B;
   p.C = C;
-  const uint32_t sk_ctas = choose_stream_k(M, N, K, o, dev->num_sms);
   const bool vec = (K % 4 == 0) && (N % 4 == 0) &&
                    ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
                      reinterpret_cast<uintptr_t>(C)) &
                     15u) == 0;
-  if (sk_ctas) {
-    p.tiles_n = (N + BN - 1) / BN;
-    p.kt_per_tile = (K + BK - 1) / BK;
-    p.sk_iters = uint64_t(p.tiles_n) * ((M + BM - 1) / BM) * p.kt_per_tile;
-    p.splits = 1;
-    const size_t need = kWsCounterBytes + size_t(sk_ctas) * 2 * BM * BN * sizeof(float);
+  // TMA main loop: rows of A and B must be 16-byte multiples (vec)
+  const bool tma = vec && o.allow_tma;
+  p.bk = tma ? uint32_t(kTmaBk) : uint32_t(BK);
+  p.status = dev->status_word;
+  CUtensorMap tmA{}, tmB{};
+  if (tma) {
+    if (encode_tmap_2d_f32(&tmA, A, K, M, uint64_t(K) * 4, kTmaBk, BM) ||
+        encode_tmap_2d_f32(&tmB, B, N, K, uint64_t(N) * 4, BN, kTmaBk))
+      return api_error("sgemm: cuTensorMapEncodeTiled failed");
+    static int configured[64] = {0};
+    if (dev->ordinal < 0 || dev->ordinal >= 64) return api_error("sgemm: device ordinal");
+    if (!configured[dev->ordinal]) {
+      cudaError_t e = cudaFuncSetAttribute(sgemm_kernel<true, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem);
+      if (e != cudaSuccess) return FelixCode{FELIX_API_ERROR, e};
+      configured[dev->ordinal] = 1;
+    }
+  }
+  auto launch = [&](dim3 grid) -> FelixCode {
+    constexpr size_t kRegSmem = size_t(2) * BK * (BM + APAD) * 4 + size_t(2) * BK * BN * 4;
+    if (tma)
+      sgemm_kernel<true, true><<<grid, kThreads, kTmaSmem, stream>>>(tmA, tmB, p);
+    else if (vec)
+      sgemm_kernel<true, false><<<grid, kThreads, kRegSmem, stream>>>(tmA, tmB, p);
+    else
+      sgemm_kernel<false, false><<<grid, kThreads, kRegSmem, stream>>>(tmA, tmB, p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return launch_error(e, "sgemm: launch failed");
+    return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  };
+  auto attach = [&](size_t need) -> FelixCode {
     if (!workspace) {
       workspace = library_workspace(dev, stream, need);
       if (!workspace) return launch_error(cudaErrorMemoryAllocation, "sgemm: workspace");
@@ -467,40 +649,33 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
     }
     p.counters = static_cast<unsigned*>(workspace);
     p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
-    if (vec)
-      sgemm_kernel<true><<<sk_ctas, kThreads, 0, stream>>>(p);
-    else
-      sgemm_kernel<false><<<sk_ctas, kThreads, 0, stream>>>(p);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return launch_error(e, "sgemm: launch failed");
     return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  };
+
+  const uint32_t sk_ctas = choose_stream_k(M, N, K, o, dev->num_sms, p.bk);
+  if (sk_ctas) {
+    p.tiles_n = (N + BN - 1) / BN;
+    p.kt_per_tile = (K + p.bk - 1) / p.bk;
+    p.sk_iters = uint64_t(p.tiles_n) * ((M + BM - 1) / BM) * p.kt_per_tile;
+    p.splits = 1;
+    FelixCode rc = attach(kWsCounterBytes + size_t(sk_ctas) * 2 * BM * BN * sizeof(float));
+    if (rc.type != FELIX_SUCCESS) return rc;
+    return launch(dim3(sk_ctas));
   }
   p.splits = choose_splits(M, N, K, o, dev->num_sms);
-  const uint32_t kblocks = (K + BK - 1) / BK;
-  p.k_per_split = ((kblocks + p.splits - 1) / p.splits) * BK;
+  const uint32_t kblocks = (K + p.bk - 1) / p.bk;
+  if (p.splits > kblocks) p.splits = kblocks;
+  p.k_per_split = ((kblocks + p.splits - 1) / p.splits) * p.bk;
   // Recompute the split count so that no split is empty.
   p.splits = (K + p.k_per_split - 1) / p.k_per_split;
   const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, p.splits);
   if (grid.y > 65535u) return api_error("sgemm: M too large");
   if (p.splits > 1) {
     const size_t tiles = size_t(grid.x) * grid.y;
-    const size_t need = kWsCounterBytes + tiles * p.splits * BM * BN * sizeof(float);
-    if (!workspace) {
-      workspace = library_workspace(dev, stream, need);
-      if (!workspace) return launch_error(cudaErrorMemoryAllocation, "sgemm: workspace");
-    } else if (ws_bytes < need) {
-      return api_error("sgemm: workspace too small");
-    }
-    p.counters = static_cast<unsigned*>(workspace);
-    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
+    FelixCode rc = attach(kWsCounterBytes + tiles * p.splits * BM * BN * sizeof(float));
+    if (rc.type != FELIX_SUCCESS) return rc;
   }
-  if (vec)
-    sgemm_kernel<true><<<grid, kThreads, 0, stream>>>(p);
-  else
-    sgemm_kernel<false><<<grid, kThreads, 0, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return launch_error(e, "sgemm: launch failed");
-  return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  return launch(grid);
 }
 
 namespace {
@@ -536,6 +711,7 @@ FelixCode sgemm_noalloc_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, 
   SgemmOptions o;
   o.split_k = split_k;
   o.allow_stream_k = false;  // the static scratch is sized for split-K partials
+  o.allow_tma = false;
   size_t need = sgemm_workspace_bytes(M, N, K, o, dev->num_sms);
   if (need > kNoAllocScratchBytes) {
     if (split_k > 0)
