@@ -164,7 +164,7 @@ int encode_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint6
 }
 
 int encode_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-                       uint64_t pitch, uint32_t bi, uint32_t bo) {
+                       uint64_t pitch, uint32_t bi, uint32_t bo, bool swizzle128) {
   std::call_once(g_encode_once, load_encode);
   if (!g_encode) return -1;
   cuuint64_t dims[2] = {inner, outer};
@@ -173,8 +173,8 @@ int encode_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint6
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : int(r);
 }
 

@@ -54,9 +54,11 @@ int encode_tmap_2d_f16_swizzle(CUtensorMap* map, const void* base, uint64_t inne
 int encode_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer1,
                        uint64_t outer2, uint64_t pitch1_bytes, uint64_t pitch2_bytes,
                        uint32_t box_inner, uint32_t box_outer1, uint32_t box_outer2);
-// 2-D fp32 tensor map without swizzle (row pitch in bytes, multiple of 16).
+// 2-D fp32 tensor map (row pitch in bytes, multiple of 16), unswizzled or with
+// the 128-byte swizzle (box_inner * 4 must then be 128).
 int encode_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-                       uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer);
+                       uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                       bool swizzle128 = false);
 // 3-D fp32 tensor map, 128-byte swizzle (box_inner * 4 must be <= 128).
 int encode_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer1,
                        uint64_t outer2, uint64_t pitch1_bytes, uint64_t pitch2_bytes,

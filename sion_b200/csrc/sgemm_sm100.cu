@@ -250,10 +250,13 @@ __device__ __forceinline__ void mainloop(const Params& p, uint32_t m0, uint32_t 
 // unswizzled, loaded by TMA (zero fill past M, N, K). Thread 0 issues the
 // loads; each warp releases a stage with one mbarrier arrival, so there is no
 // CTA-wide barrier per k-tile and no register staging of global loads. A stays
-// row-major: a thread reads its 8 rows as 16-byte (4 k) pieces, so one LDS.128
-// feeds 32 FFMAs, as in the transposed layout.
+// row-major: a thread reads its 8 rows as 8-byte (2 k) pieces.
 constexpr int kTmaBk = 32;
 constexpr int kTmaStages = 3;
+// k values of A read per shared-memory load: 2 (LDS.64, 16 fragment
+// registers). 4 (LDS.128) needs 16 more registers and spilled at the 128 that
+// two CTAs per SM allow: 4096^3 45.4 vs 51.9 TFLOP/s.
+constexpr int kTmaAk = 2;
 constexpr int kTmaATile = BM * kTmaBk * 4;  // 16 KB
 constexpr int kTmaBTile = kTmaBk * BN * 4;  // 16 KB (BN = 128)
 constexpr int kTmaSmem = kTmaStages * (kTmaATile + kTmaBTile) + 2 * kTmaStages * 8 + 16;
@@ -309,17 +312,25 @@ __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
       return false;
     const float* a_s = q.sA + st * (kTmaATile / 4);  // [128][32]
     const float* b_s = q.sB + st * (kTmaBTile / 4);  // [32][128]
-#pragma unroll
-    for (int k4 = 0; k4 < kTmaBk / 4; ++k4) {
-      float4 af[8];
+    // one group of kTmaAk k-steps per iteration, not unrolled: unrolled, the
+    // compiler hoists the B loads of later groups and spills at 128 registers
+#pragma unroll 1
+    for (int k2 = 0; k2 < kTmaBk / kTmaAk; ++k2) {
+      // A: kTmaAk consecutive k of each of the thread's 8 rows per load (the
+      // two rows a warp reads at once share banks: a 2-way conflict, cheaper
+      // here than the per-load address arithmetic of a swizzled tile, which
+      // measured 40 vs 52 TFLOP/s at 4096^3)
+      float af[8][kTmaAk];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint32_t row = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
-        af[i] = *reinterpret_cast<const float4*>(a_s + row * kTmaBk + k4 * 4);
+        const float2 v = *reinterpret_cast<const float2*>(a_s + row * kTmaBk + k2 * kTmaAk);
+        af[i][0] = v.x;
+        af[i][1] = v.y;
       }
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const int k = k4 * 4 + kk;
+      for (int kk = 0; kk < kTmaAk; ++kk) {
+        const int k = k2 * kTmaAk + kk;
         float b[TN];
 #pragma unroll
         for (int g = 0; g < NB; ++g) {
@@ -330,11 +341,9 @@ __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
           b[4 * g + 3] = bv.w;
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float a = kk == 0 ? af[i].x : kk == 1 ? af[i].y : kk == 2 ? af[i].z : af[i].w;
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int jj = 0; jj < TN; ++jj) acc[i][jj] = fmaf(a, b[jj], acc[i][jj]);
-        }
+          for (int jj = 0; jj < TN; ++jj) acc[i][jj] = fmaf(af[i][kk], b[jj], acc[i][jj]);
       }
     }
     __syncwarp();
