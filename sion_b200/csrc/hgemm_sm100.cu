@@ -70,6 +70,7 @@ struct Params {
   uint64_t sk_iters;
   uint32_t group_m;
   uint32_t tma_store;     // 1: epilogue writes C through smem + TMA (beta == 0)
+  uint32_t ksplit2;       // 1: 2-CTA clusters split each tile's K in halves (see below)
   float* ws_partials;     // [gridDim.x][2] slots of BM*BN fp32, see partial_index()
   unsigned* ws_counters;  // [sk_tiles], zero between launches
   unsigned* status;       // watchdog word
@@ -93,7 +94,9 @@ struct Sched {
   uint64_t I, it, end, start;
   uint32_t dp_next;
 
+  uint32_t ksplit_rank;  // cluster split-K: 0 or 1 (which half of K); 2 = unit taken
   __device__ __forceinline__ void init(const Params& p) {
+    ksplit_rank = p.ksplit2 ? (blockIdx.x & 1u) : 3u;
     cta = blockIdx.x;
     P = gridDim.x;
     sk_tiles = p.sk_tiles;
@@ -106,6 +109,19 @@ struct Sched {
     dp_next = sk_tiles + cta;
   }
   __device__ __forceinline__ bool next(Unit& u) {
+    if (ksplit_rank < 2) {
+      // cluster split-K: tile blockIdx.x / 2, K half blockIdx.x % 2
+      const uint32_t half = KB / 2;
+      u.tile = cta >> 1;
+      u.kb0 = ksplit_rank ? half : 0;
+      u.kb1 = ksplit_rank ? KB : half;
+      u.partial = false;
+      u.sk = 0;
+      u.seg = ksplit_rank;
+      ksplit_rank = 2;
+      return true;
+    }
+    if (ksplit_rank == 2) return false;
     if (it < end) {
       const uint32_t s = static_cast<uint32_t>(it / KB);
       const uint32_t kb0 = static_cast<uint32_t>(it - uint64_t(s) * KB);
@@ -214,7 +230,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = bars + 2 * S;      // [2]
   uint64_t* tempty = bars + 2 * S + 2; // [2]
   uint64_t* drain = bars + 2 * S + 4;  // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint64_t* recv = bars + 2 * S + 5;   // [1] cluster split-K: rank 1's half arrived (rank 0)
+  uint64_t* ring_free = bars + 2 * S + 6;  // [1] cluster split-K: rank 0's ring idle (rank 1)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
+  // Cluster split-K: rank 1's accumulator (BM x BN fp32) goes into the start
+  // of rank 0's TMA ring once rank 0's MMAs have finished with it.
+  const uint32_t NS = uint32_t(S);
+  uint8_t* recv_buf = ring;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* bcast = tmem_slot + 2;
 
@@ -231,6 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(recv, 128);  // one arrival per epilogue thread of rank 1
+    mbar_init(ring_free, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -242,7 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   tc_fence_before();
-  __syncthreads();
+  if (p.ksplit2)
+    cluster_sync();  // rank 1 arrives on rank 0's barrier: it must be initialised
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -276,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sb, &tmB, &full[stage], int(kb * BK), n0);
           }
           ++filled;
-          if (++stage == S) {
+          if (++stage == NS) {
             stage = 0;
             phase ^= 1u;
           }
@@ -284,12 +311,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: wait (bounded) for the last fill of every stage so that no TMA
       // write is in flight when the CTA exits.
-      const uint32_t n = filled < uint32_t(S) ? filled : uint32_t(S);
+      const uint32_t n = filled < NS ? filled : NS;
       for (uint32_t i = 0; i < n; ++i) {
         // stage of the i-th most recent fill, and the phase parity it filled
         const uint32_t f = filled - 1 - i;
-        const uint32_t st = f % S;
-        const uint32_t par = (f / S) & 1u;
+        const uint32_t st = f % NS;
+        const uint32_t par = (f / NS) & 1u;
         int dummy = 0;
         mbar_wait(&full[st], par, &dummy, p.status, kWdDrain, 100000000ull);
       }
@@ -335,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_f16_ss(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
-          if (++stage == S) {
+          if (++stage == NS) {
             stage = 0;
             phase ^= 1u;
           }
@@ -369,7 +396,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t col0 = tn * BN;
       const uint32_t taddr = tmem_base + ((q * 32u) << 16) + buf * BN;
 
-      if (!u.partial && p.tma_store) {
+      if (p.ksplit2 && u.seg == 1) {
+        // Cluster split-K, second half of K: the fp32 accumulator goes to rank
+        // 0's receive buffer over DSMEM (partial_index layout: a warp's 32 rows
+        // are 512 contiguous bytes), then every thread arrives on rank 0's
+        // barrier (release: its stores are visible before the arrival counts).
+        const uint32_t rbuf = mapa_shared(smem_u32(recv_buf), 0);
+        if (!mbar_wait(ring_free, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st_shared_cluster_v4(rbuf + partial_index(c / 32, j, row_in_tile) * 16, r[4 * j],
+                                 r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        }
+        mbar_arrive_cluster(mapa_shared(smem_u32(recv), 0));
+      } else if (p.ksplit2) {
+        // Cluster split-K, first half: C = alpha * (own + rank 1's half), in
+        // that order (deterministic), through the TMA-store staging below.
+        // tfull: every MMA of this CTA has completed, so its ring is idle
+        // (nothing more is loaded: this is the CTA's only unit)
+        if (epi_tid == 0) mbar_arrive_cluster(mapa_shared(smem_u32(ring_free), 1));
+        if (!mbar_wait(recv, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
+        const float4* r4 = reinterpret_cast<const float4*>(recv_buf);
+        uint8_t* stg = staging + (warp - 2) * 8192;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(taddr + c, r0);
+          tmem_ld_32x32b_x32(taddr + c + 32, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x0 = r4[partial_index(c / 32, j, row_in_tile)];
+            const float4 x1 = r4[partial_index(c / 32 + 1, j, row_in_tile)];
+            r0[4 * j] = __float_as_uint(__uint_as_float(r0[4 * j]) + x0.x);
+            r0[4 * j + 1] = __float_as_uint(__uint_as_float(r0[4 * j + 1]) + x0.y);
+            r0[4 * j + 2] = __float_as_uint(__uint_as_float(r0[4 * j + 2]) + x0.z);
+            r0[4 * j + 3] = __float_as_uint(__uint_as_float(r0[4 * j + 3]) + x0.w);
+            r1[4 * j] = __float_as_uint(__uint_as_float(r1[4 * j]) + x1.x);
+            r1[4 * j + 1] = __float_as_uint(__uint_as_float(r1[4 * j + 1]) + x1.y);
+            r1[4 * j + 2] = __float_as_uint(__uint_as_float(r1[4 * j + 2]) + x1.z);
+            r1[4 * j + 3] = __float_as_uint(__uint_as_float(r1[4 * j + 3]) + x1.w);
+          }
+          uint8_t* buf = stg + ((c / 64) & 1) * 4096;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* src = j < 4 ? &r0[8 * j] : &r1[8 * (j - 4)];
+            uint4 v;
+            v.x = pack_half2(p.alpha * __uint_as_float(src[0]), p.alpha * __uint_as_float(src[1]));
+            v.y = pack_half2(p.alpha * __uint_as_float(src[2]), p.alpha * __uint_as_float(src[3]));
+            v.z = pack_half2(p.alpha * __uint_as_float(src[4]), p.alpha * __uint_as_float(src[5]));
+            v.w = pack_half2(p.alpha * __uint_as_float(src[6]), p.alpha * __uint_as_float(src[7]));
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((uint32_t(j) ^ (lane & 7u)) * 16)) = v;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, buf, int(col0 + c), int(tm * BM + q * 32));
+            bulk_commit_group();
+          }
+        }
+      } else if (!u.partial && p.tma_store) {
         // 64-column chunks: TMEM -> registers -> fp16 -> 128-byte-swizzled
         // smem rows (conflict-free) -> one TMA store of 32 rows x 64 columns
         // per warp. Two staging buffers per warp; TMA clips the ragged edge.
@@ -486,7 +579,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (p.ksplit2)
+    cluster_sync();  // rank 0 is done with the DSMEM traffic before either CTA exits
+  else
+    __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -520,6 +616,7 @@ int configure_once(int device) {
 
 struct Plan {
   int bn;
+  bool ksplit2;  // 2-CTA clusters, each tile's K split in halves (grid = 2 x tiles)
   uint32_t tiles_m, tiles_n, kblocks, tiles;
   uint32_t grid;
   uint32_t dp_tiles, sk_tiles;
@@ -651,6 +748,34 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   p.sk_iters = pl.sk_iters;
   p.group_m = 16;
   p.status = dev->status_word;
+  // Few tiles, long K, C through TMA: split each 128 x 128 tile's K over a
+  // 2-CTA cluster that reduces through DSMEM, instead of stream-K partials in
+  // global memory whose fix-up forms a tail (skinny 128 x 8192 x 16384).
+  {
+    const uint32_t t128 = ((M + BM - 1) / BM) * ((N + 127) / 128);
+    const uint32_t kb = (K + BK - 1) / BK;
+    const uint32_t sms = uint32_t(dev->num_sms);
+    if (o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 && tma_store && kb >= 64 &&
+        2 * t128 <= sms && 8 * t128 >= 3 * sms) {
+      if (pl.bn != 128) {
+        pl = plan_for(M, N, K, 128, o, dev->num_sms);
+        // the "nt" B box is BN rows tall; the "nn" box does not depend on BN
+        if (!b_kn &&
+            encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK, 128, kSwizzleK))
+          return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
+        p.tiles_n = pl.tiles_n;
+      }
+      pl.ksplit2 = true;
+      pl.sk_tiles = 0;
+      pl.dp_tiles = pl.tiles;
+      pl.sk_iters = 0;
+      pl.grid = 2 * pl.tiles;
+      p.dp_tiles = pl.dp_tiles;
+      p.sk_tiles = 0;
+      p.sk_iters = 0;
+      p.ksplit2 = 1;
+    }
+  }
   if (pl.sk_tiles) {
     const size_t need = kWsCounterBytes + size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float);
     if (!workspace) {
@@ -675,8 +800,25 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
     case 128:
       if ((rc = configure_once<128>(dev->ordinal)))
         return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-      hgemm_persistent_kernel<128>
-          <<<pl.grid, kThreads, Cfg<128>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
+      if (pl.ksplit2) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(pl.grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Cfg<128>::kSmemBytes;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<128>, tmA, tmB, tmC, p);
+        if (e != cudaSuccess) return launch_error(e, "hgemm: cluster launch failed");
+      } else {
+        hgemm_persistent_kernel<128>
+            <<<pl.grid, kThreads, Cfg<128>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
+      }
       break;
     default:
       if ((rc = configure_once<64>(dev->ordinal)))

@@ -82,6 +82,29 @@ def test_hgemm_skinny_config_sampled(felix):
     assert_fp16_close(ref, out, ctx="skinny sampled")
 
 
+@pytest.mark.parametrize("nt", [True, False])
+@pytest.mark.parametrize("M,N,K", [(128, 8192, 8192), (200, 4096, 4096)])
+def test_hgemm_cluster_split_k(felix, nt, M, N, K):
+    # few 128 x 128 tiles and a long K: each tile's K is split over a 2-CTA
+    # cluster that reduces through DSMEM (the automatic plan); sampled columns
+    # against the oracle, and bit-identical on a second call
+    g = torch.Generator().manual_seed(M + N + K)
+    A = ((torch.rand(M, K, generator=g) * 2 - 1) * 0.05).half()
+    B = ((torch.rand(N, K, generator=g) * 2 - 1) * 0.05).half()
+    Bd = B.cuda() if nt else B.t().contiguous().cuda()
+    lay = felix.B_NK if nt else felix.B_KN
+    C = torch.empty(M, N, dtype=torch.half, device="cuda")
+    felix.hgemm(A.cuda(), Bd, C, b_layout=lay)
+    torch.cuda.synchronize()
+    out = C.cpu().numpy()
+    cols = np.r_[0:40, N // 2 - 7:N // 2 + 9, N - 40:N]
+    ref = oracle.hgemm(A.numpy(), B[cols].numpy(), True)
+    assert_fp16_close(ref, out[:, cols].astype(np.float64), ctx="cluster split-K")
+    felix.hgemm(A.cuda(), Bd, C, b_layout=lay)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out, C.cpu().numpy())
+
+
 def test_hgemm_config2_sampled_rows(felix):
     from sion_b200.workloads import HGEMM_4096, gemm_inputs
     A, B = gemm_inputs(HGEMM_4096)
