@@ -72,11 +72,14 @@ FA_8192_CAUSAL = AttnConfig("flash_attn_fwd_causal_f16_4x32x8192x128", 4, 32, 81
                             causal=True)
 FA_BWD_8192 = AttnConfig("flash_attn_bwd_f16_4x32x8192x128", 4, 32, 8192, 128, 3,
                          backward=True)
+# a smaller backward case for detailed ncu captures (1/8 of the (b, h, query) rows)
+FA_BWD_4096 = AttnConfig("flash_attn_bwd_f16_2x16x4096x128", 2, 16, 4096, 128, 3,
+                         backward=True)
 HGEMM_16384 = GemmConfig("hgemm_f16_16384_nt", 16384, 16384, 16384, "f16", "nk", "uniform", 1.0,
                          4)
 
 CONFIGS = {c.name: c for c in (SGEMM_1024, HGEMM_4096, HGEMM_SKINNY, FA_8192, HGEMM_16384,
-                               FA_8192_CAUSAL, FA_BWD_8192)}
+                               FA_8192_CAUSAL, FA_BWD_8192, FA_BWD_4096)}
 
 
 def _draw(gen: torch.Generator, shape, dist: str, std: float) -> torch.Tensor:
