@@ -117,6 +117,19 @@ int felix_hgemm_ex(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* 
                    int max_ctas, void* workspace, size_t workspace_bytes, void* stream);
 int felix_hgemm_workspace_size(uint32_t M, uint32_t N, uint32_t K, int block_n, int stream_k,
                                int max_ctas, size_t* bytes);
+/*
+ * felix_hgemm_ex plus cta_pair (no reference counterpart): 0 auto (currently
+ * off), 1 off, 2 = 256 x 256 tiles computed by 2-CTA clusters with
+ * cta_group::2 MMAs (each CTA loads half of the tile's B, the leader issues
+ * M = 256 MMAs); block_n must then be 0 or 256. Workspace size from
+ * felix_hgemm_workspace_size2 with the same options.
+ */
+int felix_hgemm_ex2(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* A,
+                    const void* B, float beta, void* C, int b_layout, int block_n, int stream_k,
+                    int max_ctas, int cta_pair, void* workspace, size_t workspace_bytes,
+                    void* stream);
+int felix_hgemm_workspace_size2(uint32_t M, uint32_t N, uint32_t K, int block_n, int stream_k,
+                                int max_ctas, int cta_pair, size_t* bytes);
 
 /*
  * Flash-attention forward, fp16, no mask: O = softmax(Q K^T * scale) V per

@@ -41,6 +41,12 @@ _SIGS = {
                                                      C.c_void_p]),
     "felix_hgemm_workspace_size": (C.c_int, [C.c_uint32] * 3 + [C.c_int, C.c_int, C.c_int,
                                                                  C.POINTER(C.c_size_t)]),
+    "felix_hgemm_ex2": (C.c_int, [C.c_uint32] * 3 + [C.c_float, C.c_void_p, C.c_void_p,
+                                                      C.c_float, C.c_void_p, C.c_int, C.c_int,
+                                                      C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                                      C.c_size_t, C.c_void_p]),
+    "felix_hgemm_workspace_size2": (C.c_int, [C.c_uint32] * 3 + [C.c_int] * 4 +
+                                    [C.POINTER(C.c_size_t)]),
     "felix_flash_attn_fwd": (C.c_int, [C.c_void_p] * 5 + [C.c_uint32] * 4 + [C.c_float,
                                                                             C.c_void_p]),
     "felix_flash_attn_bwd": (C.c_int, [C.c_void_p] * 9 + [C.c_uint32] * 4 +
@@ -131,10 +137,16 @@ def sgemm_noalloc(A, B, C_out, alpha=1.0, beta=0.0, split_k=0, stream=None):
 
 
 def hgemm(A, B, C_out, alpha=1.0, beta=0.0, b_layout=B_NK, block_n=None, stream_k=None,
-          max_ctas=None, workspace=None, stream=None):
+          max_ctas=None, workspace=None, stream=None, cta_pair=None):
     M, K = A.shape
     N = B.shape[0] if b_layout == B_NK else B.shape[1]
     L = lib()
+    if cta_pair is not None:
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        check(L.felix_hgemm_ex2(M, N, K, alpha, _ptr(A), _ptr(B), beta, _ptr(C_out), b_layout,
+                                int(block_n or 0), int(stream_k or 0), int(max_ctas or 0),
+                                int(cta_pair), _ptr(workspace), ws_bytes, _stream(stream)))
+        return C_out
     if block_n is None and stream_k is None and max_ctas is None and workspace is None:
         check(L.felix_hgemm(M, N, K, alpha, _ptr(A), _ptr(B), beta, _ptr(C_out), b_layout,
                             _stream(stream)))
@@ -149,6 +161,13 @@ def hgemm(A, B, C_out, alpha=1.0, beta=0.0, b_layout=B_NK, block_n=None, stream_
 def hgemm_workspace_size(M, N, K, block_n=0, stream_k=0, max_ctas=0) -> int:
     n = C.c_size_t(0)
     check(lib().felix_hgemm_workspace_size(M, N, K, block_n, stream_k, max_ctas, C.byref(n)))
+    return n.value
+
+
+def hgemm_workspace_size2(M, N, K, block_n=0, stream_k=0, max_ctas=0, cta_pair=0) -> int:
+    n = C.c_size_t(0)
+    check(lib().felix_hgemm_workspace_size2(M, N, K, block_n, stream_k, max_ctas, cta_pair,
+                                            C.byref(n)))
     return n.value
 
 

@@ -322,6 +322,40 @@ int felix_hgemm_ex(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* 
                              static_cast<cudaStream_t>(stream)));
 }
 
+int felix_hgemm_ex2(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* A, const void* B,
+                    float beta, void* C, int b_layout, int block_n, int stream_k, int max_ctas,
+                    int cta_pair, void* workspace, size_t workspace_bytes, void* stream) {
+  if (b_layout != FELIX_B_KN && b_layout != FELIX_B_NK)
+    return api_error("hgemm: b_layout must be FELIX_B_KN or FELIX_B_NK").type;
+  if (stream_k < 0 || stream_k > 2) return api_error("hgemm: stream_k must be 0, 1 or 2").type;
+  if (max_ctas < 0) return api_error("hgemm: max_ctas must be >= 0").type;
+  if (cta_pair < 0 || cta_pair > 2) return api_error("hgemm: cta_pair must be 0, 1 or 2").type;
+  if (cta_pair == 2 && block_n != 0 && block_n != 256)
+    return api_error("hgemm: CTA pairs use 256-wide tiles (block_n 0 or 256)").type;
+  HgemmOptions o;
+  o.block_n = block_n;
+  o.stream_k = stream_k;
+  o.max_ctas = max_ctas;
+  o.cta_pair = cta_pair;
+  return finish(hgemm_launch(M, N, K, alpha, static_cast<const __half*>(A),
+                             static_cast<const __half*>(B), beta, static_cast<__half*>(C),
+                             b_layout == FELIX_B_KN, o, workspace, workspace_bytes,
+                             static_cast<cudaStream_t>(stream)));
+}
+
+int felix_hgemm_workspace_size2(uint32_t M, uint32_t N, uint32_t K, int block_n, int stream_k,
+                                int max_ctas, int cta_pair, size_t* bytes) {
+  DeviceInfo* d = current_device_info();
+  if (!d) return launch_error(cudaGetLastError(), "no device").type;
+  HgemmOptions o;
+  o.block_n = block_n;
+  o.stream_k = stream_k;
+  o.max_ctas = max_ctas;
+  o.cta_pair = cta_pair;
+  if (bytes) *bytes = hgemm_workspace_bytes(M, N, K, o, d->num_sms);
+  return FELIX_SUCCESS;
+}
+
 int felix_hgemm_workspace_size(uint32_t M, uint32_t N, uint32_t K, int block_n, int stream_k,
                                int max_ctas, size_t* bytes) {
   DeviceInfo* d = current_device_info();

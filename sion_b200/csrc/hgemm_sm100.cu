@@ -47,11 +47,15 @@ static_assert(BK == 32 || BK == 64, "k step");
 constexpr int kSwizzleK = BK * 2;  // bytes per K-major operand row = swizzle span
 constexpr int kThreads = 192;
 
-template <int BN>
+// CG = 2: CTA pairs (cta_group::2): a 2-CTA cluster computes a 256 x BN tile;
+// each CTA holds 128 rows of A and BN / 2 rows (N) of B, the leader issues the
+// MMAs (M = 256) and each CTA's TMEM gets its own 128 rows of the tile.
+template <int BN, int CG = 1>
 struct Cfg {
-  static constexpr int kStages = (192 * 1024) / ((BM + BN) * BK * 2);
+  static constexpr int kBRows = BN / CG;  // B rows (N) loaded by one CTA
+  static constexpr int kStages = (192 * 1024) / ((BM + kBRows) * BK * 2);
   static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   // epilogue staging for TMA stores: 4 warps x 2 buffers x (32 rows x 128 B)
@@ -71,6 +75,7 @@ struct Params {
   uint32_t group_m;
   uint32_t tma_store;     // 1: epilogue writes C through smem + TMA (beta == 0)
   uint32_t ksplit2;       // 1: 2-CTA clusters split each tile's K in halves (see below)
+  uint32_t pair;          // 1: CTA pairs (cta_group::2); units and slots are per pair
   float* ws_partials;     // [gridDim.x][2] slots of BM*BN fp32, see partial_index()
   unsigned* ws_counters;  // [sk_tiles], zero between launches
   unsigned* status;       // watchdog word
@@ -97,8 +102,8 @@ struct Sched {
   uint32_t ksplit_rank;  // cluster split-K: 0 or 1 (which half of K); 2 = unit taken
   __device__ __forceinline__ void init(const Params& p) {
     ksplit_rank = p.ksplit2 ? (blockIdx.x & 1u) : 3u;
-    cta = blockIdx.x;
-    P = gridDim.x;
+    cta = p.pair ? blockIdx.x >> 1 : blockIdx.x;
+    P = p.pair ? gridDim.x >> 1 : gridDim.x;
     sk_tiles = p.sk_tiles;
     tiles = p.sk_tiles + p.dp_tiles;
     KB = p.kblocks;
@@ -212,12 +217,14 @@ __device__ __forceinline__ void store_row_chunk(const Params& p, uint32_t row, u
   }
 }
 
-template <int BN>
+template <int BN, int CG = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmC, const Params p) {
-  using C_ = Cfg<BN>;
+  using C_ = Cfg<BN, CG>;
+  static_assert(CG == 1 || BN == 256, "CTA pairs use 256-wide tiles");
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
   constexpr int S = C_::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -250,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], 4 * CG);  // a pair's leader counts both CTAs' epilogue warps
     }
     mbar_init(drain, 1);
     mbar_init(recv, 128);  // one arrival per epilogue thread of rank 1
@@ -261,15 +268,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmB);
     if (p.tma_store) tma_prefetch_desc(&tmC);
   }
+  if (CG == 2 || p.ksplit2)
+    cluster_sync();  // the peer uses this CTA's barriers: they must be initialised
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C_::kTmemCols);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, C_::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C_::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  if (p.ksplit2)
-    cluster_sync();  // rank 1 arrives on rank 0's barrier: it must be initialised
-  else
-    __syncthreads();
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -282,10 +293,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t stage = 0, phase = 0;
       uint32_t filled = 0;
       bool ok = true;
+      // loads of a pair's CTAs complete on the leader's barrier
+      auto load2d = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+        if constexpr (CG == 2)
+          tma_load_2d_pair(dst, map, mapa_shared(smem_u32(bar), 0), x, y);
+        else
+          tma_load_2d(dst, map, bar, x, y);
+      };
       while (ok && sc.next(u)) {
         uint32_t tm, tn;
         tile_coords(p, u.tile, tm, tn);
-        const int m0 = int(tm * BM), n0 = int(tn * BN);
+        const int m0 = int(tm * BM * CG + rank * BM), n0 = int(tn * BN + rank * C_::kBRows);
         for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kWdProducerEmpty)) {
             ok = false;
@@ -293,14 +311,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = ring + stage * C_::kStageBytes;
           uint8_t* sb = sa + C_::kABytes;
-          mbar_arrive_expect_tx(&full[stage], C_::kStageBytes);
-          tma_load_2d(sa, &tmA, &full[stage], int(kb * BK), m0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], CG * C_::kStageBytes);
+          load2d(sa, &tmA, &full[stage], int(kb * BK), m0);
           if (p.b_mn_major) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sb + j * (64 * BK * 2), &tmB, &full[stage], n0 + 64 * j, int(kb * BK));
+            for (int j = 0; j < C_::kBRows / 64; ++j)
+              load2d(sb + j * (64 * BK * 2), &tmB, &full[stage], n0 + 64 * j, int(kb * BK));
           } else {
-            tma_load_2d(sb, &tmB, &full[stage], int(kb * BK), n0);
+            load2d(sb, &tmB, &full[stage], int(kb * BK), n0);
           }
           ++filled;
           if (++stage == NS) {
@@ -310,8 +328,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Drain: wait (bounded) for the last fill of every stage so that no TMA
-      // write is in flight when the CTA exits.
-      const uint32_t n = filled < NS ? filled : NS;
+      // write is in flight when the CTA exits (a pair's leader counts both
+      // CTAs' bytes; the final cluster barrier holds the peer until then).
+      const uint32_t n = rank == 0 ? (filled < NS ? filled : NS) : 0u;
       for (uint32_t i = 0; i < n; ++i) {
         // stage of the i-th most recent fill, and the phase parity it filled
         const uint32_t f = filled - 1 - i;
@@ -323,8 +342,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_f16_f32(BM, BN, false, p.b_mn_major != 0);
+    if (lane == 0 && rank == 0) {  // a pair's leader issues for both CTAs
+      const uint32_t idesc = make_idesc_f16_f32(BM * CG, BN, false, p.b_mn_major != 0);
+      // completion signals go to the barrier in every CTA of the group
+      auto commit_all = [&](uint64_t* bar) {
+        if constexpr (CG == 2) {
+          const uint32_t a = smem_u32(bar);
+          umma_commit_pair(a);
+          umma_commit_pair(mapa_shared(a, 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
       Sched sc;
       sc.init(p);
       Unit u;
@@ -359,20 +388,26 @@ __global__ void __launch_bounds__(kThreads, 1)
               bd = p.b_mn_major ? make_sdesc_sw128(b0 + k * 2048, 64 * BK * 2, 1024)
                                 : make_sdesc_sw64(b0 + k * 32, 16, 512);
             }
-            umma_f16_ss(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+            if constexpr (CG == 2)
+              umma_f16_ss_pair(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+            else
+              umma_f16_ss(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          commit_all(&empty[stage]);
           if (++stage == NS) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[buf]);
+        commit_all(&tfull[buf]);
         ++i;
       }
       // Wait (bounded) until every issued MMA has completed before teardown.
-      umma_commit(drain);
+      if constexpr (CG == 2)
+        umma_commit_pair(smem_u32(drain));
+      else
+        umma_commit(drain);
       int dummy = 0;
       mbar_wait(drain, 0, &dummy, p.status, kWdDrain, 100000000ull);
     }
@@ -392,7 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       uint32_t tm, tn;
       tile_coords(p, u.tile, tm, tn);
-      const uint32_t row = tm * BM + row_in_tile;
+      const uint32_t row0 = tm * BM * CG + rank * BM;  // this CTA's first row of the tile
+      const uint32_t row = row0 + row_in_tile;
       const uint32_t col0 = tn * BN;
       const uint32_t taddr = tmem_base + ((q * 32u) << 16) + buf * BN;
 
@@ -458,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, buf, int(col0 + c), int(tm * BM + q * 32));
+            tma_store_2d(&tmC, buf, int(col0 + c), int(row0 + q * 32));
             bulk_commit_group();
           }
         }
@@ -489,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, buf, int(col0 + c), int(tm * BM + q * 32));
+            tma_store_2d(&tmC, buf, int(col0 + c), int(row0 + q * 32));
             bulk_commit_group();
           }
         }
@@ -507,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         // Stream-K contribution: publish the fp32 partial, take a ticket.
         float4* slot = reinterpret_cast<float4*>(p.ws_partials) +
-                       (size_t(sc.cta) * 2 + u.seg) * (BM * BN / 4);
+                       ((size_t(sc.cta) * 2 + u.seg) * CG + rank) * (BM * BN / 4);
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -526,9 +562,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t c_last = sc.cta_of(tile_first + sc.KB - 1);
         const uint32_t ncontrib = c_last - c_first + 1;
         if (epi_tid == 0) {
-          const unsigned old = atomicAdd(&p.ws_counters[u.sk], 1u);
+          const unsigned old = atomicAdd(&p.ws_counters[u.sk * CG + rank], 1u);
           const uint32_t last = (old == ncontrib - 1) ? 1u : 0u;
-          if (last) atomicExch(&p.ws_counters[u.sk], 0u);
+          if (last) atomicExch(&p.ws_counters[u.sk * CG + rank], 0u);
           *bcast = last;
         }
         named_barrier_sync(1, 128);
@@ -546,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t cc = c_first; cc <= c_last; ++cc) {
               const uint32_t seg = (sc.I * cc / sc.P) / sc.KB == u.sk ? 0u : 1u;
               const float4* s4 = reinterpret_cast<const float4*>(p.ws_partials) +
-                                 (size_t(cc) * 2 + seg) * (BM * BN / 4);
+                                 ((size_t(cc) * 2 + seg) * CG + rank) * (BM * BN / 4);
               float4 x0[8], x1[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
@@ -570,7 +606,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (lane == 0) {
+        if (CG == 2 && rank == 1)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));  // the leader's MMA waits
+        else
+          mbar_arrive(&tempty[buf]);
+      }
       ++i;
     }
     // staging smem must stay valid until the TMA stores have read it
@@ -579,14 +620,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
-  if (p.ksplit2)
-    cluster_sync();  // rank 0 is done with the DSMEM traffic before either CTA exits
+  if (CG == 2 || p.ksplit2)
+    cluster_sync();  // no CTA exits while its peer may still use its memory
   else
     __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, C_::kTmemCols);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem_base, C_::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, C_::kTmemCols);
   }
 }
 
@@ -600,14 +644,14 @@ using namespace felix_sm100::hgemm;
 
 namespace {
 
-template <int BN>
+template <int BN, int CG = 1>
 int configure_once(int device) {
   static int done[64] = {0};
   if (device < 0 || device >= 64) return -1;
   if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(felix_sm100::hgemm::hgemm_persistent_kernel<BN>,
+    cudaError_t e = cudaFuncSetAttribute(felix_sm100::hgemm::hgemm_persistent_kernel<BN, CG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg<BN>::kSmemBytes);
+                                         Cfg<BN, CG>::kSmemBytes);
     if (e != cudaSuccess) return int(e);
     done[device] = 1;
   }
@@ -616,6 +660,7 @@ int configure_once(int device) {
 
 struct Plan {
   int bn;
+  bool pair;     // CTA pairs: tiles, grid and units counted per pair (grid launched x 2)
   bool ksplit2;  // 2-CTA clusters, each tile's K split in halves (grid = 2 x tiles)
   uint32_t tiles_m, tiles_n, kblocks, tiles;
   uint32_t grid;
@@ -668,6 +713,15 @@ Plan plan_for(uint32_t M, uint32_t N, uint32_t K, int bn, const HgemmOptions& o,
 }
 
 Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int num_sms) {
+  if (o.cta_pair == 2) {
+    // 256 x 256 tiles, one unit per CTA pair: plan as 128-row tiles of
+    // ceil(M / 2) rows over num_sms / 2 "CTAs"
+    HgemmOptions op = o;
+    if (op.max_ctas > 0) op.max_ctas = op.max_ctas / 2 > 0 ? op.max_ctas / 2 : 1;
+    Plan pl = plan_for((M + 1) / 2, N, K, 256, op, num_sms / 2);
+    pl.pair = true;
+    return pl;
+  }
   if (o.block_n) return plan_for(M, N, K, o.block_n, o, num_sms);
   // Fewer 128x256 tiles than SMs (skinny / decode shapes): the stream-K
   // fix-up of 128 KB partials with many contributors per tile becomes a
@@ -686,7 +740,7 @@ size_t hgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const HgemmOpti
                              int num_sms) {
   Plan pl = make_plan(M, N, K, o, num_sms);
   if (pl.sk_tiles == 0) return 0;
-  return kWsCounterBytes + size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float);
+  return kWsCounterBytes + size_t(pl.grid) * 2 * (pl.pair ? 2 : 1) * BM * pl.bn * sizeof(float);
 }
 
 FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __half* A,
@@ -719,7 +773,9 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   if (b_kn)
     rc = encode_tmap_2d_f16(&tmB, B, N, K, uint64_t(N) * 2, 64, BK);
   else
-    rc = encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK, pl.bn, kSwizzleK);
+    // (a CTA of a pair loads half of the tile's B rows)
+    rc = encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK,
+                                    pl.pair ? pl.bn / 2 : pl.bn, kSwizzleK);
   if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
 
   // C through TMA when nothing has to be read back (beta == 0) and its rows
@@ -755,7 +811,8 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
     const uint32_t t128 = ((M + BM - 1) / BM) * ((N + 127) / 128);
     const uint32_t kb = (K + BK - 1) / BK;
     const uint32_t sms = uint32_t(dev->num_sms);
-    if (o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 && tma_store && kb >= 64 &&
+    if (!pl.pair && o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 && tma_store &&
+        kb >= 64 &&
         2 * t128 <= sms && 8 * t128 >= 3 * sms) {
       if (pl.bn != 128) {
         pl = plan_for(M, N, K, 128, o, dev->num_sms);
@@ -776,8 +833,12 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
       p.ksplit2 = 1;
     }
   }
+  p.pair = pl.pair ? 1u : 0u;
   if (pl.sk_tiles) {
-    const size_t need = kWsCounterBytes + size_t(pl.grid) * 2 * BM * pl.bn * sizeof(float);
+    if (uint64_t(pl.sk_tiles) * (pl.pair ? 2 : 1) > kWsMaxCounters)
+      return api_error("hgemm: too many stream-K tiles");
+    const size_t need =
+        kWsCounterBytes + size_t(pl.grid) * 2 * (pl.pair ? 2 : 1) * BM * pl.bn * sizeof(float);
     if (!workspace) {
       workspace = library_workspace(dev, stream, need);
       if (!workspace) return launch_error(cudaErrorMemoryAllocation, "hgemm: workspace");
@@ -790,6 +851,25 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   }
 
   cudaError_t e;
+  if (pl.pair) {
+    if ((rc = configure_once<256, 2>(dev->ordinal)))
+      return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * pl.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg<256, 2>::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<256, 2>, tmA, tmB, tmC, p);
+    if (e != cudaSuccess) return launch_error(e, "hgemm: CTA-pair launch failed");
+    return FelixCode{FELIX_SUCCESS, cudaSuccess};
+  }
   switch (pl.bn) {
     case 256:
       if ((rc = configure_once<256>(dev->ordinal)))

@@ -177,6 +177,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 // Load for a CTA pair (cta_group::2): the tile lands in this CTA's shared
 // memory and its bytes are signalled on the mbarrier at `bar_cluster_addr`,
 // which may belong to the other CTA of the pair (the MMA leader).
+// 2-D tile load of one CTA of a pair; completion is counted on the leader's
+// mbarrier (address from mapa_shared).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster_addr, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map,
                                                  uint32_t bar_cluster_addr, int32_t x, int32_t y,
                                                  int32_t z) {

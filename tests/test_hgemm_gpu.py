@@ -134,3 +134,28 @@ def test_hgemm_rejects_unaligned_k(felix):
     with pytest.raises(felix.FelixError) as e:
         felix.hgemm(A, B, C)
     assert e.value.code == felix.API_ERROR
+
+
+@pytest.mark.parametrize("nt", [True, False])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 1024), (300, 520, 200),
+                                   (1024, 1024, 2048)])
+def test_hgemm_cta_pair(felix, nt, M, N, K):
+    # 256 x 256 tiles on 2-CTA clusters (cta_group::2 MMAs issued by the leader)
+    ref, out = _run(felix, M, N, K, nt=nt, cta_pair=2)
+    assert_fp16_close(ref, out, ctx="CTA pair")
+
+
+@pytest.mark.parametrize("nt", [True, False])
+def test_hgemm_cta_pair_stream_k(felix, nt):
+    # incomplete last wave of pair tiles spread by k-iterations over few pairs,
+    # deterministic fix-up
+    M, N, K = 768, 1280, 2048
+    ref, out = _run(felix, M, N, K, nt=nt, cta_pair=2, stream_k=2, max_ctas=6)
+    assert_fp16_close(ref, out, ctx="CTA pair stream-K")
+    _, out2 = _run(felix, M, N, K, nt=nt, cta_pair=2, stream_k=2, max_ctas=6)
+    np.testing.assert_array_equal(out, out2)
+
+
+def test_hgemm_cta_pair_alpha_beta(felix):
+    ref, out = _run(felix, 384, 512, 256, nt=True, alpha=0.5, beta=-0.75, cta_pair=2)
+    assert_fp16_close(ref, out, ctx="CTA pair alpha/beta")
