@@ -8,25 +8,10 @@
 // dP = dO V^T, Delta = rowsum(dO * O), dS = P * (dP - Delta),
 // dK = scale * dS^T Q, dQ = scale * dS K.
 //
-// Kernel layout: one CTA per (b, h) and 128-key block j, looping over the
-// 128-query blocks i (from the diagonal block when causal). Everything is
-// computed in the "transposed" orientation so that TMEM lanes are keys:
-//   S^T  = K_j Q_i^T        (SS MMA)              -> TMEM cols [0, 128)
-//   dP^T = V_j dO_i^T       (SS MMA)              -> TMEM cols [128, 256)
-//   P^T, dS^T (fp16) overwrite the first half of each 64-column half of
-//   those regions (TMEM A operands); dS is also written to shared memory as
-//   an MN-major tile;
-//   dV_j += P^T dO_i        (TS MMA)              -> TMEM cols [256, 256 + D)
-//   dK_j += dS^T Q_i        (TS MMA)              -> TMEM cols [384, 384 + D)
-//   dQ_i  = dS K_j          (SS MMA, A MN-major)  -> TMEM cols [0, D)
-// dQ_i is read out of TMEM in 32 x 32 fp32 boxes, staged in shared memory
-// (128-byte swizzle) and added into an fp32 buffer [BH][S][D] with TMA tensor
-// reductions (cp.reduce.async.bulk.tensor ... add), which run asynchronously and
-// clip rows past S; a small kernel scales and converts the buffer to fp16 at
-// the end. MMAs of a CTA execute in issue order, so dQ_i may overwrite the P^T
-// columns right behind the dV MMA that reads them. Warps: 0 TMA loader, 1 MMA
-// issuer, 4-11 two warpgroups of element-wise work (one key row per thread,
-// each warpgroup one half of the query columns / of D).
+// Kernel layout: one CTA per (b, h) and 128-key block j (TMEM lanes = its
+// keys), looping over 128-query blocks i (from the diagonal block when
+// causal); every MMA is N >= 64 wide and 128 queries deep (narrower MMAs cost
+// as much per instruction on this tensor core). See the pipe namespace below.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -36,21 +21,18 @@
 #include "sm100_ptx.cuh"
 
 // Timing experiments only (results are wrong when set): skip the dQ
-// reductions / the exponentials.
+// reductions.
 #ifndef FELIX_FA_BWD_EXP_NO_DQRED
 #define FELIX_FA_BWD_EXP_NO_DQRED 0
 #endif
-#ifndef FELIX_FA_BWD_EXP_NO_EW
-#define FELIX_FA_BWD_EXP_NO_EW 0
-#endif
-// bit mask of MMA groups left out of the D = 128 kernel: 1 S^T, 2 dP^T, 4 dV,
-// 8 dK, 16 dQ^T (their commits stay, so the barrier protocol is unchanged)
+// bit mask of MMA groups left out: 1 S^T, 2 dP^T, 4 dV, 8 dK, 16 dQ (their
+// commits stay, so the barrier protocol is unchanged)
 #ifndef FELIX_FA_BWD_EXP_SKIP
 #define FELIX_FA_BWD_EXP_SKIP 0
 #endif
 
 // Timing experiments only: per-role cycle counters around the waits of the
-// D = 128 kernel, summed over all CTAs (read with felix_debug_bwd_trace, which
+// kernel, summed over all CTAs (read with felix_debug_bwd_trace, which
 // exists only in such builds).
 #ifndef FELIX_FA_BWD_TRACE
 #define FELIX_FA_BWD_TRACE 0
@@ -70,27 +52,6 @@ namespace felix_sm100 {
 namespace attn_bwd {
 
 constexpr int kBlk = 128;  // keys per CTA, queries per loop step
-constexpr int kThreads = 384;
-constexpr int kEwWarps = 8;  // element-wise warps (two warpgroups)
-
-template <int D>
-struct Cfg {
-  static constexpr int kChunks = D / 64;
-  static constexpr int kTile = kBlk * D * 2;  // one 128 x D fp16 tile
-  static constexpr int kKOff = 0;
-  static constexpr int kVOff = kKOff + kTile;
-  static constexpr int kQOff = kVOff + kTile;         // Q_i, two stages
-  static constexpr int kDOOff = kQOff + 2 * kTile;    // dO_i, two stages
-  // dS: 128 queries x 128 keys fp16; after the dQ MMA has read it, each
-  // element-wise warp's 4 KB of it is that warp's dQ staging box
-  static constexpr int kDSOff = kDOOff + 2 * kTile;
-  // lse2[2][128], delta[2][128]: double-buffered by step parity
-  static constexpr int kVecOff = kDSOff + kBlk * kBlk * 2;
-  static constexpr int kBarOff = kVecOff + 4 * kBlk * 4;
-  // No alignment slack (D = 128 needs all but 768 B of the 227 KB): the
-  // kernel checks that the dynamic shared memory starts 1024-byte aligned.
-  static constexpr int kSmemBytes = kBarOff + 256;
-};
 
 struct Params {
   const float* lse;     // [BH, S] natural log (forward output)
@@ -125,301 +86,16 @@ __device__ __forceinline__ uint64_t mnmajor(uint32_t tile, int k) {
   return make_sdesc_sw128(tile + uint32_t(k) * 2048, kBlk * 128, 1024);
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
-    flash_attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ,
-                          const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmV,
-                          const __grid_constant__ CUtensorMap tmDO,
-                          const __grid_constant__ CUtensorMap tmDQ, const Params p) {
-  using C_ = Cfg<D>;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = smem_raw;
-  if (smem_u32(smem) & 1023u) {  // uniform over the CTA: nobody touches a barrier
-    if (threadIdx.x == 0) atomicCAS(p.status, 0u, unsigned(kWdSmemAlign));
-    return;
-  }
-  float* s_vec = reinterpret_cast<float*>(smem + C_::kVecOff);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
-  uint64_t* kv_full = bars;        // K_j, V_j landed
-  uint64_t* st_full = bars + 1;    // S^T, dP^T in TMEM
-  uint64_t* p_ready = bars + 2;    // P^T, dS^T in TMEM, dS in smem (8 warp arrivals)
-  uint64_t* dq_full = bars + 3;    // dQ_i in TMEM
-  uint64_t* dq_free = bars + 4;    // dQ_i read out (8 warp arrivals)
-  uint64_t* done = bars + 5;       // every MMA complete
-  uint64_t* qdo_full = bars + 6;   // [2] Q_i, dO_i landed in stage i % 2
-  uint64_t* qdo_empty = bars + 8;  // [2] MMAs of step i done with stage i % 2
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const uint32_t bh = blockIdx.x / p.n_blk;
-  const uint32_t j = blockIdx.x % p.n_blk;  // key block
-  const uint32_t i0 = p.causal ? j : 0;     // first query block
-  const uint32_t n_i = p.n_blk - i0;
-
-  if (threadIdx.x == 0) {
-    for (int b = 0; b < 10; ++b) mbar_init(&bars[b], (b == 2 || b == 4) ? kEwWarps : 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-    tma_prefetch_desc(&tmDO);
-    tma_prefetch_desc(&tmDQ);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
-
-  if (warp == 0) {
-    // ---------------------------------------------------------------- loader
-    if (elect_one()) {
-      mbar_arrive_expect_tx(kv_full, 2 * C_::kTile);
-#pragma unroll
-      for (int c = 0; c < C_::kChunks; ++c) {
-        tma_load_3d(smem + C_::kKOff + c * (kBlk * 128), &tmK, kv_full, 64 * c, int(j * kBlk),
-                    int(bh));
-        tma_load_3d(smem + C_::kVOff + c * (kBlk * 128), &tmV, kv_full, 64 * c, int(j * kBlk),
-                    int(bh));
-      }
-      uint32_t filled = 0;
-      for (uint32_t s = 0; s < n_i; ++s) {
-        const uint32_t i = i0 + s;
-        const uint32_t st = s & 1u, use = s >> 1;
-        if (!mbar_wait(qdo_empty + st, (use & 1u) ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
-        mbar_arrive_expect_tx(qdo_full + st, 2 * C_::kTile);
-#pragma unroll
-        for (int c = 0; c < C_::kChunks; ++c) {
-          tma_load_3d(smem + C_::kQOff + st * C_::kTile + c * (kBlk * 128), &tmQ, qdo_full + st,
-                      64 * c, int(i * kBlk), int(bh));
-          tma_load_3d(smem + C_::kDOOff + st * C_::kTile + c * (kBlk * 128), &tmDO,
-                      qdo_full + st, 64 * c, int(i * kBlk), int(bh));
-        }
-        ++filled;
-      }
-      // drain: the last load of each stage has landed
-      int dummy = 0;
-      mbar_wait(kv_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
-      for (uint32_t s = filled > 2 ? filled - 2 : 0; s < filled; ++s)
-        mbar_wait(qdo_full + (s & 1u), (s >> 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t id_st = make_idesc_f16_f32(kBlk, kBlk, false, false);  // S^T, dP^T
-      const uint32_t id_acc = make_idesc_f16_f32(kBlk, D, false, true);     // dV, dK
-      const uint32_t id_dq = make_idesc_f16_f32(kBlk, D, true, true);       // dQ
-      const uint32_t sK = smem_u32(smem + C_::kKOff), sV = smem_u32(smem + C_::kVOff);
-      const uint32_t sDS = smem_u32(smem + C_::kDSOff);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kWdAttnMma);
-      for (uint32_t s = 0; ok && s < n_i; ++s) {
-        const uint32_t ph = s & 1u;
-        const uint32_t st = s & 1u, use = s >> 1;
-        const uint32_t sQ = smem_u32(smem + C_::kQOff + st * C_::kTile);
-        const uint32_t sDO = smem_u32(smem + C_::kDOOff + st * C_::kTile);
-        if (!(ok = mbar_wait(qdo_full + st, use & 1u, abort_flag, p.status, kWdAttnMma))) break;
-        // the dQ of the previous step must have been read out of cols [0, D)
-        if (s > 0 && !(ok = mbar_wait(dq_free, ph ^ 1u, abort_flag, p.status, kWdAttnMma))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k)
-          umma_f16_ss(tmem + kColS, kmajor<kBlk>(sK, k), kmajor<kBlk>(sQ, k), id_st,
-                      k > 0 ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k)
-          umma_f16_ss(tmem + kColDP, kmajor<kBlk>(sV, k), kmajor<kBlk>(sDO, k), id_st,
-                      k > 0 ? 1u : 0u);
-        umma_commit(st_full);
-        if (!(ok = mbar_wait(p_ready, ph, abort_flag, p.status, kWdAttnMma))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < kBlk / 16; ++k)
-          umma_f16_ts(tmem + kColDV, tmem + kColS + packed_col(16 * k), mnmajor(sDO, k), id_acc,
-                      (s > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < kBlk / 16; ++k)
-          umma_f16_ts(tmem + kColDK, tmem + kColDP + packed_col(16 * k), mnmajor(sQ, k), id_acc,
-                      (s > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < kBlk / 16; ++k)
-          umma_f16_ss(tmem + kColS, mnmajor(sDS, k), mnmajor(sK, k), id_dq, k > 0 ? 1u : 0u);
-        umma_commit(qdo_empty + st);
-        umma_commit(dq_full);
-      }
-      umma_commit(done);
-      int dummy = 0;
-      mbar_wait(done, 0, &dummy, p.status, kWdDrain, 100000000ull);
-    }
-  } else if (warp >= 4) {
-    // ---------------------------------------------------------------- element-wise
-    const uint32_t q4 = warp & 3u;         // TMEM lane quadrant
-    const uint32_t g = (warp - 4) >> 2;    // column half handled by this warpgroup
-    const uint32_t r = q4 * 32 + lane;     // key row of this CTA (TMEM lane)
-    const uint32_t key = j * kBlk + r;
-    const uint32_t la = (q4 * 32u) << 16;
-    const uint32_t tid = threadIdx.x - 128;
-    uint8_t* sDS = smem + C_::kDSOff;
-    // dQ staging box: this warp's own 4 KB of the dS tile (free once the dQ
-    // MMA has read it)
-    uint8_t* stg = sDS + (g * 4 + q4) * 4096;
-    const float sl2 = p.scale_log2;
-    bool ok = true;
-    for (uint32_t s = 0; ok && s < n_i; ++s) {
-      const uint32_t ph = s & 1u;
-      const uint32_t i = i0 + s;
-      // per-query vectors of this step (queries past S: P = 0 through lse = +inf);
-      // double-buffered by step parity, so slower threads may still read the
-      // previous step's copy while this one is written
-      float* s_lse2 = s_vec + ph * (2 * kBlk);
-      float* s_delta = s_lse2 + kBlk;
-      if (tid < kBlk) {
-        const uint32_t q = i * kBlk + tid;
-        s_lse2[tid] = q < p.S ? __ldg(p.lse + size_t(bh) * p.S + q) * 1.4426950408889634f
-                              : INFINITY;
-        s_delta[tid] = q < p.S ? __ldg(p.delta + size_t(bh) * p.S + q) : 0.f;
-      }
-      // the dS writes below reuse the staging box: its last reduction must
-      // have been read out of shared memory
-      if (lane == 0) bulk_wait_group_read<0>();
-      named_barrier_sync(1, kEwWarps * 32);
-      if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, kWdAttnSoftmax))) break;
-      tc_fence_after();
-      const bool key_ok = key < p.S;
-#pragma unroll 1
-      for (int c = int(g) * 64; c < int(g) * 64 + 64; c += 32) {
-        uint32_t sr[32], dr[32];
-        tmem_ld_32x32b_x32(tmem + la + kColS + c, sr);
-        tmem_ld_32x32b_x32(tmem + la + kColDP + c, dr);
-        tmem_ld_wait();
-        uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t qi = uint32_t(c + e + h);
-            const uint32_t q = i * kBlk + qi;
-            float pr = FELIX_FA_BWD_EXP_NO_EW
-                           ? __uint_as_float(sr[e + h])
-                           : ex2(fmaf(__uint_as_float(sr[e + h]), sl2, -s_lse2[qi]));
-            if (!key_ok || (p.causal && q < key)) pr = 0.f;
-            pv[h] = pr;
-            dv[h] = pr * (__uint_as_float(dr[e + h]) - s_delta[qi]);
-          }
-          pk[e / 2] = pack_half2(pv[0], pv[1]);
-          dk[e / 2] = pack_half2(dv[0], dv[1]);
-        }
-        // packed fp16 P^T / dS^T: each warpgroup packs its 64 query columns into
-        // the first 32 of them, so it never overwrites columns the other one
-        // is still reading
-        tmem_st_32x32b_x16(tmem + la + kColS + packed_col(c), pk);
-        tmem_st_32x32b_x16(tmem + la + kColDP + packed_col(c), dk);
-        // dS (queries x keys) as an MN-major A tile: query chunk c / 64, row = key r,
-        // 16-byte units swizzled with the row (128-byte swizzle)
-        uint8_t* row = sDS + (c / 64) * (kBlk * 128) + r * 128;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t unit = uint32_t((c % 64) / 8 + u);
-          *reinterpret_cast<uint4*>(row + ((unit ^ (r & 7u)) * 16)) =
-              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
-        }
-      }
-      tmem_st_wait();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);
-      // dQ_i rows (lane = query), columns [g * D / 2, (g + 1) * D / 2) -> staged
-      // 32 x 32 boxes -> TMA reduction into the fp32 accumulator
-      if (!(ok = mbar_wait(dq_full, ph, abort_flag, p.status, kWdAttnSoftmax))) break;
-      tc_fence_after();
-      const uint32_t q0 = i * kBlk + q4 * 32;
-      constexpr int kDqBoxes = D / 64;
-#pragma unroll
-      for (int b = 0; b < kDqBoxes; ++b) {
-        const int c = int(g) * (D / 2) + b * 32;
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + la + kColS + c, v);
-        tmem_ld_wait();
-        if (b == kDqBoxes - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(dq_free);
-        }
-        if (b > 0) {
-          // the previous box's reduction must have been read
-          if (lane == 0) bulk_wait_group_read<0>();
-          __syncwarp();
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<uint4*>(stg + lane * 128 + ((u ^ (lane & 7u)) * 16)) =
-              make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && q0 < p.S && !FELIX_FA_BWD_EXP_NO_DQRED) {
-          tma_reduce_add_3d(&tmDQ, stg, c, int(q0), int(bh));
-        }
-        if (lane == 0) bulk_commit_group();
-      }
-    }
-    // dK_j, dV_j (lane = key) -> fp16, columns [g * D / 2, (g + 1) * D / 2)
-    if (ok && mbar_wait(done, 0, abort_flag, p.status, kWdAttnSoftmax)) {
-      tc_fence_after();
-#pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t col = which ? kColDK : kColDV;
-        const float mul = which ? p.scale : 1.f;
-        __half* out = (which ? p.dK : p.dV) + (size_t(bh) * p.S + key) * D;
-#pragma unroll 1
-        for (int c = int(g) * (D / 2); c < int(g + 1) * (D / 2); c += 32) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tmem + la + col + c, v);
-          tmem_ld_wait();
-          if (key < p.S) {
-            uint4 o4[4];
-            uint32_t* o = reinterpret_cast<uint32_t*>(o4);
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-              o[e] = pack_half2(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(out + c)[e] = o4[e];
-          }
-        }
-      }
-    }
-    // every staged reduction complete before the shared memory goes away
-    if (lane == 0) bulk_wait_group<0>();
-    __syncwarp();
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 // ---------------------------------------------------------------------------
-// D = 128: 128-query steps (every MMA N = 128: narrower MMAs cost as much
-// per instruction on this tensor core) with the work of neighbouring steps
-// interleaved.
+// The kernel (D = 64 or 128): 128-query steps with the work of neighbouring
+// steps interleaved.
 //
 // TMEM (512 columns, lanes = the CTA's 128 keys unless noted):
 //   [0, 128)   S^T(i) fp32; P^T(i) fp16 packed into the first 32 columns of
 //              each 64-query half (TS operand of dV)
 //   [128, 256) dP^T(i) fp32; dS^T(i) fp16 packed the same way (TS operand of
 //              dK); then dQ(i) = dS K (lanes = queries, columns = d)
-//   [256, 384) dV, [384, 512) dK
+//   [256, 256 + D) dV, [384, 384 + D) dK
 // MMA issue order per step i:
 //   dV(i) | S^T(i + 1) | dP^T(i) | dK(i) dQ(i)
 // with the waits: P^T(i) ready; Q(i + 1) loaded; dQ(i - 1) read out; dS(i)
@@ -432,29 +108,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 // one half of the queries (S/P/dS) and one half of d (dQ, dK, dV).
 namespace pipe {
 
-constexpr int kD = 128;
 constexpr int kB = 128;  // keys per CTA, queries per step
 constexpr int kThreads = 384;
 constexpr int kEwWarps = 8;
-constexpr int kTile = kB * kD * 2;  // 32 KB
-constexpr int kKOff = 0;
-constexpr int kVOff = kKOff + kTile;
-constexpr int kQOff = kVOff + kTile;        // [2]
-constexpr int kDOOff = kQOff + 2 * kTile;   // [2]
-// dS (rows = keys, 64-query 128-byte chunks); after the dQ MMA has read it,
-// each element-wise warp's 4 KB of it is that warp's dQ staging box
-constexpr int kDSOff = kDOOff + 2 * kTile;
-constexpr int kVecOff = kDSOff + kB * kB * 2;  // [2] x (lse2[128], delta[128])
-constexpr int kBarOff = kVecOff + 2 * 2 * kB * 4;
-constexpr int kSmemBytes = kBarOff + 256;  // no alignment slack: checked in the kernel
-static_assert(kSmemBytes <= 232448, "shared memory");
 
+template <int D>
+struct PCfg {
+  static constexpr int kTile = kB * D * 2;  // 32 KB at D = 128
+  static constexpr int kKOff = 0;
+  static constexpr int kVOff = kKOff + kTile;
+  static constexpr int kQOff = kVOff + kTile;        // [2]
+  static constexpr int kDOOff = kQOff + 2 * kTile;   // [2]
+  // dS (rows = keys, 64-query 128-byte chunks); after the dQ MMA has read it,
+  // each element-wise warp's 4 KB of it is that warp's dQ staging box
+  static constexpr int kDSOff = kDOOff + 2 * kTile;
+  static constexpr int kVecOff = kDSOff + kB * kB * 2;  // [2] x (lse2[128], delta[128])
+  static constexpr int kBarOff = kVecOff + 2 * 2 * kB * 4;
+  static constexpr int kSmemBytes = kBarOff + 256;  // no alignment slack: checked in the kernel
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tmQ,
                                const __grid_constant__ CUtensorMap tmK,
                                const __grid_constant__ CUtensorMap tmV,
                                const __grid_constant__ CUtensorMap tmDO,
                                const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+  constexpr int kD = D;
+  constexpr int kTile = PCfg<D>::kTile;
+  constexpr int kKOff = PCfg<D>::kKOff, kVOff = PCfg<D>::kVOff, kQOff = PCfg<D>::kQOff;
+  constexpr int kDOOff = PCfg<D>::kDOOff, kDSOff = PCfg<D>::kDSOff;
+  constexpr int kVecOff = PCfg<D>::kVecOff, kBarOff = PCfg<D>::kBarOff;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {  // uniform over the CTA: nobody touches a barrier
     if (threadIdx.x == 0) atomicCAS(p.status, 0u, unsigned(kWdSmemAlign));
@@ -622,7 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale_log2;
     uint8_t* sDS = smem + kDSOff;
     uint8_t* stg = sDS + (g * 4 + q4) * 4096;  // this warp's 4 KB of dS = dQ staging box
-    const int c0 = int(g) * 64;
+    const int c0 = int(g) * 64;        // this warpgroup's 64 queries of a step
+    const int dc0 = int(g) * (kD / 2);  // its half of d (dQ read-out, dK, dV)
     // threads 0..127 fetch lse * log2(e), 128..255 Delta, one step ahead
     auto fetch_vec = [&](uint32_t s) -> float {
       const uint32_t q = (i0 + s) * kB + (tid & (kB - 1));
@@ -740,16 +426,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait(dq_full, i & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
       BWD_TR_ACC(tr_sts, t4);
       tc_fence_after();
+      constexpr int kBoxes = kD / 64;  // 32-column boxes per warpgroup
       uint32_t v0[32], v1[32];
-      tmem_ld_32x32b_x32(tmem + la + kColDP + c0, v0);
-      tmem_ld_32x32b_x32(tmem + la + kColDP + c0 + 32, v1);
+      tmem_ld_32x32b_x32(tmem + la + kColDP + dc0, v0);
+      if constexpr (kBoxes > 1) tmem_ld_32x32b_x32(tmem + la + kColDP + dc0 + 32, v1);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
       const uint32_t q0 = (i0 + i) * kB + q4 * 32;
 #pragma unroll
-      for (int bx = 0; bx < 2; ++bx) {
+      for (int bx = 0; bx < kBoxes; ++bx) {
         const uint32_t(&v)[32] = bx ? v1 : v0;
         if (bx) {
           if (lane == 0) bulk_wait_group_read<0>();
@@ -763,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           if (q0 < p.S && !FELIX_FA_BWD_EXP_NO_DQRED)
-            tma_reduce_add_3d(&tmDQ, stg, c0 + 32 * bx, int(q0), int(bh));
+            tma_reduce_add_3d(&tmDQ, stg, dc0 + 32 * bx, int(q0), int(bh));
           bulk_commit_group();
         }
       }
@@ -788,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mul = which ? p.scale : 1.f;
         __half* out = (which ? p.dK : p.dV) + (size_t(bh) * p.S + key) * kD;
 #pragma unroll 1
-        for (int c = c0; c < c0 + 64; c += 32) {
+        for (int c = dc0; c < dc0 + kD / 2; c += 32) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem + la + col + c, v);
           tmem_ld_wait();
@@ -856,32 +543,20 @@ namespace felix_impl {
 using namespace felix_sm100::attn_bwd;
 
 namespace {
+template <int D>
 int configure_bwd_pipe(int device) {
   static int done[64] = {0};
   if (device < 0 || device >= 64) return -1;
   if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(pipe::flash_attn_bwd_pipe_kernel,
+    cudaError_t e = cudaFuncSetAttribute(pipe::flash_attn_bwd_pipe_kernel<D>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         pipe::kSmemBytes);
+                                         pipe::PCfg<D>::kSmemBytes);
     if (e != cudaSuccess) return int(e);
     done[device] = 1;
   }
   return 0;
 }
 
-template <int D>
-int configure_bwd(int device) {
-  static int done[64] = {0};
-  if (device < 0 || device >= 64) return -1;
-  if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(flash_attn_bwd_kernel<D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg<D>::kSmemBytes);
-    if (e != cudaSuccess) return int(e);
-    done[device] = 1;
-  }
-  return 0;
-}
 }  // namespace
 
 size_t flash_attn_bwd_workspace_bytes(uint32_t heads, uint32_t batch, uint32_t seqlen,
@@ -925,7 +600,6 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
   }
 
   CUtensorMap tq, tk, tv, tdo, tdq;
-  const bool pipelined = head_dim == 128;
   auto enc = [&](CUtensorMap* m, const void* base, uint32_t rows) {
     return encode_tmap_3d_f16(m, base, head_dim, seqlen, bh, uint64_t(head_dim) * 2,
                               uint64_t(seqlen) * head_dim * 2, 64, rows, 1);
@@ -954,19 +628,18 @@ FelixCode flash_attn_bwd_launch(const __half* Q, const __half* K, const __half* 
   const uint64_t grid = bh * p.n_blk;
   if (grid > 0x7fffffffull) return api_error("flash_attn_bwd: grid too large");
   int rc;
-  if (pipelined) {
-    if ((rc = configure_bwd_pipe(dev->ordinal)))
+  if (head_dim == 128) {
+    if ((rc = configure_bwd_pipe<128>(dev->ordinal)))
       return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    pipe::flash_attn_bwd_pipe_kernel<<<unsigned(grid), pipe::kThreads, pipe::kSmemBytes,
-                                       stream>>>(tq, tk, tv, tdo, tdq, p);
-  } else if (head_dim == 128) {
-    if ((rc = configure_bwd<128>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    flash_attn_bwd_kernel<128><<<unsigned(grid), kThreads, Cfg<128>::kSmemBytes, stream>>>(
-        tq, tk, tv, tdo, tdq, p);
+    pipe::flash_attn_bwd_pipe_kernel<128><<<unsigned(grid), pipe::kThreads,
+                                            pipe::PCfg<128>::kSmemBytes, stream>>>(tq, tk, tv,
+                                                                                   tdo, tdq, p);
   } else {
-    if ((rc = configure_bwd<64>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    flash_attn_bwd_kernel<64><<<unsigned(grid), kThreads, Cfg<64>::kSmemBytes, stream>>>(
-        tq, tk, tv, tdo, tdq, p);
+    if ((rc = configure_bwd_pipe<64>(dev->ordinal)))
+      return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    pipe::flash_attn_bwd_pipe_kernel<64><<<unsigned(grid), pipe::kThreads,
+                                           pipe::PCfg<64>::kSmemBytes, stream>>>(tq, tk, tv, tdo,
+                                                                                 tdq, p);
   }
   dq_convert_kernel<<<592, 256, 0, stream>>>(dq_acc, dQ, rows * head_dim, p.scale);
   e = cudaGetLastError();
