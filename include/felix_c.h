@@ -118,11 +118,15 @@ int felix_hgemm_ex(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* 
 int felix_hgemm_workspace_size(uint32_t M, uint32_t N, uint32_t K, int block_n, int stream_k,
                                int max_ctas, size_t* bytes);
 /*
- * felix_hgemm_ex plus cta_pair (no reference counterpart): 0 auto (currently
- * off), 1 off, 2 = 256 x 256 tiles computed by 2-CTA clusters with
- * cta_group::2 MMAs (each CTA loads half of the tile's B, the leader issues
- * M = 256 MMAs); block_n must then be 0 or 256. Workspace size from
- * felix_hgemm_workspace_size2 with the same options.
+ * felix_hgemm_ex plus cta_pair (no reference counterpart): 0 auto (pairs when
+ * M, N >= 256, K >= 512 with K (and N for FELIX_B_KN) a multiple of 64, and at
+ * least one wave of 256 x 256 tiles, with block_n, stream_k, max_ctas all 0),
+ * 1 off, 2 = 256 x 256 tiles computed by 2-CTA clusters with cta_group::2 MMAs
+ * (each CTA loads its 128 rows of A and half of the tile's B, the leader
+ * issues M = 256 MMAs; block_n must be 0 or 256; K, and N for FELIX_B_KN,
+ * multiples of 64). felix_hgemm and felix_hgemm_ex use the same automatic
+ * choice. Workspace size from felix_hgemm_workspace_size2 with the same
+ * options.
  */
 int felix_hgemm_ex2(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* A,
                     const void* B, float beta, void* C, int b_layout, int block_n, int stream_k,

@@ -75,7 +75,7 @@ struct HgemmOptions {
   int block_n = 0;   // 0 = auto, 64, 128 or 256
   int stream_k = 0;  // 0 = auto, 1 = off, 2 = on whenever the last wave is partial
   int max_ctas = 0;  // 0 = one per SM; otherwise cap the persistent grid
-  int cta_pair = 0;  // 0 = auto (off), 1 = off, 2 = 256 x 256 tiles on CTA pairs (cta_group::2)
+  int cta_pair = 0;  // 0 = auto (pairs for large shapes), 1 = off, 2 = CTA pairs (cta_group::2)
 };
 
 size_t hgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o,

@@ -50,12 +50,16 @@ constexpr int kThreads = 192;
 // CG = 2: CTA pairs (cta_group::2): a 2-CTA cluster computes a 256 x BN tile;
 // each CTA holds 128 rows of A and BN / 2 rows (N) of B, the leader issues the
 // MMAs (M = 256) and each CTA's TMEM gets its own 128 rows of the tile.
+// A pair's stages hold two 64-deep k-blocks, loaded by one 32 KB TMA request
+// per operand (3-D tensor-map view): requests of 16 KB stream at only ~57
+// B/clk per SM from L2 against ~90 for 32 KB ones, and the pair needs ~63.
 template <int BN, int CG = 1>
 struct Cfg {
   static constexpr int kBRows = BN / CG;  // B rows (N) loaded by one CTA
-  static constexpr int kStages = (192 * 1024) / ((BM + kBRows) * BK * 2);
-  static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = kBRows * BK * 2;
+  static constexpr int kSub = CG == 2 ? 2 : 1;  // 64-deep k-blocks per stage
+  static constexpr int kStages = (192 * 1024) / ((BM + kBRows) * BK * 2 * kSub);
+  static constexpr int kABytes = BM * BK * 2 * kSub;
+  static constexpr int kBBytes = kBRows * BK * 2 * kSub;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   // epilogue staging for TMA stores: 4 warps x 2 buffers x (32 rows x 128 B)
@@ -223,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmC, const Params p) {
   using C_ = Cfg<BN, CG>;
-  static_assert(CG == 1 || BN == 256, "CTA pairs use 256-wide tiles");
+  static_assert(CG == 1 || (BN == 256 && BK == 64), "CTA pairs use 256-wide tiles, BK = 64");
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
   constexpr int S = C_::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -295,10 +299,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       // loads of a pair's CTAs complete on the leader's barrier
       auto load2d = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-        if constexpr (CG == 2)
-          tma_load_2d_pair(dst, map, mapa_shared(smem_u32(bar), 0), x, y);
-        else
-          tma_load_2d(dst, map, bar, x, y);
+        tma_load_2d(dst, map, bar, x, y);
+      };
+      // pairs: 3-D views (64-element inner, rows, 64-wide k-blocks or n-chunks)
+      auto load3d = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int y, int z) {
+        tma_load_3d_pair(dst, map, mapa_shared(smem_u32(bar), 0), 0, y, z);
       };
       while (ok && sc.next(u)) {
         uint32_t tm, tn;
@@ -312,13 +317,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = ring + stage * C_::kStageBytes;
           uint8_t* sb = sa + C_::kABytes;
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], CG * C_::kStageBytes);
-          load2d(sa, &tmA, &full[stage], int(kb * BK), m0);
-          if (p.b_mn_major) {
-#pragma unroll
-            for (int j = 0; j < C_::kBRows / 64; ++j)
-              load2d(sb + j * (64 * BK * 2), &tmB, &full[stage], n0 + 64 * j, int(kb * BK));
+          if constexpr (CG == 2) {
+            // A rows [m0, m0 + 128), k-blocks 2 kb, 2 kb + 1; B likewise, or
+            // ("nn") k rows [128 kb, 128 kb + 128) of n-chunks n0 / 64, + 1
+            load3d(sa, &tmA, &full[stage], m0, int(2 * kb));
+            if (p.b_mn_major)
+              load3d(sb, &tmB, &full[stage], int(kb * BK * 2), n0 / 64);
+            else
+              load3d(sb, &tmB, &full[stage], n0, int(2 * kb));
           } else {
-            load2d(sb, &tmB, &full[stage], int(kb * BK), n0);
+            load2d(sa, &tmA, &full[stage], int(kb * BK), m0);
+            if (p.b_mn_major) {
+#pragma unroll
+              for (int j = 0; j < C_::kBRows / 64; ++j)
+                load2d(sb + j * (64 * BK * 2), &tmB, &full[stage], n0 + 64 * j, int(kb * BK));
+            } else {
+              load2d(sb, &tmB, &full[stage], int(kb * BK), n0);
+            }
           }
           ++filled;
           if (++stage == NS) {
@@ -377,12 +392,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a0 = smem_u32(ring + stage * C_::kStageBytes);
           const uint32_t b0 = a0 + C_::kABytes;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
+          for (int k = 0; k < BK * C_::kSub / 16; ++k) {
             uint64_t ad, bd;
             if constexpr (BK == 64) {
-              ad = make_sdesc_sw128(a0 + k * 32, 16, 1024);
-              bd = p.b_mn_major ? make_sdesc_sw128(b0 + k * 2048, 64 * BK * 2, 1024)
-                                : make_sdesc_sw128(b0 + k * 32, 16, 1024);
+              // K-major: 64-deep k-blocks of rows x 128 B, 32 B per 16 k;
+              // MN-major: 64-wide chunks of (BK * kSub) k-rows x 128 B
+              constexpr int kq = BK / 16;
+              ad = make_sdesc_sw128(a0 + (k / kq) * (BM * BK * 2) + (k % kq) * 32, 16, 1024);
+              bd = p.b_mn_major
+                       ? make_sdesc_sw128(b0 + k * 2048, BK * C_::kSub * 128, 1024)
+                       : make_sdesc_sw128(b0 + (k / kq) * (C_::kBRows * BK * 2) + (k % kq) * 32,
+                                          16, 1024);
             } else {
               ad = make_sdesc_sw64(a0 + k * 32, 16, 512);
               bd = p.b_mn_major ? make_sdesc_sw128(b0 + k * 2048, 64 * BK * 2, 1024)
@@ -712,13 +732,26 @@ Plan plan_for(uint32_t M, uint32_t N, uint32_t K, int bn, const HgemmOptions& o,
   return pl;
 }
 
-Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int num_sms) {
-  if (o.cta_pair == 2) {
+// Automatic choice of CTA pairs: large enough for at least one wave of
+// 256 x 256 tiles, and whole 64-wide k-blocks (and n-chunks for "nn") so that
+// the 32 KB 3-D loads are exact. pair_shape_ok carries the layout condition.
+bool auto_pair(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int num_sms,
+               bool pair_shape_ok) {
+  if (o.cta_pair != 0 || o.block_n != 0 || o.stream_k != 0 || o.max_ctas != 0) return false;
+  if (!pair_shape_ok || M < 256 || N < 256 || K < 512 || K % 64 != 0) return false;
+  const uint64_t pair_tiles = uint64_t((M + 255) / 256) * ((N + 255) / 256);
+  return pair_tiles >= uint64_t(num_sms / 2);
+}
+
+Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int num_sms,
+               bool pair_shape_ok = true) {
+  if (o.cta_pair == 2 || auto_pair(M, N, K, o, num_sms, pair_shape_ok)) {
     // 256 x 256 tiles, one unit per CTA pair: plan as 128-row tiles of
     // ceil(M / 2) rows over num_sms / 2 "CTAs"
     HgemmOptions op = o;
     if (op.max_ctas > 0) op.max_ctas = op.max_ctas / 2 > 0 ? op.max_ctas / 2 : 1;
-    Plan pl = plan_for((M + 1) / 2, N, K, 256, op, num_sms / 2);
+    // (k-blocks of 128 = two 64-deep ones per stage: plan with K / 2)
+    Plan pl = plan_for((M + 1) / 2, N, (K + 1) / 2, 256, op, num_sms / 2);
     pl.pair = true;
     return pl;
   }
@@ -738,9 +771,16 @@ Plan make_plan(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o, int nu
 
 size_t hgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const HgemmOptions& o,
                              int num_sms) {
-  Plan pl = make_plan(M, N, K, o, num_sms);
-  if (pl.sk_tiles == 0) return 0;
-  return kWsCounterBytes + size_t(pl.grid) * 2 * (pl.pair ? 2 : 1) * BM * pl.bn * sizeof(float);
+  // the larger of the pair and single-CTA plans (the layout is not known here)
+  size_t need = 0;
+  for (int pair_ok = 0; pair_ok < 2; ++pair_ok) {
+    Plan pl = make_plan(M, N, K, o, num_sms, pair_ok != 0);
+    if (pl.sk_tiles == 0) continue;
+    const size_t n =
+        kWsCounterBytes + size_t(pl.grid) * 2 * (pl.pair ? 2 : 1) * BM * pl.bn * sizeof(float);
+    need = n > need ? n : need;
+  }
+  return need;
 }
 
 FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __half* A,
@@ -765,18 +805,30 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
 
   DeviceInfo* dev = current_device_info();
   if (!dev) return launch_error(cudaGetLastError(), "hgemm: no CUDA device");
-  Plan pl = make_plan(M, N, K, o, dev->num_sms);
+  const bool pair_shape_ok = (K % 64 == 0) && (!b_kn || N % 64 == 0);
+  Plan pl = make_plan(M, N, K, o, dev->num_sms, pair_shape_ok);
 
   CUtensorMap tmA, tmB;
-  int rc = encode_tmap_2d_f16_swizzle(&tmA, A, K, M, uint64_t(K) * 2, BK, BM, kSwizzleK);
-  if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(A) failed");
-  if (b_kn)
-    rc = encode_tmap_2d_f16(&tmB, B, N, K, uint64_t(N) * 2, 64, BK);
-  else
-    // (a CTA of a pair loads half of the tile's B rows)
-    rc = encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK,
-                                    pl.pair ? pl.bn / 2 : pl.bn, kSwizzleK);
-  if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
+  int rc;
+  if (pl.pair) {
+    // 3-D views [k-block or n-chunk][rows][64]: one 32 KB request = 128 rows x
+    // two 64-wide blocks. The view is exact only for whole 64-wide blocks.
+    if (K % 64 != 0 || (b_kn && N % 64 != 0))
+      return api_error("hgemm: CTA pairs need K (and N when B is K x N) multiples of 64");
+    rc = encode_tmap_3d_f16(&tmA, A, 64, M, K / 64, uint64_t(K) * 2, 128, 64, BM, 2);
+    if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(A) failed");
+    rc = b_kn ? encode_tmap_3d_f16(&tmB, B, 64, K, N / 64, uint64_t(N) * 2, 128, 64, 128, 2)
+              : encode_tmap_3d_f16(&tmB, B, 64, N, K / 64, uint64_t(K) * 2, 128, 64, 128, 2);
+    if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
+  } else {
+    rc = encode_tmap_2d_f16_swizzle(&tmA, A, K, M, uint64_t(K) * 2, BK, BM, kSwizzleK);
+    if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(A) failed");
+    if (b_kn)
+      rc = encode_tmap_2d_f16(&tmB, B, N, K, uint64_t(N) * 2, 64, BK);
+    else
+      rc = encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK, pl.bn, kSwizzleK);
+    if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
+  }
 
   // C through TMA when nothing has to be read back (beta == 0) and its rows
   // are 16-byte multiples.

@@ -137,12 +137,21 @@ def test_hgemm_rejects_unaligned_k(felix):
 
 
 @pytest.mark.parametrize("nt", [True, False])
-@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 1024), (300, 520, 200),
-                                   (1024, 1024, 2048)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 1024), (300, 576, 192),
+                                   (1024, 1024, 2048), (130, 320, 320)])
 def test_hgemm_cta_pair(felix, nt, M, N, K):
-    # 256 x 256 tiles on 2-CTA clusters (cta_group::2 MMAs issued by the leader)
+    # 256 x 256 tiles on 2-CTA clusters (cta_group::2 MMAs issued by the leader),
+    # stages of two 64-deep k-blocks (odd counts end in a zero-filled block)
     ref, out = _run(felix, M, N, K, nt=nt, cta_pair=2)
     assert_fp16_close(ref, out, ctx="CTA pair")
+
+
+def test_hgemm_cta_pair_rejects_ragged_k(felix):
+    A = torch.zeros(256, 200, dtype=torch.half, device="cuda")
+    B = torch.zeros(256, 200, dtype=torch.half, device="cuda")
+    C = torch.empty(256, 256, dtype=torch.half, device="cuda")
+    with pytest.raises(felix.FelixError):
+        felix.hgemm(A, B, C, b_layout=felix.B_NK, cta_pair=2)
 
 
 @pytest.mark.parametrize("nt", [True, False])
