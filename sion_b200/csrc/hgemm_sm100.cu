@@ -53,10 +53,11 @@ constexpr int kThreads = 192;
 // A pair's stages hold two 64-deep k-blocks, loaded by one 32 KB TMA request
 // per operand (3-D tensor-map view): requests of 16 KB stream at only ~57
 // B/clk per SM from L2 against ~90 for 32 KB ones, and the pair needs ~63.
-template <int BN, int CG = 1>
+template <int BN, int CG = 1, int SUB = (CG == 2 ? 2 : 1)>
 struct Cfg {
+  static_assert(CG == 1 || SUB == 2, "CTA pairs load two k-blocks per stage");
   static constexpr int kBRows = BN / CG;  // B rows (N) loaded by one CTA
-  static constexpr int kSub = CG == 2 ? 2 : 1;  // 64-deep k-blocks per stage
+  static constexpr int kSub = SUB;        // 64-deep k-blocks per stage
   static constexpr int kStages = (192 * 1024) / ((BM + kBRows) * BK * 2 * kSub);
   static constexpr int kABytes = BM * BK * 2 * kSub;
   static constexpr int kBBytes = kBRows * BK * 2 * kSub;
@@ -221,13 +222,14 @@ __device__ __forceinline__ void store_row_chunk(const Params& p, uint32_t row, u
   }
 }
 
-template <int BN, int CG = 1>
+template <int BN, int CG = 1, int SUB = (CG == 2 ? 2 : 1)>
 __global__ void __launch_bounds__(kThreads, 1)
     hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmC, const Params p) {
-  using C_ = Cfg<BN, CG>;
-  static_assert(CG == 1 || (BN == 256 && BK == 64), "CTA pairs use 256-wide tiles, BK = 64");
+  using C_ = Cfg<BN, CG, SUB>;
+  static_assert(CG == 1 || BN == 256, "CTA pairs use 256-wide tiles");
+  static_assert(SUB == 1 || (BK == 64 && C_::kBRows == 128), "3-D loads: 128-row boxes, BK = 64");
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
   constexpr int S = C_::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -301,9 +303,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto load2d = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
         tma_load_2d(dst, map, bar, x, y);
       };
-      // pairs: 3-D views (64-element inner, rows, 64-wide k-blocks or n-chunks)
+      // two-k-block stages: 3-D views (64-element inner, rows, 64-wide k-blocks
+      // or n-chunks); a pair's loads complete on the leader's barrier
       auto load3d = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int y, int z) {
-        tma_load_3d_pair(dst, map, mapa_shared(smem_u32(bar), 0), 0, y, z);
+        if constexpr (CG == 2)
+          tma_load_3d_pair(dst, map, mapa_shared(smem_u32(bar), 0), 0, y, z);
+        else
+          tma_load_3d(dst, map, bar, 0, y, z);
       };
       while (ok && sc.next(u)) {
         uint32_t tm, tn;
@@ -317,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = ring + stage * C_::kStageBytes;
           uint8_t* sb = sa + C_::kABytes;
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], CG * C_::kStageBytes);
-          if constexpr (CG == 2) {
+          if constexpr (SUB == 2) {
             // A rows [m0, m0 + 128), k-blocks 2 kb, 2 kb + 1; B likewise, or
             // ("nn") k rows [128 kb, 128 kb + 128) of n-chunks n0 / 64, + 1
             load3d(sa, &tmA, &full[stage], m0, int(2 * kb));
@@ -664,14 +670,14 @@ using namespace felix_sm100::hgemm;
 
 namespace {
 
-template <int BN, int CG = 1>
+template <int BN, int CG = 1, int SUB = (CG == 2 ? 2 : 1)>
 int configure_once(int device) {
   static int done[64] = {0};
   if (device < 0 || device >= 64) return -1;
   if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(felix_sm100::hgemm::hgemm_persistent_kernel<BN, CG>,
+    cudaError_t e = cudaFuncSetAttribute(felix_sm100::hgemm::hgemm_persistent_kernel<BN, CG, SUB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg<BN, CG>::kSmemBytes);
+                                         Cfg<BN, CG, SUB>::kSmemBytes);
     if (e != cudaSuccess) return int(e);
     done[device] = 1;
   }
@@ -681,6 +687,7 @@ int configure_once(int device) {
 struct Plan {
   int bn;
   bool pair;     // CTA pairs: tiles, grid and units counted per pair (grid launched x 2)
+  int sub;       // 64-deep k-blocks per stage (2: 32 KB 3-D loads; kblocks count 128-deep)
   bool ksplit2;  // 2-CTA clusters, each tile's K split in halves (grid = 2 x tiles)
   uint32_t tiles_m, tiles_n, kblocks, tiles;
   uint32_t grid;
@@ -691,6 +698,7 @@ struct Plan {
 Plan plan_for(uint32_t M, uint32_t N, uint32_t K, int bn, const HgemmOptions& o, int num_sms) {
   Plan pl{};
   pl.bn = bn;
+  pl.sub = 1;
   pl.tiles_m = (M + BM - 1) / BM;
   pl.tiles_n = (N + pl.bn - 1) / pl.bn;
   pl.kblocks = (K + BK - 1) / BK;
@@ -805,16 +813,50 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
 
   DeviceInfo* dev = current_device_info();
   if (!dev) return launch_error(cudaGetLastError(), "hgemm: no CUDA device");
-  const bool pair_shape_ok = (K % 64 == 0) && (!b_kn || N % 64 == 0);
-  Plan pl = make_plan(M, N, K, o, dev->num_sms, pair_shape_ok);
+  // 3-D views (two 64-wide k-blocks per 32 KB request) are exact only for
+  // whole 64-wide blocks: K, and N when B is K x N
+  const bool sub2_ok = (K % 64 == 0) && (!b_kn || N % 64 == 0);
+  Plan pl = make_plan(M, N, K, o, dev->num_sms, sub2_ok);
+  if (pl.pair && !sub2_ok)
+    return api_error("hgemm: CTA pairs need K (and N when B is K x N) multiples of 64");
+  // C through TMA when nothing has to be read back (beta == 0) and its rows
+  // are 16-byte multiples.
+  const bool tma_store = beta == 0.f && (N % 8 == 0) &&
+                         (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
+  // Few tiles, long K, C through TMA: split each 128 x 128 tile's K over a
+  // 2-CTA cluster that reduces through DSMEM, instead of stream-K partials in
+  // global memory whose fix-up forms a tail (skinny 128 x 8192 x 16384).
+  bool ksplit2 = false;
+  {
+    const uint32_t t128 = ((M + BM - 1) / BM) * ((N + 127) / 128);
+    const uint32_t kb = (K + BK - 1) / BK;
+    const uint32_t sms = uint32_t(dev->num_sms);
+    if (!pl.pair && o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 && tma_store &&
+        kb >= 64 && 2 * t128 <= sms && 8 * t128 >= 3 * sms) {
+      pl = plan_for(M, N, K, 128, o, dev->num_sms);
+      ksplit2 = true;
+    }
+  }
+  // 128-wide single-CTA tiles also take stages of two 64-deep k-blocks (32 KB
+  // requests) when the view is exact: plan in 128-deep k-blocks
+  if (!pl.pair && pl.bn == 128 && sub2_ok && K >= 128) {
+    pl = plan_for(M, N, (K + 1) / 2, 128, o, dev->num_sms);
+    pl.sub = 2;
+  }
+  if (pl.pair) pl.sub = 2;
+  if (ksplit2) {
+    pl.ksplit2 = true;
+    pl.sk_tiles = 0;
+    pl.dp_tiles = pl.tiles;
+    pl.sk_iters = 0;
+    pl.grid = 2 * pl.tiles;
+  }
 
   CUtensorMap tmA, tmB;
   int rc;
-  if (pl.pair) {
+  if (pl.sub == 2) {
     // 3-D views [k-block or n-chunk][rows][64]: one 32 KB request = 128 rows x
-    // two 64-wide blocks. The view is exact only for whole 64-wide blocks.
-    if (K % 64 != 0 || (b_kn && N % 64 != 0))
-      return api_error("hgemm: CTA pairs need K (and N when B is K x N) multiples of 64");
+    // two 64-wide blocks (a pair's CTA loads half of the tile's B rows).
     rc = encode_tmap_3d_f16(&tmA, A, 64, M, K / 64, uint64_t(K) * 2, 128, 64, BM, 2);
     if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(A) failed");
     rc = b_kn ? encode_tmap_3d_f16(&tmB, B, 64, K, N / 64, uint64_t(N) * 2, 128, 64, 128, 2)
@@ -829,12 +871,7 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
       rc = encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK, pl.bn, kSwizzleK);
     if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
   }
-
-  // C through TMA when nothing has to be read back (beta == 0) and its rows
-  // are 16-byte multiples.
   CUtensorMap tmC;
-  const bool tma_store = beta == 0.f && (N % 8 == 0) &&
-                         (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
   if (tma_store && encode_tmap_2d_f16(&tmC, C, N, M, uint64_t(N) * 2, 64, 32))
     return api_error("hgemm: cuTensorMapEncodeTiled(C) failed");
   if (!tma_store) tmC = tmA;  // unused placeholder
@@ -856,35 +893,7 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   p.sk_iters = pl.sk_iters;
   p.group_m = 16;
   p.status = dev->status_word;
-  // Few tiles, long K, C through TMA: split each 128 x 128 tile's K over a
-  // 2-CTA cluster that reduces through DSMEM, instead of stream-K partials in
-  // global memory whose fix-up forms a tail (skinny 128 x 8192 x 16384).
-  {
-    const uint32_t t128 = ((M + BM - 1) / BM) * ((N + 127) / 128);
-    const uint32_t kb = (K + BK - 1) / BK;
-    const uint32_t sms = uint32_t(dev->num_sms);
-    if (!pl.pair && o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 && tma_store &&
-        kb >= 64 &&
-        2 * t128 <= sms && 8 * t128 >= 3 * sms) {
-      if (pl.bn != 128) {
-        pl = plan_for(M, N, K, 128, o, dev->num_sms);
-        // the "nt" B box is BN rows tall; the "nn" box does not depend on BN
-        if (!b_kn &&
-            encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK, 128, kSwizzleK))
-          return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
-        p.tiles_n = pl.tiles_n;
-      }
-      pl.ksplit2 = true;
-      pl.sk_tiles = 0;
-      pl.dp_tiles = pl.tiles;
-      pl.sk_iters = 0;
-      pl.grid = 2 * pl.tiles;
-      p.dp_tiles = pl.dp_tiles;
-      p.sk_tiles = 0;
-      p.sk_iters = 0;
-      p.ksplit2 = 1;
-    }
-  }
+  p.ksplit2 = pl.ksplit2 ? 1u : 0u;
   p.pair = pl.pair ? 1u : 0u;
   if (pl.sk_tiles) {
     if (uint64_t(pl.sk_tiles) * (pl.pair ? 2 : 1) > kWsMaxCounters)
@@ -929,14 +938,18 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
       hgemm_persistent_kernel<256>
           <<<pl.grid, kThreads, Cfg<256>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
       break;
-    case 128:
-      if ((rc = configure_once<128>(dev->ordinal)))
-        return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-      if (pl.ksplit2) {
+    case 128: {
+      // launch the 128-wide kernel with one or two k-blocks per stage, as a
+      // 2-CTA cluster for the cluster split-K plan
+      auto launch128 = [&](auto kernel, int smem) -> cudaError_t {
+        if (!pl.ksplit2) {
+          kernel<<<pl.grid, kThreads, smem, stream>>>(tmA, tmB, tmC, p);
+          return cudaGetLastError();
+        }
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(pl.grid);
         cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = Cfg<128>::kSmemBytes;
+        cfg.dynamicSmemBytes = smem;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -945,13 +958,20 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<128>, tmA, tmB, tmC, p);
-        if (e != cudaSuccess) return launch_error(e, "hgemm: cluster launch failed");
+        return cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmC, p);
+      };
+      if (pl.sub == 2) {
+        if ((rc = configure_once<128, 1, 2>(dev->ordinal)))
+          return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+        e = launch128(hgemm_persistent_kernel<128, 1, 2>, Cfg<128, 1, 2>::kSmemBytes);
       } else {
-        hgemm_persistent_kernel<128>
-            <<<pl.grid, kThreads, Cfg<128>::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
+        if ((rc = configure_once<128>(dev->ordinal)))
+          return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+        e = launch128(hgemm_persistent_kernel<128>, Cfg<128>::kSmemBytes);
       }
+      if (e != cudaSuccess) return launch_error(e, "hgemm: launch failed");
       break;
+    }
     default:
       if ((rc = configure_once<64>(dev->ordinal)))
         return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
