@@ -48,8 +48,13 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // D columns), so per-SM shared-memory operand traffic drops by ~40%.
 template <int D, int CG>
 struct Cfg {
+#ifdef FELIX_FA_KST
+  static constexpr int kKStages = FELIX_FA_KST;
+  static constexpr int kVStages = FELIX_FA_VST;
+#else
   static constexpr int kKStages = CG == 2 ? 4 : (D == 128 ? 3 : 4);  // K ring
   static constexpr int kVStages = CG == 2 ? 4 : (D == 128 ? 2 : 4);  // V ring
+#endif
   static constexpr int kChunks = D / 64;                 // 128-byte swizzle chunks per row
   static constexpr int kTileBytes = kBlockQ * D * 2;     // one 128 x D fp16 Q tile
   static constexpr int kKeys = kBlockKV / CG;            // K rows held per CTA
@@ -82,7 +87,7 @@ struct Params {
 #ifdef FELIX_FA_TRACE
 // Development-only phase trace of CTA 0 (compiled out of the library build):
 // [role][block j][event] = clock64 value.
-__device__ unsigned long long g_fa_trace[3][64][8];
+__device__ unsigned long long g_fa_trace[4][64][8];
 #define FA_TRACE(role, j, ev)                                           \
   do {                                                                  \
     if (blockIdx.x == 0 && (j) < 64) g_fa_trace[role][j][ev] = clock64(); \
@@ -196,10 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_empty + KST;          // [VST] (leader's counts both CTAs)
   uint64_t* v_empty = v_full + VST;          // [VST]
   uint64_t* s_full = v_empty + VST;          // [2]
-  uint64_t* p_full = s_full + 2;             // [2]   (leader's counts both CTAs)
-  uint64_t* pv_done = s_full + 4;            // [2]
-  uint64_t* drain = s_full + 6;              // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 7);
+  uint64_t* p_full = s_full + 2;             // [2 tiles][2 halves] (leader's counts both CTAs)
+  uint64_t* pv_done = s_full + 6;            // [2]
+  uint64_t* drain = s_full + 8;              // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = threadIdx.x / 32;
@@ -228,7 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4 * CG);
+      mbar_init(&p_full[2 * i], 4 * CG);
+      mbar_init(&p_full[2 * i + 1], 4 * CG);
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -289,6 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t st = j % NS;
         const uint32_t ph = (j / NS) & 1u;
         if (!mbar_wait(&empty[st], ph ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
+        FA_TRACE(3, j, is_k ? 3 : 2);
         uint8_t* dst = ring + st * slot_bytes;
         if (rank == 0) mbar_arrive_expect_tx(&full[st], CG * slot_bytes);
         if (is_k) {
@@ -321,7 +328,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0 && rank == 0) {
+    // The whole warp runs the loop (waits, descriptor arithmetic) converged;
+    // one elected lane issues the MMAs and commits.
+    if (rank == 0) {
       const uint32_t idesc_qk = make_idesc_f16_f32(kBlockQ * CG, kBlockKV, false, false);
       const uint32_t idesc_pv = make_idesc_f16_f32(kBlockQ * CG, D, false, true);
       const uint32_t sq = smem_u32(smem + C_::kQOff);
@@ -334,39 +343,56 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(bar);
         }
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kWdAttnMma);
+      // every lane waits and the lanes agree, so the warp stays converged
+      // even when a wait gives up
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu,
+                          mbar_wait(bar, parity, abort_flag, p.status, kWdAttnMma)) != 0;
+      };
+      bool ok = wait_all(q_full, 0);
       auto issue_s = [&](uint32_t j, int t) {
         const uint32_t sk = smem_u32(smem + C_::kKOff + (j % KST) * C_::kKBytes);
         const uint32_t qa = sq + t * C_::kTileBytes;
+        FA_TRACE(3, j, 6 + t);
+        if (elect_one()) {
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint64_t ad = kmajor_desc<kBlockQ>(qa, k);
-          const uint64_t bd = kmajor_desc<C_::kKeys>(sk, k);
-          if constexpr (CG == 2)
-            umma_f16_ss_pair(tmem + col_s(t), ad, bd, idesc_qk, k > 0 ? 1u : 0u);
-          else
-            umma_f16_ss(tmem + col_s(t), ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; ++k) {
+            const uint64_t ad = kmajor_desc<kBlockQ>(qa, k);
+            const uint64_t bd = kmajor_desc<C_::kKeys>(sk, k);
+            if constexpr (CG == 2)
+              umma_f16_ss_pair(tmem + col_s(t), ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+            else
+              umma_f16_ss(tmem + col_s(t), ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+          }
+          commit_all(&s_full[t]);
+          if (t == 1) commit_all(&k_empty[j % KST]);  // K_j consumed by both tiles
         }
-        commit_all(&s_full[t]);
-        if (t == 1) commit_all(&k_empty[j % KST]);  // K_j consumed by both tiles
+        __syncwarp();
+        FA_TRACE(3, j, 4 + t);
       };
-      auto issue_pv = [&](uint32_t j, int t) {
+      // PV_t(j) over keys [64 h, 64 h + 64): P's half h
+      auto issue_pv = [&](uint32_t j, int t, int h) {
         const uint32_t sv = smem_u32(smem + C_::kVOff + (j % VST) * C_::kVBytes);
+        if (elect_one()) {
 #pragma unroll
-        for (int k = 0; k < kBlockKV / 16; ++k) {
-          const uint32_t a = tmem + col_s(t) + k * 8;
-          if constexpr (CG == 2)
-            umma_f16_ts_pair(tmem + col_o(t), a, vmajor_desc(sv, k), idesc_pv,
-                             (j > 0 || k > 0) ? 1u : 0u);
-          else
-            umma_f16_ts(tmem + col_o(t), a, vmajor_desc(sv, k), idesc_pv,
-                        (j > 0 || k > 0) ? 1u : 0u);
+          for (int k = h * (kBlockKV / 32); k < (h + 1) * (kBlockKV / 32); ++k) {
+            const uint32_t a = tmem + col_s(t) + k * 8;
+            if constexpr (CG == 2)
+              umma_f16_ts_pair(tmem + col_o(t), a, vmajor_desc(sv, k), idesc_pv,
+                               (j > 0 || k > 0) ? 1u : 0u);
+            else
+              umma_f16_ts(tmem + col_o(t), a, vmajor_desc(sv, k), idesc_pv,
+                          (j > 0 || k > 0) ? 1u : 0u);
+          }
+          if (h == 1) {
+            commit_all(&pv_done[t]);
+            if (t == 1) commit_all(&v_empty[j % VST]);  // V_j consumed by both tiles
+          }
         }
-        commit_all(&pv_done[t]);
-        if (t == 1) commit_all(&v_empty[j % VST]);  // V_j consumed by both tiles
+        __syncwarp();
       };
       if (ok && n > 0) {
-        ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, kWdAttnMma);
+        ok = wait_all(&k_full[0], 0);
         if (ok) {
           tc_fence_after();
           issue_s(0, 0);
@@ -379,22 +405,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The two tiles run half a period apart, so the softmax of one tile
       // overlaps the other tile's MMAs.
       for (uint32_t j = 0; ok && j < n; ++j) {
-        if (!(ok = mbar_wait(&v_full[j % VST], (j / VST) & 1u, abort_flag, p.status,
-                             kWdAttnMma)))
+        FA_TRACE(3, j, 0);
+        if (!(ok = wait_all(&v_full[j % VST], (j / VST) & 1u)))
           break;
+        FA_TRACE(3, j, 1);
         for (int t = 0; t < 2; ++t) {
           FA_TRACE(2, j, 4 * t + 0);
-          if (!(ok = mbar_wait(&p_full[t], j & 1u, abort_flag, p.status, kWdAttnMma))) break;
+          // P_t(j) arrives in two halves of 64 keys: PV over the first half
+          // overlaps the softmax of the second
+          if (!(ok = wait_all(&p_full[2 * t], j & 1u))) break;
           tc_fence_after();
           FA_TRACE(2, j, 4 * t + 1);
-          issue_pv(j, t);
+          issue_pv(j, t, 0);
+          if (!(ok = wait_all(&p_full[2 * t + 1], j & 1u)))
+            break;
+          tc_fence_after();
+          issue_pv(j, t, 1);
           if (j + 1 < n) {
             FA_TRACE(2, j, 4 * t + 2);
-            if (t == 0 && !(ok = mbar_wait(&k_full[(j + 1) % KST], ((j + 1) / KST) & 1u,
-                                           abort_flag, p.status, kWdAttnMma)))
+            if (t == 0 && !(ok = wait_all(&k_full[(j + 1) % KST], ((j + 1) / KST) & 1u)))
               break;
             if (kWaitPV &&
-                !(ok = mbar_wait(&pv_done[t], j & 1u, abort_flag, p.status, kWdAttnMma)))
+                !(ok = wait_all(&pv_done[t], j & 1u)))
               break;
             tc_fence_after();
             FA_TRACE(2, j, 4 * t + 3);
@@ -402,10 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if constexpr (CG == 2)
-        umma_commit_pair(smem_u32(drain));
-      else
-        umma_commit(drain);
+      if (elect_one()) {
+        if constexpr (CG == 2)
+          umma_commit_pair(smem_u32(drain));
+        else
+          umma_commit(drain);
+      }
+      __syncwarp();
       int dummy = 0;
       mbar_wait(drain, 0, &dummy, p.status, kWdDrain, 100000000ull);
     }
@@ -417,7 +452,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = (q * 32u) << 16;
     const uint32_t tS = tmem + lane_addr + col_s(t);
     const uint32_t tO = tmem + lane_addr + col_o(t);
-    const uint32_t p_full_addr = leader_bar(&p_full[t]);
     const float sl2 = p.scale_log2;
     float m = -INFINITY;  // running max in log2 units (the one P is relative to)
     float l = 0.f;
@@ -450,6 +484,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kBlockKV; ++i)
           if (uint32_t(i) >= valid) s[i] = -INFINITY;
       }
+      // P = 2^(s * scale_log2 - m) for keys [64 h, 64 h + 64), two columns at
+      // a time in packed fp32x2 (one pair in kEmuEvery on the FMA pipe, the
+      // rest on MUFU), stored as fp16 pairs over the first half of S's columns
+      const uint64_t scale2 = pack_f32x2(sl2, sl2);
+      uint64_t l2[2] = {0ull, 0ull};  // packed partial row sums
+      auto exp_half = [&](int h) {
+        const uint64_t negm2 = pack_f32x2(-m, -m);
+#pragma unroll
+        for (int c = h * (kBlockKV / 2); c < (h + 1) * (kBlockKV / 2); c += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int e = c + 2 * i;
+            const uint64_t x2 = ffma2(pack_f32x2(s[e], s[e + 1]), scale2, negm2);
+            uint64_t p2;
+            if (kEmuEvery > 0 && (i % (kEmuEvery > 0 ? kEmuEvery : 1)) == kEmuEvery - 1) {
+              p2 = exp2_fma_x2(x2);
+            } else {
+              p2 = pack_f32x2(ex2(lo_f32(x2)), ex2(hi_f32(x2)));
+            }
+            l2[i & 1] = fadd2(l2[i & 1], p2);
+            pk[i] = pack_half2(lo_f32(p2), hi_f32(p2));
+          }
+          tmem_st_32x32b_x16(tS + c / 2, pk);
+        }
+      };
+      auto publish = [&](int h) {
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 2)
+            mbar_arrive_cluster(leader_bar(&p_full[2 * t + h]));
+          else
+            mbar_arrive(&p_full[2 * t + h]);
+        }
+      };
+      // The first half is computed against the current running max while the
+      // row max of this block is formed (the two are independent, so they
+      // interleave); it is recomputed only when the max grows past the
+      // threshold (always for the first block, where m is -inf and these
+      // values are discarded).
+      exp_half(0);
       // row max: 3-input max, 4 independent chains
       float m4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
@@ -482,44 +559,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x16(tO + c, r);
           }
         }
+        l2[0] = l2[1] = 0ull;
+        exp_half(0);
       }
-      // P = 2^(s * scale_log2 - m), two columns at a time in packed fp32x2;
-      // one pair in kEmuEvery on the FMA pipe, the rest on MUFU.
-      const uint64_t scale2 = pack_f32x2(sl2, sl2);
-      const uint64_t negm2 = pack_f32x2(-m, -m);
-      uint64_t l2[2] = {0ull, 0ull};  // packed partial row sums
-#pragma unroll
-      for (int c = 0; c < kBlockKV; c += 32) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int e = c + 2 * i;
-          const uint64_t x2 = ffma2(pack_f32x2(s[e], s[e + 1]), scale2, negm2);
-          uint64_t p2;
-          if (kEmuEvery > 0 && (i % (kEmuEvery > 0 ? kEmuEvery : 1)) == kEmuEvery - 1) {
-            p2 = exp2_fma_x2(x2);
-          } else {
-            p2 = pack_f32x2(ex2(lo_f32(x2)), ex2(hi_f32(x2)));
-          }
-          l2[i & 1] = fadd2(l2[i & 1], p2);
-          pk[i] = pack_half2(lo_f32(p2), hi_f32(p2));
-        }
-        tmem_st_32x32b_x16(tS + c / 2, pk);
-      }
+      publish(0);
+      exp_half(1);
       const uint64_t lsum = fadd2(l2[0], l2[1]);
       l += lo_f32(lsum) + hi_f32(lsum);
       if (lane == 0 && q == 0) FA_TRACE(t, j, 4);
-      tmem_st_wait();
+      publish(1);
       if (lane == 0 && q == 0) FA_TRACE(t, j, 5);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if constexpr (CG == 2)
-          mbar_arrive_cluster(p_full_addr);
-        else
-          mbar_arrive(&p_full[t]);
-      }
       if (lane == 0 && q == 0) FA_TRACE(t, j, 6);
+#ifdef FELIX_FA_TRACE
+      if (lane == 0 && blockIdx.x == 0 && j < 64) atomicMax(&g_fa_trace[t][j][7], clock64());
+#endif
     }
     // ---------------------------------------------------------------- epilogue
     if (ok && n > 0 &&
