@@ -355,10 +355,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t qa = sq + t * C_::kTileBytes;
         FA_TRACE(3, j, 6 + t);
         if (elect_one()) {
+          // descriptors of K step k = step 0's plus the byte offset / 16 (the
+          // start-address field holds any shared-memory address + offset here)
+          const uint64_t a0 = kmajor_desc<kBlockQ>(qa, 0);
+          const uint64_t b0 = kmajor_desc<C_::kKeys>(sk, 0);
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
-            const uint64_t ad = kmajor_desc<kBlockQ>(qa, k);
-            const uint64_t bd = kmajor_desc<C_::kKeys>(sk, k);
+            const uint64_t ad = a0 + uint64_t(((k >> 2) * (kBlockQ * 128) + (k & 3) * 32) >> 4);
+            const uint64_t bd = b0 + uint64_t(((k >> 2) * (C_::kKeys * 128) + (k & 3) * 32) >> 4);
             if constexpr (CG == 2)
               umma_f16_ss_pair(tmem + col_s(t), ad, bd, idesc_qk, k > 0 ? 1u : 0u);
             else
@@ -374,15 +378,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_pv = [&](uint32_t j, int t, int h) {
         const uint32_t sv = smem_u32(smem + C_::kVOff + (j % VST) * C_::kVBytes);
         if (elect_one()) {
+          const uint64_t v0 = vmajor_desc(sv, 0);
 #pragma unroll
           for (int k = h * (kBlockKV / 32); k < (h + 1) * (kBlockKV / 32); ++k) {
             const uint32_t a = tmem + col_s(t) + k * 8;
+            const uint64_t vd = v0 + uint64_t(k * (2048 >> 4));
             if constexpr (CG == 2)
-              umma_f16_ts_pair(tmem + col_o(t), a, vmajor_desc(sv, k), idesc_pv,
-                               (j > 0 || k > 0) ? 1u : 0u);
+              umma_f16_ts_pair(tmem + col_o(t), a, vd, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
             else
-              umma_f16_ts(tmem + col_o(t), a, vmajor_desc(sv, k), idesc_pv,
-                          (j > 0 || k > 0) ? 1u : 0u);
+              umma_f16_ts(tmem + col_o(t), a, vd, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
           }
           if (h == 1) {
             commit_all(&pv_done[t]);
