@@ -563,6 +563,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x16(tO + c, r);
           }
         }
+        // the speculative stores must land before their replacements (stores
+        // to the same TMEM columns are not ordered among themselves)
+        tmem_st_wait();
         l2[0] = l2[1] = 0ull;
         exp_half(0);
       }
