@@ -85,6 +85,15 @@ __device__ __forceinline__ uint64_t kmajor(uint32_t tile, int k) {
 __device__ __forceinline__ uint64_t mnmajor(uint32_t tile, int k) {
   return make_sdesc_sw128(tile + uint32_t(k) * 2048, kBlk * 128, 1024);
 }
+// The same descriptors from step 0's: the start-address field (address / 16)
+// advances by the byte offset / 16 and never carries for shared memory.
+template <int ROWS>
+__device__ __forceinline__ uint64_t kmajor_step(uint64_t d0, int k) {
+  return d0 + uint64_t(((k >> 2) * (ROWS * 128) + (k & 3) * 32) >> 4);
+}
+__device__ __forceinline__ uint64_t mnmajor_step(uint64_t d0, int k) {
+  return d0 + uint64_t(k * (2048 >> 4));
+}
 
 // ---------------------------------------------------------------------------
 // The kernel (D = 64 or 128): 128-query steps with the work of neighbouring
@@ -218,7 +227,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop converged (every lane waits, the lanes
+    // agree on the outcome); one elected lane issues the MMAs and commits.
+    {
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu,
+                          mbar_wait(bar, parity, abort_flag, p.status, kWdAttnMma)) != 0;
+      };
       const uint32_t id_st = make_idesc_f16_f32(kB, kB, false, false);  // S^T, dP^T
       const uint32_t id_acc = make_idesc_f16_f32(kB, kD, false, true);  // dV, dK
       const uint32_t id_dq = make_idesc_f16_f32(kB, kD, true, true);    // dQ
@@ -231,69 +246,88 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto sdo = [&](uint32_t s) { return smem_u32(smem + kDOOff + (s & 1u) * kTile); };
       auto issue_s = [&](uint32_t s) -> bool {
         BWD_TR_BEGIN(t0);
-        if (!mbar_wait(qdo_full + (s & 1u), (s >> 1) & 1u, abort_flag, p.status, kWdAttnMma))
-          return false;
+        if (!wait_all(qdo_full + (s & 1u), (s >> 1) & 1u)) return false;
         BWD_TR_ACC(tr_qdo, t0);
         tc_fence_after();
+        if (elect_one()) {
+          const uint64_t a0 = kmajor<kB>(sK, 0), b0 = kmajor<kB>(sq(s), 0);
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k)
-          if (!(FELIX_FA_BWD_EXP_SKIP & 1))
-          umma_f16_ss(tmem + kColS, kmajor<kB>(sK, k), kmajor<kB>(sq(s), k), id_st,
-                      k > 0 ? 1u : 0u);
-        umma_commit(s_full);
+          for (int k = 0; k < kD / 16; ++k)
+            if (!(FELIX_FA_BWD_EXP_SKIP & 1))
+              umma_f16_ss(tmem + kColS, kmajor_step<kB>(a0, k), kmajor_step<kB>(b0, k), id_st,
+                          k > 0 ? 1u : 0u);
+          umma_commit(s_full);
+        }
+        __syncwarp();
         return true;
       };
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kWdAttnMma) && issue_s(0);
+      bool ok = wait_all(kv_full, 0) && issue_s(0);
       for (uint32_t i = 0; ok && i < n; ++i) {
         BWD_TR_BEGIN(t1);
-        if (!(ok = mbar_wait(p_ready, i & 1u, abort_flag, p.status, kWdAttnMma))) break;
+        if (!(ok = wait_all(p_ready, i & 1u))) break;
         BWD_TR_ACC(tr_pr, t1);
         tc_fence_after();
+        if (elect_one()) {
+          const uint64_t b0 = mnmajor(sdo(i), 0);
 #pragma unroll
-        for (int k = 0; k < kB / 16; ++k)
-          if (!(FELIX_FA_BWD_EXP_SKIP & 4))
-          umma_f16_ts(tmem + kColDV, tmem + kColS + packed_col(16 * k), mnmajor(sdo(i), k),
-                      id_acc, (i > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kB / 16; ++k)
+            if (!(FELIX_FA_BWD_EXP_SKIP & 4))
+              umma_f16_ts(tmem + kColDV, tmem + kColS + packed_col(16 * k), mnmajor_step(b0, k),
+                          id_acc, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        __syncwarp();
         if (i + 1 < n && !(ok = issue_s(i + 1))) break;
         // dQ(i - 1) sits in the dP^T columns until it has been read out
         BWD_TR_BEGIN(t2);
-        if (i > 0 && !(ok = mbar_wait(dq_free, (i - 1) & 1u, abort_flag, p.status, kWdAttnMma)))
-          break;
+        if (i > 0 && !(ok = wait_all(dq_free, (i - 1) & 1u))) break;
         BWD_TR_ACC(tr_dqf, t2);
         tc_fence_after();
+        if (elect_one()) {
+          const uint64_t a0 = kmajor<kB>(sV, 0), b0 = kmajor<kB>(sdo(i), 0);
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k)
-          if (!(FELIX_FA_BWD_EXP_SKIP & 2))
-          umma_f16_ss(tmem + kColDP, kmajor<kB>(sV, k), kmajor<kB>(sdo(i), k), id_st,
-                      k > 0 ? 1u : 0u);
-        umma_commit(dp_full);
+          for (int k = 0; k < kD / 16; ++k)
+            if (!(FELIX_FA_BWD_EXP_SKIP & 2))
+              umma_f16_ss(tmem + kColDP, kmajor_step<kB>(a0, k), kmajor_step<kB>(b0, k), id_st,
+                          k > 0 ? 1u : 0u);
+          umma_commit(dp_full);
+        }
+        __syncwarp();
         BWD_TR_BEGIN(t3);
-        if (!(ok = mbar_wait(ds_ready, i & 1u, abort_flag, p.status, kWdAttnMma))) break;
+        if (!(ok = wait_all(ds_ready, i & 1u))) break;
         BWD_TR_ACC(tr_pr, t3);
         tc_fence_after();
+        if (elect_one()) {
+          const uint64_t b0 = mnmajor(sq(i), 0);
 #pragma unroll
-        for (int k = 0; k < kB / 16; ++k)
-          if (!(FELIX_FA_BWD_EXP_SKIP & 8))
-          umma_f16_ts(tmem + kColDK, tmem + kColDP + packed_col(16 * k), mnmajor(sq(i), k),
-                      id_acc, (i > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kB / 16; ++k)
+            if (!(FELIX_FA_BWD_EXP_SKIP & 8))
+              umma_f16_ts(tmem + kColDK, tmem + kColDP + packed_col(16 * k), mnmajor_step(b0, k),
+                          id_acc, (i > 0 || k > 0) ? 1u : 0u);
+          const uint64_t a1 = mnmajor(sDS, 0), b1 = mnmajor(sK, 0);
 #pragma unroll
-        for (int k = 0; k < kB / 16; ++k)
-          if (!(FELIX_FA_BWD_EXP_SKIP & 16))
-          umma_f16_ss(tmem + kColDP, mnmajor(sDS, k), mnmajor(sK, k), id_dq, k > 0 ? 1u : 0u);
-        umma_commit(qdo_empty + (i & 1u));
-        umma_commit(dq_full);
+          for (int k = 0; k < kB / 16; ++k)
+            if (!(FELIX_FA_BWD_EXP_SKIP & 16))
+              umma_f16_ss(tmem + kColDP, mnmajor_step(a1, k), mnmajor_step(b1, k), id_dq,
+                          k > 0 ? 1u : 0u);
+          umma_commit(qdo_empty + (i & 1u));
+          umma_commit(dq_full);
+        }
+        __syncwarp();
       }
-      umma_commit(done);
+      if (elect_one()) umma_commit(done);
+      __syncwarp();
       int dummy = 0;
       mbar_wait(done, 0, &dummy, p.status, kWdDrain, 100000000ull);
       long long tr_all = 0;
       (void)tr_all;
       BWD_TR_ACC(tr_all, tr_total);
-      BWD_TR_FLUSH(0, tr_qdo);
-      BWD_TR_FLUSH(1, tr_dqf);
-      BWD_TR_FLUSH(2, tr_pr);
-      BWD_TR_FLUSH(3, tr_all);
-      BWD_TR_FLUSH(15, 1);
+      if (lane == 0) {
+        BWD_TR_FLUSH(0, tr_qdo);
+        BWD_TR_FLUSH(1, tr_dqf);
+        BWD_TR_FLUSH(2, tr_pr);
+        BWD_TR_FLUSH(3, tr_all);
+        BWD_TR_FLUSH(15, 1);
+      }
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- element-wise

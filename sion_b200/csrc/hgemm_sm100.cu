@@ -363,7 +363,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && rank == 0) {  // a pair's leader issues for both CTAs
+    // a pair's leader issues for both CTAs. The whole warp runs the loop
+    // converged (every lane waits, the lanes agree on the outcome); one
+    // elected lane issues the MMAs and commits.
+    if (rank == 0) {
+      auto wait_all = [&](uint64_t* bar, uint32_t parity, unsigned site) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, site)) != 0;
+      };
       const uint32_t idesc = make_idesc_f16_f32(BM * CG, BN, false, p.b_mn_major != 0);
       // completion signals go to the barrier in every CTA of the group
       auto commit_all = [&](uint64_t* bar) {
@@ -382,58 +388,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       while (ok && sc.next(u)) {
         const uint32_t buf = i & 1u;
-        if (!mbar_wait(&tempty[buf], ((i >> 1) & 1u) ^ 1u, abort_flag, p.status,
-                       kWdMmaTmemEmpty)) {
+        if (!wait_all(&tempty[buf], ((i >> 1) & 1u) ^ 1u, kWdMmaTmemEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
         for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kWdMmaFull)) {
+          if (!wait_all(&full[stage], phase, kWdMmaFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(ring + stage * C_::kStageBytes);
-          const uint32_t b0 = a0 + C_::kABytes;
-#pragma unroll
-          for (int k = 0; k < BK * C_::kSub / 16; ++k) {
-            uint64_t ad, bd;
+          if (elect_one()) {
+            const uint32_t a0 = smem_u32(ring + stage * C_::kStageBytes);
+            const uint32_t b0 = a0 + C_::kABytes;
+            // descriptors of step k = step 0's + byte offset / 16 (the
+            // start-address field never carries for shared memory)
+            uint64_t ad0, bd0;
             if constexpr (BK == 64) {
-              // K-major: 64-deep k-blocks of rows x 128 B, 32 B per 16 k;
-              // MN-major: 64-wide chunks of (BK * kSub) k-rows x 128 B
-              constexpr int kq = BK / 16;
-              ad = make_sdesc_sw128(a0 + (k / kq) * (BM * BK * 2) + (k % kq) * 32, 16, 1024);
-              bd = p.b_mn_major
-                       ? make_sdesc_sw128(b0 + k * 2048, BK * C_::kSub * 128, 1024)
-                       : make_sdesc_sw128(b0 + (k / kq) * (C_::kBRows * BK * 2) + (k % kq) * 32,
-                                          16, 1024);
+              ad0 = make_sdesc_sw128(a0, 16, 1024);
+              bd0 = p.b_mn_major ? make_sdesc_sw128(b0, BK * C_::kSub * 128, 1024)
+                                 : make_sdesc_sw128(b0, 16, 1024);
             } else {
-              ad = make_sdesc_sw64(a0 + k * 32, 16, 512);
-              bd = p.b_mn_major ? make_sdesc_sw128(b0 + k * 2048, 64 * BK * 2, 1024)
-                                : make_sdesc_sw64(b0 + k * 32, 16, 512);
+              ad0 = make_sdesc_sw64(a0, 16, 512);
+              bd0 = p.b_mn_major ? make_sdesc_sw128(b0, 64 * BK * 2, 1024)
+                                 : make_sdesc_sw64(b0, 16, 512);
             }
-            if constexpr (CG == 2)
-              umma_f16_ss_pair(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
-            else
-              umma_f16_ss(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int k = 0; k < BK * C_::kSub / 16; ++k) {
+              uint32_t aoff, boff;
+              if constexpr (BK == 64) {
+                // K-major: 64-deep k-blocks of rows x 128 B, 32 B per 16 k;
+                // MN-major: 64-wide chunks of (BK * kSub) k-rows x 128 B
+                constexpr int kq = BK / 16;
+                aoff = (k / kq) * (BM * BK * 2) + (k % kq) * 32;
+                boff = p.b_mn_major ? k * 2048 : (k / kq) * (C_::kBRows * BK * 2) + (k % kq) * 32;
+              } else {
+                aoff = k * 32;
+                boff = p.b_mn_major ? k * 2048 : k * 32;
+              }
+              const uint64_t ad = ad0 + (aoff >> 4), bd = bd0 + (boff >> 4);
+              if constexpr (CG == 2)
+                umma_f16_ss_pair(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+              else
+                umma_f16_ss(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+            }
+            commit_all(&empty[stage]);
           }
-          commit_all(&empty[stage]);
+          __syncwarp();
           if (++stage == NS) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        commit_all(&tfull[buf]);
+        if (elect_one()) commit_all(&tfull[buf]);
+        __syncwarp();
         ++i;
       }
       // Wait (bounded) until every issued MMA has completed before teardown.
-      if constexpr (CG == 2)
-        umma_commit_pair(smem_u32(drain));
-      else
-        umma_commit(drain);
+      if (elect_one()) {
+        if constexpr (CG == 2)
+          umma_commit_pair(smem_u32(drain));
+        else
+          umma_commit(drain);
+      }
+      __syncwarp();
       int dummy = 0;
       mbar_wait(drain, 0, &dummy, p.status, kWdDrain, 100000000ull);
     }
