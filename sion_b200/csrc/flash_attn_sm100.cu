@@ -133,9 +133,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-#ifndef FELIX_FA_EMU_EVERY
-#define FELIX_FA_EMU_EVERY 0
-#endif
 #ifndef FELIX_FA_WAIT_PV
 #define FELIX_FA_WAIT_PV 0
 #endif
@@ -144,32 +141,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // order, so the later MMA's accumulator writes to S_t cannot overtake the
 // earlier MMA's reads of P_t from the same columns.
 constexpr int kWaitPV = FELIX_FA_WAIT_PV;
-// One column pair in kEmuEvery takes its exponentials on the FMA pipe
-// (exp2_fma_x2) instead of MUFU; 0 disables the split.
-constexpr int kEmuEvery = FELIX_FA_EMU_EVERY;
-
-// 2^x for two lanes on the FMA pipe, x <= 8 (softmax exponents are relative to
-// a running max that is at most 8 below the true one). Range reduction
-// x = j + f with j = round(x) (magic-number add), f in [-1/2, 1/2]; 2^f from a
-// degree-3 polynomial fitted here by a Remez exchange on the relative error
-// over [-1/2, 1/2] (max relative error 7.5e-5 in fp32 evaluation, below the
-// fp16 half-ulp 4.9e-4 of P); 2^j is added into the exponent field. Inputs are
-// clamped at -125 so masked keys (-inf) give 2^-125, which rounds to 0 in fp16.
-__device__ __forceinline__ uint64_t exp2_fma_x2(uint64_t x2) {
-  const float x0 = fmaxf(lo_f32(x2), -125.0f), x1 = fmaxf(hi_f32(x2), -125.0f);
-  const uint64_t x = pack_f32x2(x0, x1);
-  const uint64_t t = fadd2(x, pack_f32x2(12582912.0f, 12582912.0f));  // 1.5 * 2^23
-  const uint64_t jf = fadd2(t, pack_f32x2(-12582912.0f, -12582912.0f));
-  const uint64_t f = ffma2(jf, pack_f32x2(-1.0f, -1.0f), x);
-  uint64_t p = ffma2(pack_f32x2(0.0551716685295105f, 0.0551716685295105f), f,
-                     pack_f32x2(0.2426111251115799f, 0.2426111251115799f));
-  p = ffma2(p, f, pack_f32x2(0.6932609677314758f, 0.6932609677314758f));
-  p = ffma2(p, f, pack_f32x2(0.9999280571937561f, 0.9999280571937561f));
-  const float r0 = __int_as_float(__float_as_int(lo_f32(p)) + (__float_as_int(lo_f32(t)) << 23));
-  const float r1 = __int_as_float(__float_as_int(hi_f32(p)) + (__float_as_int(hi_f32(t)) << 23));
-  return pack_f32x2(r0, r1);
-}
-
 // Smem descriptor of a K-major ROWS x D tile (chunks of 64 columns, ROWS*128
 // bytes each), advanced to K step k (16 elements).
 template <int ROWS>
@@ -489,8 +460,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (uint32_t(i) >= valid) s[i] = -INFINITY;
       }
       // P = 2^(s * scale_log2 - m) for keys [64 h, 64 h + 64), two columns at
-      // a time in packed fp32x2 (one pair in kEmuEvery on the FMA pipe, the
-      // rest on MUFU), stored as fp16 pairs over the first half of S's columns
+      // a time in packed fp32x2, exponentials on MUFU, stored as fp16 pairs over
+      // the first half of S's columns
       const uint64_t scale2 = pack_f32x2(sl2, sl2);
       uint64_t l2[2] = {0ull, 0ull};  // packed partial row sums
       auto exp_half = [&](int h) {
@@ -502,12 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 16; ++i) {
             const int e = c + 2 * i;
             const uint64_t x2 = ffma2(pack_f32x2(s[e], s[e + 1]), scale2, negm2);
-            uint64_t p2;
-            if (kEmuEvery > 0 && (i % (kEmuEvery > 0 ? kEmuEvery : 1)) == kEmuEvery - 1) {
-              p2 = exp2_fma_x2(x2);
-            } else {
-              p2 = pack_f32x2(ex2(lo_f32(x2)), ex2(hi_f32(x2)));
-            }
+            const uint64_t p2 = pack_f32x2(ex2(lo_f32(x2)), ex2(hi_f32(x2)));
             l2[i & 1] = fadd2(l2[i & 1], p2);
             pk[i] = pack_half2(lo_f32(p2), hi_f32(p2));
           }
