@@ -436,16 +436,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait(&s_full[t], j & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
       tc_fence_after();
       if (lane == 0 && q == 0) FA_TRACE(t, j, 1);
-      float s[kBlockKV];
-#pragma unroll
-      for (int c = 0; c < kBlockKV; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tS + c, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(r[i]);
-      }
-      tmem_ld_wait();
-      if (lane == 0 && q == 0) FA_TRACE(t, j, 2);
       // keys of this block the row may see: the ragged tail of the sequence
       // and, when causal, keys past the row's own position are masked
       uint32_t valid = p.S - j * kBlockKV;
@@ -454,20 +444,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t upto = qrow + 1 > j * kBlockKV ? qrow + 1 - j * kBlockKV : 0u;
         valid = min(valid, upto);
       }
-      if (__any_sync(0xffffffffu, valid < uint32_t(kBlockKV))) {
+      const bool ragged = __any_sync(0xffffffffu, valid < uint32_t(kBlockKV)) != 0;
+      // S is held 64 keys at a time (half h of the block), so the registers
+      // left over give the exponential phase room to overlap its MUFU work
+      constexpr int kHalf = kBlockKV / 2;
+      float s[kHalf];
+      auto load_half = [&](int h) {  // issues the loads; tmem_ld_wait() completes them
 #pragma unroll
-        for (int i = 0; i < kBlockKV; ++i)
-          if (uint32_t(i) >= valid) s[i] = -INFINITY;
-      }
-      // P = 2^(s * scale_log2 - m) for keys [64 h, 64 h + 64), two columns at
-      // a time in packed fp32x2, exponentials on MUFU, stored as fp16 pairs over
+        for (int c = 0; c < kHalf; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tS + h * kHalf + c, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(r[i]);
+        }
+      };
+      auto mask_half = [&](int h) {
+        if (ragged) {
+#pragma unroll
+          for (int i = 0; i < kHalf; ++i)
+            if (uint32_t(h * kHalf + i) >= valid) s[i] = -INFINITY;
+        }
+      };
+      auto max_half = [&]() -> float {  // 3-input max, 4 independent chains
+        float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+        for (int i = 4; i < kHalf; i += 8) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) m4[c] = fmax3(m4[c], s[i + c], s[i + 4 + c]);
+        }
+        return fmax3(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
+      };
+      // P = 2^(s * scale_log2 - m) for the keys of half h, two columns at a
+      // time in packed fp32x2, exponentials on MUFU, stored as fp16 pairs over
       // the first half of S's columns
       const uint64_t scale2 = pack_f32x2(sl2, sl2);
       uint64_t l2[2] = {0ull, 0ull};  // packed partial row sums
       auto exp_half = [&](int h) {
         const uint64_t negm2 = pack_f32x2(-m, -m);
 #pragma unroll
-        for (int c = h * (kBlockKV / 2); c < (h + 1) * (kBlockKV / 2); c += 32) {
+        for (int c = 0; c < kHalf; c += 32) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -477,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             l2[i & 1] = fadd2(l2[i & 1], p2);
             pk[i] = pack_half2(lo_f32(p2), hi_f32(p2));
           }
-          tmem_st_32x32b_x16(tS + c / 2, pk);
+          tmem_st_32x32b_x16(tS + (h * kHalf + c) / 2, pk);
         }
       };
       auto publish = [&](int h) {
@@ -491,21 +506,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&p_full[2 * t + h]);
         }
       };
-      // The first half is computed against the current running max while the
-      // row max of this block is formed (the two are independent, so they
-      // interleave); it is recomputed only when the max grows past the
-      // threshold (always for the first block, where m is -inf and these
-      // values are discarded).
+      // the second half's max first, then the first half, whose exponentials
+      // are computed against the current running max while its own max forms
+      // (the two are independent, so they interleave); they are recomputed
+      // only when the max grows past the threshold (always for the first
+      // block, where m is -inf and these values are discarded)
+      load_half(1);
+      tmem_ld_wait();
+      mask_half(1);
+      const float mx1 = max_half();
+      load_half(0);
+      tmem_ld_wait();
+      if (lane == 0 && q == 0) FA_TRACE(t, j, 2);
+      mask_half(0);
       exp_half(0);
-      // row max: 3-input max, 4 independent chains
-      float m4[4] = {s[0], s[1], s[2], s[3]};
-#pragma unroll
-      for (int i = 4; i < kBlockKV; i += 8) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) m4[c] = fmax3(m4[c], s[i + c], s[i + 4 + c]);
-      }
-      const float mx = fmax3(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
-      const float mc = mx * sl2;
+      const float mc = fmaxf(max_half(), mx1) * sl2;
       if (lane == 0 && q == 0) FA_TRACE(t, j, 3);
       const bool need = mc > m + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
@@ -535,7 +550,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         l2[0] = l2[1] = 0ull;
         exp_half(0);
       }
+      load_half(1);  // columns 64..127: untouched by P and by PV
       publish(0);
+      tmem_ld_wait();
+      mask_half(1);
       exp_half(1);
       const uint64_t lsum = fadd2(l2[0], l2[1]);
       l += lo_f32(lsum) + hi_f32(lsum);
