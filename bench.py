@@ -325,7 +325,8 @@ def cpu_sample(cfg, budget_s: float = 10.0):
         flops_per = 2.0 * rows * cfg.N * cfg.K
         def fn():
             return torch.matmul(a, b)
-        desc = (f"torch.matmul fp32 on CPU (fp16 inputs upcast), {rows} rows of A x full B "
+        upcast = "fp32 inputs" if A.dtype == torch.float32 else "fp16 inputs upcast"
+        desc = (f"torch.matmul fp32 on CPU ({upcast}), {rows} rows of A x full B "
                 f"per call, repeated for ~{budget_s:.0f} s")
     fn()
     n, t0 = 0, time.perf_counter()

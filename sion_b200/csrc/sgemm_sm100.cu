@@ -31,6 +31,24 @@
 namespace felix_sm100 {
 namespace sgemm {
 
+#ifdef FELIX_SGEMM_TRACE
+// Development-only per-CTA timeline (compiled out of the library build):
+// [cta][event] = globaltimer ns.
+__device__ unsigned long long g_sg_trace[1024][8];
+#define SG_TR(ev)                                                          \
+  do {                                                                     \
+    if (threadIdx.x == 0 && blockIdx.x < 1024) {                           \
+      unsigned long long t_;                                               \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                \
+      g_sg_trace[blockIdx.x][ev] = t_;                                     \
+    }                                                                      \
+  } while (0)
+#else
+#define SG_TR(ev) \
+  do {            \
+  } while (0)
+#endif
+
 #ifndef FELIX_SGEMM_BK
 #define FELIX_SGEMM_BK 16
 #endif
@@ -257,12 +275,22 @@ constexpr int kTmaStages = 3;
 // registers). 4 (LDS.128) needs 16 more registers and spilled at the 128 that
 // two CTAs per SM allow: 4096^3 45.4 vs 51.9 TFLOP/s.
 constexpr int kTmaAk = 2;
-constexpr int kTmaATile = BM * kTmaBk * 4;  // 16 KB
 constexpr int kTmaBTile = kTmaBk * BN * 4;  // 16 KB (BN = 128)
-constexpr int kTmaSmem = kTmaStages * (kTmaATile + kTmaBTile) + 2 * kTmaStages * 8 + 16;
+// A tile of AP floats per row (AP = row pitch). AP = 32: the rows a warp reads
+// at once (4 apart) share banks, a 2-way conflict on every A load. AP = 36: the
+// box is 36 k wide (the last 4 columns are the next k-tile's, unused) and the
+// 144-byte pitch puts those rows in different banks; each row then spans two
+// L2 lines. Measured: 36 is faster for K <= 2048 (1024^3 69.6 -> 67.6 us,
+// 2048^3 390 -> 376 us), 32 for long K (4096^3 2650 vs 2803 us).
+template <int AP>
+struct TmaTile {
+  static constexpr int kA = BM * AP * 4;
+  static constexpr int kSmem = kTmaStages * (kA + kTmaBTile) + 2 * kTmaStages * 8 + 16;
+};
 static_assert(BN == 128, "TMA main loop: 128 x 128 tiles");
 
 struct TmaPipe {
+  uint32_t tr_seg;  // trace builds: segment index of the current main loop
   float* sA;
   float* sB;
   uint64_t* full;
@@ -271,6 +299,7 @@ struct TmaPipe {
   uint32_t kt_load, kt_use;  // k-tiles issued / consumed by this CTA so far
 };
 
+template <int AP>
 __device__ __forceinline__ bool tma_issue(TmaPipe& q, const CUtensorMap* tmA,
                                           const CUtensorMap* tmB, const Params& p, uint32_t m0,
                                           uint32_t n0, uint32_t kb) {
@@ -278,8 +307,8 @@ __device__ __forceinline__ bool tma_issue(TmaPipe& q, const CUtensorMap* tmA,
   if (!felix_sm100::mbar_wait(q.empty + st, (use & 1u) ^ 1u, q.abort_flag, p.status,
                               felix_sm100::kWdProducerEmpty))
     return false;
-  felix_sm100::mbar_arrive_expect_tx(q.full + st, kTmaATile + kTmaBTile);
-  felix_sm100::tma_load_2d(q.sA + st * (kTmaATile / 4), tmA, q.full + st, int(kb * kTmaBk),
+  felix_sm100::mbar_arrive_expect_tx(q.full + st, TmaTile<AP>::kA + kTmaBTile);
+  felix_sm100::tma_load_2d(q.sA + st * (TmaTile<AP>::kA / 4), tmA, q.full + st, int(kb * kTmaBk),
                            int(m0));
   felix_sm100::tma_load_2d(q.sB + st * (kTmaBTile / 4), tmB, q.full + st, int(n0),
                            int(kb * kTmaBk));
@@ -289,6 +318,7 @@ __device__ __forceinline__ bool tma_issue(TmaPipe& q, const CUtensorMap* tmA,
 
 // acc = A[m0 : m0 + 128, kbeg : kend] * B[kbeg : kend, n0 : n0 + 128] with
 // kbeg a multiple of 32 (k past kend inside the last k-tile must be past K).
+template <int AP>
 __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
                                              const CUtensorMap* tmB, const Params& p,
                                              uint32_t m0, uint32_t n0, uint32_t kbeg,
@@ -304,27 +334,25 @@ __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
   bool ok = true;
   if (t == 0)
     for (uint32_t j = 0; ok && j < n && j < kTmaStages - 1; ++j)
-      ok = tma_issue(q, tmA, tmB, p, m0, n0, kb0 + j);
+      ok = tma_issue<AP>(q, tmA, tmB, p, m0, n0, kb0 + j);
   for (uint32_t j = 0; j < n; ++j) {
     const uint32_t st = q.kt_use % kTmaStages;
     if (!felix_sm100::mbar_wait(q.full + st, (q.kt_use / kTmaStages) & 1u, q.abort_flag, p.status,
                                 felix_sm100::kWdMmaFull))
       return false;
-    const float* a_s = q.sA + st * (kTmaATile / 4);  // [128][32]
+    if (j == 0) SG_TR(q.tr_seg * 3 + 1);
+    const float* a_s = q.sA + st * (TmaTile<AP>::kA / 4);  // [128][AP]
     const float* b_s = q.sB + st * (kTmaBTile / 4);  // [32][128]
     // one group of kTmaAk k-steps per iteration, not unrolled: unrolled, the
     // compiler hoists the B loads of later groups and spills at 128 registers
 #pragma unroll 1
     for (int k2 = 0; k2 < kTmaBk / kTmaAk; ++k2) {
-      // A: kTmaAk consecutive k of each of the thread's 8 rows per load (the
-      // two rows a warp reads at once share banks: a 2-way conflict, cheaper
-      // here than the per-load address arithmetic of a swizzled tile, which
-      // measured 40 vs 52 TFLOP/s at 4096^3)
+      // A: kTmaAk consecutive k of each of the thread's 8 rows per load
       float af[8][kTmaAk];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint32_t row = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
-        const float2 v = *reinterpret_cast<const float2*>(a_s + row * kTmaBk + k2 * kTmaAk);
+        const float2 v = *reinterpret_cast<const float2*>(a_s + row * AP + k2 * kTmaAk);
         af[i][0] = v.x;
         af[i][1] = v.y;
       }
@@ -350,7 +378,7 @@ __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
     if (lane == 0) felix_sm100::mbar_arrive(q.empty + st);
     ++q.kt_use;
     if (t == 0 && ok && j + kTmaStages - 1 < n)
-      ok = tma_issue(q, tmA, tmB, p, m0, n0, kb0 + j + kTmaStages - 1);
+      ok = tma_issue<AP>(q, tmA, tmB, p, m0, n0, kb0 + j + kTmaStages - 1);
   }
   return true;
 }
@@ -374,7 +402,7 @@ __device__ __forceinline__ uint32_t sk_cta_of(uint64_t x, uint32_t P, uint64_t I
   return static_cast<uint32_t>(((x + 1) * P - 1) / I);
 }
 
-template <bool VEC, bool TMA>
+template <bool VEC, bool TMA, int AP = 32>
 __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
     sgemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const Params p) {
@@ -390,8 +418,8 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
   TmaPipe q{};
   if constexpr (TMA) {
     q.sA = reinterpret_cast<float*>(dsmem);
-    q.sB = reinterpret_cast<float*>(dsmem + kTmaStages * kTmaATile);
-    q.full = reinterpret_cast<uint64_t*>(dsmem + kTmaStages * (kTmaATile + kTmaBTile));
+    q.sB = reinterpret_cast<float*>(dsmem + kTmaStages * TmaTile<AP>::kA);
+    q.full = reinterpret_cast<uint64_t*>(dsmem + kTmaStages * (TmaTile<AP>::kA + kTmaBTile));
     q.empty = q.full + kTmaStages;
     q.abort_flag = &s_abort;
     if (t == 0) {
@@ -406,9 +434,10 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
     }
     __syncthreads();
   }
+  SG_TR(0);
   auto run = [&](uint32_t m0, uint32_t n0, uint32_t kbeg, uint32_t kend) -> bool {
     if constexpr (TMA) {
-      return mainloop_tma(q, &tmA, &tmB, p, m0, n0, kbeg, kend, acc);
+      return mainloop_tma<AP>(q, &tmA, &tmB, p, m0, n0, kbeg, kend, acc);
     } else {
       mainloop<VEC>(p, m0, n0, kbeg, kend, As, Bs, acc);
       return true;
@@ -432,7 +461,9 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
       const uint64_t left = end - it;
       const uint32_t kb1 = left < uint64_t(KT - kb0) ? kb0 + static_cast<uint32_t>(left) : KT;
       const uint32_t m0 = (tile / p.tiles_n) * BM, n0 = (tile % p.tiles_n) * BN;
+      q.tr_seg = it == start ? 0u : 1u;
       if (!run(m0, n0, kb0 * p.bk, min(p.K, kb1 * p.bk))) break;
+      SG_TR(q.tr_seg * 3 + 2);
       if (kb0 == 0 && kb1 == KT) {
         store_acc<VEC>(p, m0, n0, acc);
       } else {
@@ -475,9 +506,11 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
           store_acc<VEC>(p, m0, n0, acc);
         }
       }
+      SG_TR(q.tr_seg * 3 + 3);
       it += kb1 - kb0;
     }
     drain_tma<TMA>(q, p);
+    SG_TR(7);
     return;
   }
 
@@ -532,6 +565,12 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
 
 }  // namespace sgemm
 }  // namespace felix_sm100
+
+#ifdef FELIX_SGEMM_TRACE
+extern "C" void sg_trace_fetch(void* dst) {
+  cudaMemcpyFromSymbol(dst, felix_sm100::sgemm::g_sg_trace, sizeof(felix_sm100::sgemm::g_sg_trace));
+}
+#endif
 
 // Scratch of felix_sgemm_noalloc: the fixed counter block followed by room
 // for 256 partial 128 x 128 fp32 tiles (16 MiB + 16 KiB). It is part of the
@@ -624,23 +663,30 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
   p.bk = tma ? uint32_t(kTmaBk) : uint32_t(BK);
   p.status = dev->status_word;
   CUtensorMap tmA{}, tmB{};
+  const int ap = K <= 2048 ? 36 : 32;  // A row pitch (TmaTile)
   if (tma) {
-    if (encode_tmap_2d_f32(&tmA, A, K, M, uint64_t(K) * 4, kTmaBk, BM) ||
+    if (encode_tmap_2d_f32(&tmA, A, K, M, uint64_t(K) * 4, uint32_t(ap), BM) ||
         encode_tmap_2d_f32(&tmB, B, N, K, uint64_t(N) * 4, BN, kTmaBk))
       return api_error("sgemm: cuTensorMapEncodeTiled failed");
     static int configured[64] = {0};
     if (dev->ordinal < 0 || dev->ordinal >= 64) return api_error("sgemm: device ordinal");
     if (!configured[dev->ordinal]) {
-      cudaError_t e = cudaFuncSetAttribute(sgemm_kernel<true, true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem);
+      cudaError_t e = cudaFuncSetAttribute(sgemm_kernel<true, true, 32>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           TmaTile<32>::kSmem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(sgemm_kernel<true, true, 36>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<36>::kSmem);
       if (e != cudaSuccess) return FelixCode{FELIX_API_ERROR, e};
       configured[dev->ordinal] = 1;
     }
   }
   auto launch = [&](dim3 grid) -> FelixCode {
     constexpr size_t kRegSmem = size_t(2) * BK * (BM + APAD) * 4 + size_t(2) * BK * BN * 4;
-    if (tma)
-      sgemm_kernel<true, true><<<grid, kThreads, kTmaSmem, stream>>>(tmA, tmB, p);
+    if (tma && ap == 36)
+      sgemm_kernel<true, true, 36><<<grid, kThreads, TmaTile<36>::kSmem, stream>>>(tmA, tmB, p);
+    else if (tma)
+      sgemm_kernel<true, true, 32><<<grid, kThreads, TmaTile<32>::kSmem, stream>>>(tmA, tmB, p);
     else if (vec)
       sgemm_kernel<true, false><<<grid, kThreads, kRegSmem, stream>>>(tmA, tmB, p);
     else
