@@ -1,6 +1,6 @@
 #!/usr/bin/env bash
 # Builds the reference's own SGEMM / HGEMM / flash-attention kernels for sm_100a
-# straight from its unmodified sources (REF, default /root/reference; nothing is
+# straight from its unmodified sources (the checkout named by REF; nothing is
 # copied into this repository) plus oracle/ref_shim.cpp, into
 # oracle/_ref/libsion_ref.so. TEST INFRASTRUCTURE ONLY (comparator in tests and
 # bench.py). The reference's CuTe kernels need CUTLASS/CuTe headers; its own
