@@ -42,6 +42,20 @@ constexpr int kBlockKV = 128;  // keys per KV block (UMMA N of QK^T, K of PV)
 constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
+// Register split: the kernel launches with 168 registers per thread (384
+// threads); warpgroup 0 (loaders, MMA issuer; it spills below 80) drops to 80
+// and the two softmax warpgroups rise to 200, so a softmax thread holds its
+// whole 128-column S row (loaded with one wait) without spilling.
+// setmaxnreg.inc draws on the registers the block was launched with:
+// 80 x 128 + 200 x 256 = 61440 <= 168 x 384 = 64512. The host refuses to
+// launch if the compiled kernel's count differs from 168.
+#ifndef FELIX_FA_REGSPLIT
+#define FELIX_FA_REGSPLIT 1
+#endif
+constexpr bool kRegSplit = FELIX_FA_REGSPLIT != 0;
+constexpr int kRegsLaunch = 168, kRegsSide = 80, kRegsSoftmax = 200;
+static_assert(kRegsSide * 128 + kRegsSoftmax * 256 <= kRegsLaunch * kThreads, "register split");
+
 // CG = 1: one CTA per 256 query rows. CG = 2 (D = 128): a cluster of two CTAs
 // per 512 query rows whose MMAs are cta_group::2 (M = 256); each CTA then
 // holds half of every K block (64 keys) and half of every V block (64 of the
@@ -242,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (warp == 0 || warp == 2) {
+    if constexpr (kRegSplit) setmaxnreg_dec<kRegsSide>();
     // ------------------------------------------------- loaders: warp 0 Q + K, warp 2 V
     if (elect_one()) {
       const bool is_k = warp == 0;
@@ -298,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
+    if constexpr (kRegSplit) setmaxnreg_dec<kRegsSide>();
     // ---------------------------------------------------------------- MMA issuer
     // The whole warp runs the loop (waits, descriptor arithmetic) converged;
     // one elected lane issues the MMAs and commits.
@@ -419,7 +435,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int dummy = 0;
       mbar_wait(drain, 0, &dummy, p.status, kWdDrain, 100000000ull);
     }
+  } else if (warp == 3) {
+    if constexpr (kRegSplit) setmaxnreg_dec<kRegsSide>();
   } else if (warp >= 4) {
+    if constexpr (kRegSplit) setmaxnreg_inc<kRegsSoftmax>();
     // ---------------------------------------------------------------- softmax
     const int t = warp >= 8 ? 1 : 0;
     const uint32_t q = warp & 3u;
@@ -448,29 +467,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       // S is held 64 keys at a time (half h of the block), so the registers
       // left over give the exponential phase room to overlap its MUFU work
       constexpr int kHalf = kBlockKV / 2;
-      float s[kHalf];
-      auto load_half = [&](int h) {  // issues the loads; tmem_ld_wait() completes them
+      float s[kHalf];                       // keys of the half being exponentiated
+      float s_hi[kRegSplit ? kHalf : 1];    // register split: the second half, held
+      auto load_half = [&](float* dst, int h) {  // issues the loads; tmem_ld_wait() completes them
 #pragma unroll
         for (int c = 0; c < kHalf; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tS + h * kHalf + c, r);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(r[i]);
+          for (int i = 0; i < 32; ++i) dst[c + i] = __uint_as_float(r[i]);
         }
       };
-      auto mask_half = [&](int h) {
+      auto mask_half = [&](float* v, int h) {
         if (ragged) {
 #pragma unroll
           for (int i = 0; i < kHalf; ++i)
-            if (uint32_t(h * kHalf + i) >= valid) s[i] = -INFINITY;
+            if (uint32_t(h * kHalf + i) >= valid) v[i] = -INFINITY;
         }
       };
-      auto max_half = [&]() -> float {  // 3-input max, 4 independent chains
-        float m4[4] = {s[0], s[1], s[2], s[3]};
+      auto max_half = [&](const float* v) -> float {  // 3-input max, 4 independent chains
+        float m4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
         for (int i = 4; i < kHalf; i += 8) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) m4[c] = fmax3(m4[c], s[i + c], s[i + 4 + c]);
+          for (int c = 0; c < 4; ++c) m4[c] = fmax3(m4[c], v[i + c], v[i + 4 + c]);
         }
         return fmax3(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
       };
@@ -479,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the first half of S's columns
       const uint64_t scale2 = pack_f32x2(sl2, sl2);
       uint64_t l2[2] = {0ull, 0ull};  // packed partial row sums
-      auto exp_half = [&](int h) {
+      auto exp_half = [&](const float* v, int h) {
         const uint64_t negm2 = pack_f32x2(-m, -m);
 #pragma unroll
         for (int c = 0; c < kHalf; c += 32) {
@@ -487,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int e = c + 2 * i;
-            const uint64_t x2 = ffma2(pack_f32x2(s[e], s[e + 1]), scale2, negm2);
+            const uint64_t x2 = ffma2(pack_f32x2(v[e], v[e + 1]), scale2, negm2);
             const uint64_t p2 = pack_f32x2(ex2(lo_f32(x2)), ex2(hi_f32(x2)));
             l2[i & 1] = fadd2(l2[i & 1], p2);
             pk[i] = pack_half2(lo_f32(p2), hi_f32(p2));
@@ -511,16 +531,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (the two are independent, so they interleave); they are recomputed
       // only when the max grows past the threshold (always for the first
       // block, where m is -inf and these values are discarded)
-      load_half(1);
-      tmem_ld_wait();
-      mask_half(1);
-      const float mx1 = max_half();
-      load_half(0);
-      tmem_ld_wait();
+      float mx1;
+      if constexpr (kRegSplit) {
+        load_half(s_hi, 1);
+        load_half(s, 0);
+        tmem_ld_wait();
+        mask_half(s_hi, 1);
+        mask_half(s, 0);
+        mx1 = max_half(s_hi);
+      } else {
+        load_half(s, 1);
+        tmem_ld_wait();
+        mask_half(s, 1);
+        mx1 = max_half(s);
+        load_half(s, 0);
+        tmem_ld_wait();
+        mask_half(s, 0);
+      }
       if (lane == 0 && q == 0) FA_TRACE(t, j, 2);
-      mask_half(0);
-      exp_half(0);
-      const float mc = fmaxf(max_half(), mx1) * sl2;
+      exp_half(s, 0);
+      const float mc = fmaxf(max_half(s), mx1) * sl2;
       if (lane == 0 && q == 0) FA_TRACE(t, j, 3);
       const bool need = mc > m + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
@@ -548,13 +578,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         // to the same TMEM columns are not ordered among themselves)
         tmem_st_wait();
         l2[0] = l2[1] = 0ull;
-        exp_half(0);
+        exp_half(s, 0);
       }
-      load_half(1);  // columns 64..127: untouched by P and by PV
-      publish(0);
-      tmem_ld_wait();
-      mask_half(1);
-      exp_half(1);
+      if constexpr (kRegSplit) {
+        publish(0);
+        exp_half(s_hi, 1);
+      } else {
+        load_half(s, 1);  // columns 64..127: untouched by P and by PV
+        publish(0);
+        tmem_ld_wait();
+        mask_half(s, 1);
+        exp_half(s, 1);
+      }
       const uint64_t lsum = fadd2(l2[0], l2[1]);
       l += lo_f32(lsum) + hi_f32(lsum);
       if (lane == 0 && q == 0) FA_TRACE(t, j, 4);
@@ -643,6 +678,13 @@ int configure_once(int device) {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg<D, CG>::kSmemBytes);
     if (e != cudaSuccess) return int(e);
+    if (kRegSplit) {
+      // the register split's arithmetic assumes the launch register count
+      cudaFuncAttributes fa{};
+      e = cudaFuncGetAttributes(&fa, flash_attn_fwd_kernel<D, CG>);
+      if (e != cudaSuccess) return int(e);
+      if (fa.numRegs != kRegsLaunch) return int(cudaErrorInvalidConfiguration);
+    }
     done[device] = 1;
   }
   return 0;
