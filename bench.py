@@ -2,35 +2,47 @@
 """Benchmark of Sion's operator hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload NAME]
+                    [--workload NAME] [--shard]
 
-Default workload: HGEMM fp16 M=N=K=4096, A row-major, B column-major (stored
-N x K, the reference's "nt" kernel), fp32 accumulate, fp16 output, seed 1 —
-the configuration the headline metric (HGEMM/FlashAttn/SGEMM TFLOPS) is quoted
-on. Other workloads: sgemm_f32_1024, hgemm_f16_128x8192x16384_nt,
-flash_attn_fwd_f16_4x32x8192x128, hgemm_f16_16384_nt.
+Default (the suite): the headline is HGEMM fp16 M=N=K=16384 (A row-major, B
+column-major = stored N x K, fp32 accumulate, fp16 output, seed 4), sharded by
+N-column blocks over the ranks (strong scaling: N=1 computes the whole
+product, N=8 one eighth of the columns per GPU; no data-path collective). The
+optional NCCL all-gather of C over NVLink is timed after the compute as its own
+field (`allgather`) and kept out of `value`. The same JSON line carries one
+sub-record per other configuration (`configs`): SGEMM 1024^3 (FFMA roofline),
+HGEMM 4096^3 (tensor roofline), skinny HGEMM 128x8192x16384 (HBM roofline) and
+flash-attention forward 4x32x8192x128 (tensor roofline). Attention is sharded
+over (b, h) groups like the headline (strong scaling); the three smaller GEMMs
+run one copy per rank (weak scaling, said in each sub-record).
 
-A step is one operator call on one synthetic batch. Each rank runs its own
-copy of the workload (independent units, no data-path collective: weak
-scaling). Steps are timed one by one with CUDA events on the launching stream;
-between steps a 512 MiB buffer is written to flush the 126 MB L2 (outside the
-events). Workloads whose inputs are larger than the L2 also read a 256 MiB
-buffer after that write, so that the L2 holds clean lines: a streaming kernel
-would otherwise be charged the write-back of the flush buffer (measured: the
-skinny HGEMM 74 us after the write alone, 64 us after write + read). The
-reported time is the max over ranks of the mean step time.
+--workload NAME runs one workload alone (one copy per rank, or split over the
+ranks with --shard); the profiles use this form.
+
+A step is one operator call on one synthetic batch. Steps are timed one by one
+with CUDA events on the launching stream; between steps a 512 MiB buffer is
+written to flush the 126 MB L2 (outside the events). Workloads whose inputs
+are larger than the L2 also read a 256 MiB buffer after that write, so that the
+L2 holds clean lines: a streaming kernel would otherwise be charged the
+write-back of the flush buffer (measured: the skinny HGEMM 74 us after the
+write alone, 64 us after write + read). The reported time is the max over
+ranks of the mean step time.
 
 `e2e` times the same call through the C ABI with pinned HOST buffers: every
 step copies its inputs host-to-device, runs the kernel and copies its output
-device-to-host, all inside the timed region. Steps are pipelined the way a
-serving loop would run them: copy-in, compute and copy-out on three streams
-with two device buffer sets, so step k+1's inputs cross PCIe while step k
-computes and step k-1's output comes back (PCIe is full duplex). The time is
-the whole K-step loop divided by K (max over ranks).
+device-to-host, all inside the timed region. Two figures: `value` /
+`ms_per_step_pipelined` run the steps the way a serving loop would (copy-in,
+compute and copy-out on three streams with two device buffer sets, so step
+k+1's inputs cross PCIe while step k computes and step k-1's output comes back)
+and divide the loop time by K; `serial_ms_per_step` is one step with the three
+phases back to back (latency). Both are max over ranks.
 
---impl reference: the reference's host path (BASELINE: LibTorch CPU
-torch.matmul / naive fp32 softmax attention, the reference tests' comparison
-path) timed on the host cores on a bounded row sample of the same workload.
+--impl reference: the reference's host path (LibTorch CPU torch.matmul /
+naive fp32 softmax attention, the reference tests' comparison path) timed on
+the host cores on a bounded row sample of the same workload, with the same
+`config` as this arm; `ms_per_step` is the sample's time scaled to the whole
+workload. Under torchrun every rank times its own shard with its share of the
+host cores, and `value` is the sum over ranks.
 """
 from __future__ import annotations
 
@@ -51,7 +63,6 @@ import torch.distributed as dist  # noqa: E402
 
 from sion_b200 import workloads as W  # noqa: E402
 
-DEFAULT_WORKLOAD = W.HGEMM_4096.name
 METRIC = "HGEMM/FlashAttn/SGEMM TFLOPS per B200 and % of peak; 1/2/4/8-GPU aggregate"
 L2_FLUSH_BYTES = 512 << 20
 L2_CLEAN_BYTES = 256 << 20
@@ -77,6 +88,13 @@ class L2Flush:
         self.w.fill_(float(i))
         if self.r is not None:
             torch.sum(self.r, dim=0, out=self.acc)
+
+    @staticmethod
+    def describe(clean: bool) -> str:
+        if not clean:
+            return "flushed between steps (512 MiB write outside the timed events)"
+        return ("inputs larger than L2; flushed between steps (512 MiB write, then 256 MiB "
+                "read so the L2 holds clean lines, outside the timed events)")
 
     @property
     def description(self) -> str:
@@ -431,6 +449,31 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def e2e_serial(runner, steps, world):
+    """Latency (ms, max over ranks) of one end-to-end step with copy-in,
+    compute and copy-out back to back on one stream (mean of `steps`)."""
+    if hasattr(runner, "_e2e_sets") and not hasattr(runner, "d_in"):
+        runner._e2e_sets()
+    s = torch.cuda.Stream()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for k in range(steps + 1):
+        barrier(world)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(s):
+            t0.record(s)
+            for d, h in zip(runner.d_in[0], runner.h_in):
+                d.copy_(h, non_blocking=True)
+            runner.compute(0)
+            for h, d in zip(runner.h_out, runner.d_out[0]):
+                h.copy_(d, non_blocking=True)
+            t1.record(s)
+        torch.cuda.synchronize()
+        if k:  # the first pass is a warm-up
+            times.append(t0.elapsed_time(t1))
+    return max_over_ranks(statistics.mean(times), world)
+
+
 def reference_gpu_timing(cfg, steps: int, warmup: int):
     """Time the reference's own kernels (oracle/_ref, built from the unmodified
     reference sources for sm_100a) on this workload, same protocol as our arm
@@ -441,7 +484,7 @@ def reference_gpu_timing(cfg, steps: int, warmup: int):
         return None
     if not (ref.available() and torch.cuda.is_available()):
         return None
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", torch.cuda.current_device())
     if isinstance(cfg, W.AttnConfig) and (cfg.backward or cfg.causal):
         return {"unavailable": "the reference has no backward or masked attention kernel"}
     if isinstance(cfg, W.AttnConfig):
@@ -470,76 +513,53 @@ def reference_gpu_timing(cfg, steps: int, warmup: int):
         times.append(s.elapsed_time(e))
     ms = statistics.mean(times)
     return {"value": cfg.flops / (ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": ms,
+            "n_gpus": 1,
             "what": "the reference's own kernels (fp16-accumulate HGEMM/attention, SIMT "
-                    "SGEMM) built unmodified for sm_100a, timed on the same B200"}
+                    "SGEMM) built unmodified for sm_100a, timed on one B200 of the same box"}
 
 
-def run_reference(args, world, rank):
-    if rank != 0:
-        return 0
-    cfg = W.CONFIGS[args.workload]
-    torch.set_num_threads(os.cpu_count() or 1)
-    vals = []
-    for _ in range(args.warmup):
-        cpu_sample(cfg, budget_s=1.0)
-    desc, threads = "", 1
-    for _ in range(args.steps):
-        v, threads, desc = cpu_sample(cfg, budget_s=max(2.0, 20.0 / max(args.steps, 1)))
-        vals.append(v)
-    value = statistics.mean(vals)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded torch CPU generator)",
-        "config": {"workload": cfg.name, "parallelism": "host cores"},
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
-                         "sample": desc},
-        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    try:
-        line["reference_gpu"] = reference_gpu_timing(cfg, max(args.steps, 5), args.warmup)
-    except Exception as e:  # the comparator is informative only
-        line["reference_gpu"] = {"unavailable": str(e)[:200]}
-    print(json.dumps(line), flush=True)
-    return 0
+HEADLINE = W.HGEMM_16384.name
+# (workload, split over the ranks?) of the sub-records, in the order printed
+SUITE = [(W.SGEMM_1024.name, False), (W.HGEMM_4096.name, False),
+         (W.HGEMM_SKINNY.name, False), (W.FA_8192.name, True)]
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(W.CONFIGS))
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--shard", action="store_true",
-                    help="strong scaling: split one workload over the ranks (GEMM N-column "
-                         "blocks, attention (b, h) groups) instead of one copy per rank")
-    args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
+def config_dict(cfg, world: int, shard: bool, l2: str | None = None) -> dict:
+    if shard:
+        how = ("N-column blocks of C" if isinstance(cfg, W.GemmConfig) else "(b, h) groups")
+        par = f"shards x{world} ({how}, no data-path collective)"
+    else:
+        par = f"replicas x{world} (one independent copy per rank)"
+    conf = {"workload": cfg.name, "parallelism": par}
+    if l2:
+        conf["l2"] = l2
+    if isinstance(cfg, W.GemmConfig):
+        conf.update({"M": cfg.M, "N": cfg.N, "K": cfg.K, "b_layout": cfg.b_layout,
+                     "seed": cfg.seed})
+    else:
+        conf.update({"B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D, "seed": cfg.seed,
+                     "causal": cfg.causal, "backward": cfg.backward})
+    return conf
 
-    world, rank, local = init_dist() if args.impl == "ours" else (
-        int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
-    if args.impl == "reference":
-        return run_reference(args, world, rank)
 
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    runner = make_runner(args.workload, device, rank if args.shard else None, world)
-    full_cfg = W.CONFIGS[args.workload]
+def _dtype(cfg) -> str:
+    return "f32" if getattr(cfg, "dtype", "f16") == "f32" else "f16 (fp32 accumulate)"
+
+
+def measure(name: str, shard: bool, args, world: int, rank: int, local: int, device,
+            cpu_budget: float, want_cpu: bool = True):
+    """One workload: device-timed steps, e2e (pipelined and serial), roofline,
+    clocks and (rank 0, N=1) the CPU host-path sample. Returns (record, runner)."""
+    runner = make_runner(name, device, rank if shard else None, world)
+    full_cfg = W.CONFIGS[name]
     flush = L2Flush(device, clean=full_cfg.io_bytes > L2_BYTES)
     stream = torch.cuda.current_stream()
-
     for _ in range(args.warmup):
         runner.step()
     torch.cuda.synchronize()
-
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    sampler = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    sampler = ClockSampler(local)
     barrier(world)
     torch.cuda.synchronize()
     with sampler:
@@ -556,67 +576,223 @@ def main():
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     mean_ms = statistics.mean(step_ms)
     ms = max_over_ranks(mean_ms, world)
+    del flush
 
     bound, work = runner.algorithmic()
-    job_flops = full_cfg.flops if args.shard else world * full_cfg.flops
+    job_flops = full_cfg.flops if shard else world * full_cfg.flops
     value = job_flops / (ms * 1e-3) / 1e12
 
-    # e2e through the C ABI with host buffers, steps pipelined over three streams
     e2e_ms = e2e_pipeline(runner, args.steps, world)
-    e2e_val = job_flops / (e2e_ms * 1e-3) / 1e12
+    serial_ms = e2e_serial(runner, max(2, min(args.steps, 5)), world)
 
     peaks = _peaks()
+    # the roofline is this rank's dominant kernel: its own work over its own time
     if bound == "hbm":
-        achieved = work / (mean_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
-                "unit": "GB/s"}
+        roof = {"bound": "hbm", "achieved": work / (mean_ms * 1e-3) / 1e9,
+                "peak": peaks["hbm_gbs"], "unit": "GB/s"}
     elif bound == "ffma":
-        ffma_peak = 148 * 128 * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12
-        achieved = work / (mean_ms * 1e-3) / 1e12
-        roof = {"bound": "ffma", "achieved": achieved, "peak": ffma_peak, "unit": "TFLOP/s"}
+        roof = {"bound": "ffma", "achieved": work / (mean_ms * 1e-3) / 1e12,
+                "peak": 148 * 128 * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12, "unit": "TFLOP/s"}
     else:
-        achieved = work / (mean_ms * 1e-3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["tflops"],
-                "unit": "TFLOP/s"}
+        roof = {"bound": "tensor", "achieved": work / (mean_ms * 1e-3) / 1e12,
+                "peak": peaks["tflops"], "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["peak_source"] = peaks["source"] + (" (148 SM x 128 FFMA x 2 x max clock)"
-                                             if bound == "ffma" else "")
-    roof["traffic"] = _ncu_traffic(runner.cfg.name)
+                                             if bound == "ffma" else " (burst)")
+    tr = _ncu_traffic(full_cfg.name)
+    roof["traffic"] = None if tr is None else tr * runner.work_fraction
+    if tr is not None and runner.work_fraction != 1.0:
+        roof["traffic_note"] = "full-workload capture scaled by this rank's share of the work"
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if want_cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
-        v, threads, desc = cpu_sample(runner.cfg, budget_s=10.0)
+        v, threads, desc = cpu_sample(runner.cfg, budget_s=cpu_budget)
         cpu = {"value": v, "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": desc}
 
-    clocks = sampler.summary()
+    rec = {
+        "value": value, "unit": "TFLOPS", "ms_per_step": ms,
+        "scaling": "strong" if shard else "weak", "dtype": _dtype(full_cfg),
+        "config": config_dict(full_cfg, world, shard, runner_l2(full_cfg)),
+        "frac_of_peak": None if bound == "hbm" else value / world / roof["peak"],
+        "roofline": roof, "cpu_baseline": cpu,
+        "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+                "ms_per_step_pipelined": e2e_ms, "serial_ms_per_step": serial_ms,
+                "serial_value": job_flops / (serial_ms * 1e-3) / 1e12,
+                "h2d_bytes_per_step": runner.h2d_bytes, "d2h_bytes_per_step": runner.d2h_bytes,
+                "pipeline": "copy-in / compute / copy-out streams, 2 device buffer sets"},
+        "gpu_launches": args.steps * runner.launches_per_step,
+        "clocks": sampler.summary(), "wall_s_timed": t_wall,
+        "step_ms_min": min(step_ms), "step_ms_median": statistics.median(step_ms),
+    }
+    return rec, runner
+
+
+def runner_l2(cfg) -> str:
+    return L2Flush.describe(cfg.io_bytes > L2_BYTES)
+
+
+def allgather_timing(runner, world: int, iters: int = 5):
+    """NCCL all-gather of every rank's C column block (the optional
+    reassembly of C over NVLink), timed alone after the compute. Blocks are
+    gathered as [rank][M][N/ranks] (equal widths); GB/s counts the bytes each
+    rank receives."""
+    if world == 1:
+        return None
+    block = runner.d_out[0][0] if hasattr(runner, "d_out") else runner.dC
+    out = torch.empty((world,) + tuple(block.shape), dtype=block.dtype, device=block.device)
+    for _ in range(2):
+        dist.all_gather_into_tensor(out, block.contiguous())
+    torch.cuda.synchronize()
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(iters):
+        dist.all_gather_into_tensor(out, block)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(t0.elapsed_time(t1) / iters, world)
+    recv = block.numel() * block.element_size() * (world - 1)
+    return {"ms": ms, "bytes_received_per_rank": recv,
+            "gbs_per_rank": recv / (ms * 1e-3) / 1e9,
+            "what": "NCCL all_gather_into_tensor of the C column blocks over NVLink, "
+                    "timed separately; not part of value"}
+
+
+def run_reference(args, world, rank):
+    """The reference's host path on this arm's workload. Under torchrun every
+    rank times its own shard with cores / world threads at the same time, and
+    the values add up (gloo); rank 0 prints."""
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("gloo")
+    cores = os.cpu_count() or 1
+    threads = max(1, cores // world)
+    torch.set_num_threads(threads)
+    names = [args.workload] if args.workload else [HEADLINE] + [n for n, _ in SUITE]
+    shard_of = {HEADLINE: True, **dict(SUITE)}
+    recs = []
+    for name in names:
+        full = W.CONFIGS[name]
+        shard = args.shard if args.workload else shard_of[name]
+        cfg = full
+        if shard and world > 1:
+            if isinstance(full, W.GemmConfig):
+                from sion_b200.shard import gemm_column_shard
+                n0, n1 = gemm_column_shard(full.N, world, rank)
+                cfg = W.GemmConfig(full.name, full.M, n1 - n0, full.K, full.dtype,
+                                   full.b_layout, full.dist, full.std, full.seed)
+            else:
+                from sion_b200.shard import attention_shard
+                s0, s1 = attention_shard(full.B, full.H, world, rank)
+                cfg = W.AttnConfig(full.name, 1, s1 - s0, full.S, full.D, full.seed,
+                                   full.causal, full.backward)
+        budget = 20.0 / max(args.steps, 1) if name == names[0] else 4.0 / max(args.steps, 1)
+        for _ in range(min(args.warmup, 3)):
+            cpu_sample(cfg, budget_s=0.5)
+        vals, desc = [], ""
+        for _ in range(args.steps):
+            v, _t, desc = cpu_sample(cfg, budget_s=max(0.5, budget))
+            vals.append(v)
+        mine = statistics.mean(vals)
+        total = mine
+        if world > 1:
+            # every rank ran its own shard (or, for replicated workloads, its own
+            # copy, as each rank of our arm does) on its share of the host cores
+            t = torch.tensor([mine], dtype=torch.float64)
+            dist.all_reduce(t)
+            total = float(t.item())
+        job_flops = full.flops if shard else world * full.flops
+        ms = job_flops / (total * 1e12) * 1e3
+        l2 = runner_l2(full)
+        rec = {"value": total, "unit": "TFLOPS", "ms_per_step": ms,
+               "ms_per_step_how": "host sample's throughput scaled to the whole workload",
+               "scaling": "strong" if shard else "weak", "dtype": "f32",
+               "config": config_dict(full, world, shard, l2),
+               "cpu_baseline": {"value": total, "unit": "TFLOPS", "cores": threads * world,
+                                "kind": "port", "sample": desc +
+                                (f"; {world} ranks x {threads} threads, each on its own shard"
+                                 if world > 1 else "")},
+               "e2e": {"value": total, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                       "d2h_bytes_per_step": 0}}
+        recs.append(rec)
+    if rank != 0:
+        dist.destroy_process_group()
+        return 0
+    head = recs[0]
+    line = {"impl": "reference", "metric": METRIC, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
+            "data": "synthetic (seeded torch CPU generator)", **head}
+    if len(recs) > 1:
+        line["configs"] = {r["config"]["workload"]: r for r in recs[1:]}
+    try:
+        line["reference_gpu"] = reference_gpu_timing(W.CONFIGS[names[0]], 5, args.warmup)
+    except Exception as e:  # the comparator is informative only
+        line["reference_gpu"] = {"unavailable": str(e)[:200]}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default=None, choices=sorted(W.CONFIGS),
+                    help="one workload alone (default: the suite, headline HGEMM 16384^3)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-suite", action="store_true",
+                    help="headline only (skip the sub-records of the other configs)")
+    ap.add_argument("--shard", action="store_true",
+                    help="with --workload: split it over the ranks (GEMM N-column blocks, "
+                         "attention (b, h) groups) instead of one copy per rank")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference(args, world, rank)
+
+    world, rank, local = init_dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    if args.workload:
+        head_name, head_shard, subs = args.workload, args.shard, []
+    else:
+        head_name, head_shard = HEADLINE, True
+        subs = [] if args.no_suite else SUITE
+
+    rec, runner = measure(head_name, head_shard, args, world, rank, local, device,
+                          cpu_budget=10.0)
+    launches = rec["gpu_launches"]
+    ag = allgather_timing(runner, world) if (head_shard and isinstance(
+        W.CONFIGS[head_name], W.GemmConfig)) else None
+    del runner
+    torch.cuda.empty_cache()
+    sub_recs = {}
+    for name, shard in subs:
+        r, run = measure(name, shard, args, world, rank, local, device, cpu_budget=5.0)
+        launches += r["gpu_launches"]
+        sub_recs[name] = r
+        del run
+        torch.cuda.empty_cache()
+
     if rank == 0:
-        cfg = full_cfg
-        par = (f"shards x{world} (N-column / (b,h) blocks, no collective)" if args.shard
-               else f"replicas x{world} (independent units)")
-        conf = {"workload": cfg.name, "parallelism": par,
-                "l2": flush.description}
-        if isinstance(cfg, W.GemmConfig):
-            conf.update({"M": cfg.M, "N": cfg.N, "K": cfg.K, "b_layout": cfg.b_layout})
-        else:
-            conf.update({"B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D})
-        line = {
-            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong" if args.shard else "weak",
-            "vs_baseline": None,
-            "dtype": "f32" if getattr(cfg, "dtype", "f16") == "f32" else "f16 (fp32 accumulate)",
-            "data": "synthetic (seeded torch CPU generator)", "config": conf,
-            "frac_of_peak": value / world / (roof["peak"] if bound != "hbm" else 1) if bound != "hbm" else None,
-            "roofline": roof, "cpu_baseline": cpu,
-            "e2e": {"value": e2e_val, "unit": "TFLOPS", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": runner.h2d_bytes,
-                    "d2h_bytes_per_step": runner.d2h_bytes,
-                    "pipeline": "copy-in / compute / copy-out streams, 2 device buffer sets"},
-            "gpu_launches": args.steps * runner.launches_per_step,
-            "clocks": clocks, "wall_s_timed": t_wall,
-            "step_ms_min": min(step_ms), "step_ms_median": statistics.median(step_ms),
-        }
+        line = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "vs_baseline": None,
+                "data": "synthetic (seeded torch CPU generator)", **rec}
+        line["gpu_launches"] = launches
+        line["gpu_launches_note"] = ("this repository's kernels launched in the timed device "
+                                     "regions of the headline and every sub-record")
+        if ag is not None:
+            line["allgather"] = ag
+        if sub_recs:
+            line["configs"] = sub_recs
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

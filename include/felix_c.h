@@ -75,8 +75,11 @@ int felix_sgemm_workspace_size(uint32_t M, uint32_t N, uint32_t K, int split_k,
  *   - size: 16 MiB of partial tiles + 16 KiB of counters, held by every GPU
  *     that loads the library until the process exits;
  *   - split_k = 0 picks the largest automatic split whose partials fit;
- *     an explicit split_k needing more (tiles x split_k > 256, tiles =
- *     ceil(M/128) * ceil(N/128)) is rejected with FELIX_API_ERROR;
+ *     an explicit split_k > 1 with tiles x split_k > 256 (tiles =
+ *     ceil(M/128) * ceil(N/128); checked on the requested split_k, before
+ *     it is clamped to ceil(K/16)) is rejected with FELIX_API_ERROR;
+ *   - it never falls back to an allocated workspace: a scratch that does not
+ *     fit is an FELIX_API_ERROR, not a cudaMalloc;
  *   - the first call on a device looks up the scratch's device address
  *     (cudaGetSymbolAddress) for that device; make that first call before any
  *     stream capture;

@@ -8,7 +8,7 @@
 # flashinfer package is used (CUTLASS_INC overrides).
 set -euo pipefail
 HERE="$(cd "$(dirname "$0")" && pwd)"
-REF="${REF:-/root/reference}"
+REF="${REF:?set REF to the reference checkout (the directory holding src/felix)}"
 OUT="$HERE/_ref"
 CUTLASS_INC="${CUTLASS_INC:-$(python -c 'import os, flashinfer; print(os.path.join(os.path.dirname(flashinfer.__file__), "data", "cutlass", "include"))' 2>/dev/null || true)}"
 NVCC="${CUDA_HOME:-/usr/local/cuda}/bin/nvcc"

@@ -1,6 +1,8 @@
 // Internal host-side interfaces shared by the kernel translation units and the
 // C-ABI layer (felix_c.cu). Nothing here is exported.
 #pragma once
+#include <atomic>
+#include <mutex>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -25,6 +27,28 @@ struct DeviceInfo {
   int num_sms;
   int max_smem_optin;
   unsigned* status_word;  // device address of the watchdog word
+};
+
+// One-time, per-device set-up (kernel attributes and the like), safe to call
+// from several host threads: the first caller on a device runs `setup`
+// (returning 0 on success) under a lock; later calls see the flag without
+// locking. A failed set-up is retried on the next call.
+class PerDeviceOnce {
+ public:
+  template <class F>
+  int run(int device, F&& setup) {
+    if (device < 0 || device >= 64) return -1;
+    if (done_[device].load(std::memory_order_acquire)) return 0;
+    std::lock_guard<std::mutex> lk(mu_);
+    if (done_[device].load(std::memory_order_relaxed)) return 0;
+    const int rc = setup();
+    if (rc == 0) done_[device].store(true, std::memory_order_release);
+    return rc;
+  }
+
+ private:
+  std::mutex mu_;
+  std::atomic<bool> done_[64] = {};
 };
 
 // Per-device facts for the current device (initialised once per device).
@@ -88,6 +112,7 @@ struct SgemmOptions {
   int split_k = 0;             // 0 = auto, 1 = none, n = n-way
   bool allow_stream_k = true;  // auto may pick stream-K (workspace grows with the SM count)
   bool allow_tma = true;       // TMA-fed main loop when rows are 16-byte aligned
+  bool forbid_alloc = false;   // never fall back to the library workspace (allocation-free callers)
 };
 size_t sgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions& o,
                              int num_sms);

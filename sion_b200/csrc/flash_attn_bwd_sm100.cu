@@ -579,16 +579,12 @@ using namespace felix_sm100::attn_bwd;
 namespace {
 template <int D>
 int configure_bwd_pipe(int device) {
-  static int done[64] = {0};
-  if (device < 0 || device >= 64) return -1;
-  if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(pipe::flash_attn_bwd_pipe_kernel<D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         pipe::PCfg<D>::kSmemBytes);
-    if (e != cudaSuccess) return int(e);
-    done[device] = 1;
-  }
-  return 0;
+  static PerDeviceOnce once;
+  return once.run(device, [] {
+    return int(cudaFuncSetAttribute(pipe::flash_attn_bwd_pipe_kernel<D>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    pipe::PCfg<D>::kSmemBytes));
+  });
 }
 
 }  // namespace

@@ -26,6 +26,7 @@
 // Online softmax in the log2 domain with packed fp32x2 arithmetic; O and l are
 // rescaled only when the row maximum grows by more than 8 (P then stays below
 // 2^8, safe in fp16), and O is normalised once at the end.
+#include <cstdio>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -671,9 +672,8 @@ int encode_qkv(CUtensorMap* map, const void* base, uint32_t BH, uint32_t S, uint
 
 template <int D, int CG>
 int configure_once(int device) {
-  static int done[64] = {0};
-  if (device < 0 || device >= 64) return -1;
-  if (!done[device]) {
+  static PerDeviceOnce once;
+  return once.run(device, [] {
     cudaError_t e = cudaFuncSetAttribute(flash_attn_fwd_kernel<D, CG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg<D, CG>::kSmemBytes);
@@ -683,11 +683,24 @@ int configure_once(int device) {
       cudaFuncAttributes fa{};
       e = cudaFuncGetAttributes(&fa, flash_attn_fwd_kernel<D, CG>);
       if (e != cudaSuccess) return int(e);
-      if (fa.numRegs != kRegsLaunch) return int(cudaErrorInvalidConfiguration);
+      if (fa.numRegs != kRegsLaunch) {
+        char msg[160];
+        std::snprintf(msg, sizeof msg,
+                      "flash_attn: the kernel was compiled with %d registers per thread, but its "
+                      "setmaxnreg split assumes %d (rebuild with FELIX_FA_REGSPLIT=0)",
+                      fa.numRegs, kRegsLaunch);
+        api_error(msg, cudaErrorInvalidConfiguration);
+        return -2;
+      }
     }
-    done[device] = 1;
-  }
-  return 0;
+    return 0;
+  });
+}
+
+FelixCode configure_error(int rc) {
+  if (rc == -2) return FelixCode{FELIX_API_ERROR, cudaErrorInvalidConfiguration};  // message set
+  return api_error("flash_attn: kernel set-up (cudaFuncSetAttribute) failed",
+                   rc > 0 ? cudaError_t(rc) : cudaErrorInvalidDevice);
 }
 
 template <int D, int CG>
@@ -751,13 +764,13 @@ FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, _
   int rc;
   cudaError_t e;
   if (head_dim == 128 && cg == 2) {
-    if ((rc = configure_once<128, 2>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    if ((rc = configure_once<128, 2>(dev->ordinal))) return configure_error(rc);
     e = launch<128, 2>(groups, tq, tk, tv, p, stream);
   } else if (head_dim == 128) {
-    if ((rc = configure_once<128, 1>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    if ((rc = configure_once<128, 1>(dev->ordinal))) return configure_error(rc);
     e = launch<128, 1>(groups, tq, tk, tv, p, stream);
   } else {
-    if ((rc = configure_once<64, 1>(dev->ordinal))) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    if ((rc = configure_once<64, 1>(dev->ordinal))) return configure_error(rc);
     e = launch<64, 1>(groups, tq, tk, tv, p, stream);
   }
   if (e == cudaSuccess) e = cudaGetLastError();

@@ -693,16 +693,12 @@ namespace {
 
 template <int BN, int CG = 1, int SUB = (CG == 2 ? 2 : 1)>
 int configure_once(int device) {
-  static int done[64] = {0};
-  if (device < 0 || device >= 64) return -1;
-  if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(felix_sm100::hgemm::hgemm_persistent_kernel<BN, CG, SUB>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg<BN, CG, SUB>::kSmemBytes);
-    if (e != cudaSuccess) return int(e);
-    done[device] = 1;
-  }
-  return 0;
+  static PerDeviceOnce once;
+  return once.run(device, [] {
+    return int(cudaFuncSetAttribute(felix_sm100::hgemm::hgemm_persistent_kernel<BN, CG, SUB>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg<BN, CG, SUB>::kSmemBytes));
+  });
 }
 
 struct Plan {

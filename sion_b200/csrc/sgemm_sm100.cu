@@ -668,18 +668,18 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
     if (encode_tmap_2d_f32(&tmA, A, K, M, uint64_t(K) * 4, uint32_t(ap), BM) ||
         encode_tmap_2d_f32(&tmB, B, N, K, uint64_t(N) * 4, BN, kTmaBk))
       return api_error("sgemm: cuTensorMapEncodeTiled failed");
-    static int configured[64] = {0};
-    if (dev->ordinal < 0 || dev->ordinal >= 64) return api_error("sgemm: device ordinal");
-    if (!configured[dev->ordinal]) {
+    static PerDeviceOnce once;
+    const int rc = once.run(dev->ordinal, [] {
       cudaError_t e = cudaFuncSetAttribute(sgemm_kernel<true, true, 32>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            TmaTile<32>::kSmem);
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(sgemm_kernel<true, true, 36>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<36>::kSmem);
-      if (e != cudaSuccess) return FelixCode{FELIX_API_ERROR, e};
-      configured[dev->ordinal] = 1;
-    }
+      return int(e);
+    });
+    if (rc < 0) return api_error("sgemm: device ordinal");
+    if (rc > 0) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
   }
   auto launch = [&](dim3 grid) -> FelixCode {
     constexpr size_t kRegSmem = size_t(2) * BK * (BM + APAD) * 4 + size_t(2) * BK * BN * 4;
@@ -697,6 +697,7 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
   };
   auto attach = [&](size_t need) -> FelixCode {
     if (!workspace) {
+      if (o.forbid_alloc) return api_error("sgemm: split-K scratch missing on an allocation-free call");
       workspace = library_workspace(dev, stream, need);
       if (!workspace) return launch_error(cudaErrorMemoryAllocation, "sgemm: workspace");
     } else if (ws_bytes < need) {
@@ -767,18 +768,22 @@ FelixCode sgemm_noalloc_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, 
   o.split_k = split_k;
   o.allow_stream_k = false;  // the static scratch is sized for split-K partials
   o.allow_tma = false;
+  o.forbid_alloc = true;     // a mismatch below becomes an error, never a cudaMalloc
+  const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  constexpr uint32_t kMaxPartials = uint32_t(kNoAllocPartialBytes / (size_t(BM) * BN * sizeof(float)));
+  // The limit is checked on the split the caller asked for, before any clamping.
+  if (split_k > 1 && uint64_t(tiles) * uint64_t(split_k) > kMaxPartials)
+    return api_error(
+        "sgemm_noalloc: this split_k needs more split-K scratch than the 16 MiB static "
+        "scratch holds (at most 256 partial 128x128 tiles: tiles x split_k <= 256)");
   size_t need = sgemm_workspace_bytes(M, N, K, o, dev->num_sms);
   if (need > kNoAllocScratchBytes) {
-    if (split_k > 0)
-      return api_error(
-          "sgemm_noalloc: this split_k needs more split-K scratch than the 16 MiB static "
-          "scratch holds (at most 256 partial 128x128 tiles: tiles x split_k <= 256)");
     // automatic split: the largest one whose partial tiles fit
-    const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    o.split_k = int(kNoAllocPartialBytes / (size_t(BM) * BN * sizeof(float)) / tiles);
+    o.split_k = int(kMaxPartials / tiles);
     if (o.split_k < 1) o.split_k = 1;
     need = sgemm_workspace_bytes(M, N, K, o, dev->num_sms);
   }
+  if (need > kNoAllocScratchBytes) return api_error("sgemm_noalloc: scratch size mismatch");
   void* scratch = nullptr;
   if (need > 0) {
     cudaError_t e = cudaSuccess;

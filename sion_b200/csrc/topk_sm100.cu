@@ -228,13 +228,14 @@ FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
   if (!grid_wide) {
     const int staged = slice_size <= kSmemKeys ? 1 : 0;
     const size_t smem = staged ? size_t(slice_size) * 4 : 0;
-    static bool configured[64] = {false};
-    if (!configured[dev->ordinal]) {
-      e = cudaFuncSetAttribute(select_per_slice_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               int(kSmemKeys * 4));
-      if (e != cudaSuccess) return FelixCode{FELIX_API_ERROR, e};
-      configured[dev->ordinal] = true;
-    }
+    static PerDeviceOnce once;
+    const int rc = once.run(dev->ordinal, [] {
+      return int(cudaFuncSetAttribute(select_per_slice_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(kSmemKeys * 4)));
+    });
+    if (rc < 0) return api_error("topk: device ordinal");
+    if (rc > 0) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
     select_per_slice_kernel<<<num_slices, kThreads, smem, stream>>>(data, out, slice_size, k,
                                                                     largest ? 1 : 0, staged);
   } else {

@@ -105,16 +105,66 @@ def test_hgemm_cluster_split_k(felix, nt, M, N, K):
     np.testing.assert_array_equal(out, C.cpu().numpy())
 
 
-def test_hgemm_config2_sampled_rows(felix):
-    from sion_b200.workloads import HGEMM_4096, gemm_inputs
-    A, B = gemm_inputs(HGEMM_4096)
-    C = torch.empty(4096, 4096, dtype=torch.half, device="cuda")
-    felix.hgemm(A.cuda(), B.cuda(), C, b_layout=felix.B_NK)
+def _tile_samples(n, tile, salt):
+    """One index in every `tile`-wide block of [0, n), at an offset that moves
+    from block to block (so both 128-row halves of a CTA-pair tile are hit)."""
+    return np.array([min(n - 1, t * tile + (t * salt + 3) % tile) for t in range(-(-n // tile))])
+
+
+def _full_size_check(felix, cfg, row_tile, col_tile):
+    """A full-size benchmark GEMM config through the C ABI (the automatic plan:
+    CTA pairs, stream-K tail), checked three ways: sampled rows and sampled
+    columns against the fp64 oracle (one of each in every output tile, so every
+    stream-K / fix-up tile and both halves of every CTA pair are hit), and the
+    whole output against cuBLAS with fp32 accumulation (torch.matmul) within
+    max(1e-2, 2 fp16 ulp) per element."""
+    from sion_b200.workloads import gemm_inputs
+    A, B = gemm_inputs(cfg)
+    dA, dB = A.cuda(), B.cuda()
+    C = torch.empty(cfg.M, cfg.N, dtype=torch.half, device="cuda")
+    felix.hgemm(dA, dB, C, b_layout=felix.B_NK)
     torch.cuda.synchronize()
-    rows = np.r_[0:3, 127:130, 2047, 4093:4096]
-    ref = oracle.hgemm(A[rows].numpy(), B.numpy(), True)
-    out = C.cpu().numpy()[rows].astype(np.float64)
-    assert_fp16_close(ref, out, ctx="4096 sampled rows")
+    rows = _tile_samples(cfg.M, row_tile, 53)
+    cols = _tile_samples(cfg.N, col_tile, 97)
+    ref_r = oracle.hgemm(A[rows].numpy(), B.numpy(), True)
+    assert_fp16_close(ref_r, C[torch.from_numpy(rows).cuda()].cpu().numpy().astype(np.float64),
+                      ctx=f"{cfg.name} sampled rows")
+    ref_c = oracle.hgemm(A.numpy(), B[cols].numpy(), True)
+    out_c = C[:, torch.from_numpy(cols).cuda()].cpu().numpy().astype(np.float64)
+    assert_fp16_close(ref_c, out_c, ctx=f"{cfg.name} sampled columns")
+    prev = torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    try:
+        R = torch.matmul(dA, dB.t())
+    finally:
+        torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = prev
+    del dA, dB
+    bad = 0
+    for r0 in range(0, cfg.M, 2048):  # chunks keep the fp32 temporaries small
+        r = R[r0:r0 + 2048].float()
+        d = (C[r0:r0 + 2048].float() - r).abs()
+        ulp = torch.exp2(torch.floor(torch.log2(r.abs().clamp(min=2.0 ** -14))) - 10)
+        tol = torch.clamp(2.0 * ulp, min=1e-2)
+        bad += int((d > tol).sum())
+    assert bad == 0, f"{cfg.name}: {bad} elements differ from cuBLAS by more than 2 ulp"
+    # a second call gives identical bits (deterministic stream-K fix-up)
+    C2 = torch.empty_like(C)
+    felix.hgemm(A.cuda(), B.cuda(), C2, b_layout=felix.B_NK)
+    torch.cuda.synchronize()
+    assert torch.equal(C, C2)
+
+
+def test_hgemm_config2_full_size(felix):
+    # benchmark config 2: 4096^3 nt, U(-1, 1), seed 1; every 128 x 128 tile sampled
+    from sion_b200.workloads import HGEMM_4096
+    _full_size_check(felix, HGEMM_4096, 128, 128)
+
+
+def test_hgemm_config5_full_size(felix):
+    # benchmark config 5: 16384^3 nt, U(-1, 1), seed 4; one row in every
+    # 256-row pair tile and one column in every 256-column tile
+    from sion_b200.workloads import HGEMM_16384
+    _full_size_check(felix, HGEMM_16384, 256, 256)
 
 
 def test_hgemm_k_zero(felix):
