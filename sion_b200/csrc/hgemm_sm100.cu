@@ -27,6 +27,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstdlib>
 
 #include "felix_internal.h"
 #include "sm100_ptx.cuh"
@@ -81,6 +82,7 @@ struct Params {
   uint32_t tma_store;     // 1: epilogue writes C through smem + TMA (beta == 0)
   uint32_t ksplit2;       // 1: 2-CTA clusters split each tile's K in halves (see below)
   uint32_t pair;          // 1: CTA pairs (cta_group::2); units and slots are per pair
+  uint32_t kstagger;      // cluster split-K: rotate each CTA's k-block order
   float* ws_partials;     // [gridDim.x][2] slots of BM*BN fp32, see partial_index()
   unsigned* ws_counters;  // [sk_tiles], zero between launches
   unsigned* status;       // watchdog word
@@ -315,7 +317,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t tm, tn;
         tile_coords(p, u.tile, tm, tn);
         const int m0 = int(tm * BM * CG + rank * BM), n0 = int(tn * BN + rank * C_::kBRows);
-        for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
+        // k-block order: cluster split-K CTAs each start at a different point
+        // of their K range (rotated), so at any moment the CTAs stream from
+        // addresses spread across B instead of the same column of every row
+        // (the MMA order does not depend on which k-block a stage holds)
+        const uint32_t klen = u.kb1 - u.kb0;
+        const uint32_t krot =
+            (p.ksplit2 && p.kstagger && klen) ? uint32_t((uint64_t(blockIdx.x >> 1) * klen) /
+                                                         (gridDim.x >> 1)) % klen
+                                              : 0u;
+        for (uint32_t kq = u.kb0; kq < u.kb1; ++kq) {
+          const uint32_t kb = u.kb0 + (kq - u.kb0 + krot) % (klen ? klen : 1u);
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kWdProducerEmpty)) {
             ok = false;
             break;
@@ -911,6 +923,13 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   p.group_m = 16;
   p.status = dev->status_word;
   p.ksplit2 = pl.ksplit2 ? 1u : 0u;
+  {
+    static const int stag = [] {
+      const char* e = std::getenv("FELIX_HGEMM_KSTAGGER");
+      return e ? std::atoi(e) : 1;
+    }();
+    p.kstagger = stag ? 1u : 0u;
+  }
   p.pair = pl.pair ? 1u : 0u;
   if (pl.sk_tiles) {
     if (uint64_t(pl.sk_tiles) * (pl.pair ? 2 : 1) > kWsMaxCounters)
