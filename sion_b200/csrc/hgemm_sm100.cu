@@ -868,7 +868,10 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   }
   // 128-wide single-CTA tiles also take stages of two 64-deep k-blocks (32 KB
   // requests) when the view is exact: plan in 128-deep k-blocks
-  if (!pl.pair && pl.bn == 128 && sub2_ok && K >= 128) {
+#ifndef FELIX_HGEMM_SKINNY_SUB1
+#define FELIX_HGEMM_SKINNY_SUB1 0
+#endif
+  if (!pl.pair && pl.bn == 128 && sub2_ok && K >= 128 && !(FELIX_HGEMM_SKINNY_SUB1 && ksplit2)) {
     pl = plan_for(M, N, (K + 1) / 2, 128, o, dev->num_sms);
     pl.sub = 2;
   }
