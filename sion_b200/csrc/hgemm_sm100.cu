@@ -16,8 +16,10 @@
 //   * CTA tile 128 x BN (BN = 256, 128 or 64), K step 64 (one 128-byte swizzle row),
 //     UMMA 128 x BN x 16; two TMEM accumulators so the epilogue of tile i
 //     overlaps the main loop of tile i+1.
-//   * schedule: whole tiles round-robin over the persistent CTAs ("data-parallel"
-//     waves); the tiles of an incomplete last wave are spread evenly over all
+//   * schedule: whole tiles over the persistent CTAs ("data-parallel" waves),
+//     in a grouped raster; with four or more waves the tiles are handed out at
+//     run time from a global counter (TileQueue), so the CTAs running together
+//     always share operand panels in L2; the tiles of an incomplete last wave are spread evenly over all
 //     CTAs by k-iterations (stream-K). A stream-K tile with several contributors
 //     is finished by whichever contributor arrives last (atomic ticket): every
 //     contributor writes its fp32 partial to the workspace, the last one sums all
@@ -27,7 +29,6 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
-#include <cstdlib>
 
 #include "felix_internal.h"
 #include "sm100_ptx.cuh"
@@ -82,7 +83,8 @@ struct Params {
   uint32_t tma_store;     // 1: epilogue writes C through smem + TMA (beta == 0)
   uint32_t ksplit2;       // 1: 2-CTA clusters split each tile's K in halves (see below)
   uint32_t pair;          // 1: CTA pairs (cta_group::2); units and slots are per pair
-  uint32_t kstagger;      // cluster split-K: rotate each CTA's k-block order
+  uint32_t dyn;           // 1: whole tiles are handed out at run time (see TileQueue)
+  unsigned* ws_dyn;       // [0] next whole tile, [1] finished leader CTAs; zero between launches
   float* ws_partials;     // [gridDim.x][2] slots of BM*BN fp32, see partial_index()
   unsigned* ws_counters;  // [sk_tiles], zero between launches
   unsigned* status;       // watchdog word
@@ -105,6 +107,7 @@ struct Sched {
   uint32_t cta, P, sk_tiles, tiles, KB;
   uint64_t I, it, end, start;
   uint32_t dp_next;
+  bool dyn;
 
   uint32_t ksplit_rank;  // cluster split-K: 0 or 1 (which half of K); 2 = unit taken
   __device__ __forceinline__ void init(const Params& p) {
@@ -119,6 +122,16 @@ struct Sched {
     end = I * (cta + 1) / P;
     it = start;
     dp_next = sk_tiles + cta;
+    dyn = p.dyn != 0;
+  }
+  // whole tile t (dynamic schedule)
+  __device__ __forceinline__ void whole(Unit& u, uint32_t t) const {
+    u.tile = t;
+    u.kb0 = 0;
+    u.kb1 = KB;
+    u.partial = false;
+    u.sk = 0;
+    u.seg = 0;
   }
   __device__ __forceinline__ bool next(Unit& u) {
     if (ksplit_rank < 2) {
@@ -148,7 +161,7 @@ struct Sched {
       it += kb1 - kb0;
       return true;
     }
-    if (dp_next < tiles) {
+    if (!dyn && dp_next < tiles) {
       u.tile = dp_next;
       u.kb0 = 0;
       u.kb1 = KB;
@@ -165,6 +178,61 @@ struct Sched {
     return static_cast<uint32_t>(((x + 1) * P - 1) / I);
   }
 };
+
+// Dynamic whole-tile schedule (Params::dyn). With a static stride the
+// persistent CTAs drift apart over many waves (16384^3: 55 waves), so the CTAs
+// running at the same time stop sharing A and B panels in L2: measured 18.9 GB
+// of DRAM reads for 1.07 GB of operands. Instead the leader CTA's producer
+// takes each next whole tile from a global counter (one atomicAdd per tile,
+// fetched one tile ahead) and hands it to every role of its CTA, and of the
+// peer CTA of a pair, through a kTq-slot queue in shared memory: tq[slot],
+// tq_full[slot] (completed by the producer's arrival; the peer's copy by a
+// remote arrival after a remote store) and the leader's tq_empty[slot] (one
+// arrival per consuming warp role, remote ones from the peer). Tiles then run
+// in the order the CTAs become free: neighbours in the grouped raster run
+// together. Each tile is still computed by one CTA (pair) in a fixed k order,
+// so results do not depend on the assignment. A tile id >= tiles ends the walk.
+constexpr uint32_t kTq = 4;
+struct TileQueue {
+  uint32_t* tq;
+  uint64_t* full;
+  uint64_t* empty;
+  uint32_t n;  // queue entries used so far
+};
+
+__device__ __forceinline__ bool tq_push(TileQueue& q, uint32_t t, bool pair,
+                                        volatile int* abort_flag, unsigned* status) {
+  const uint32_t slot = q.n % kTq, par = (q.n / kTq) & 1u;
+  if (!mbar_wait_cluster(&q.empty[slot], par ^ 1u, abort_flag, status, kWdTileQueue))
+    return false;
+  q.tq[slot] = t;
+  if (pair) {
+    st_shared_cluster_u32(mapa_shared(smem_u32(&q.tq[slot]), 1), t);
+    mbar_arrive_cluster(mapa_shared(smem_u32(&q.full[slot]), 1));
+  }
+  mbar_arrive(&q.full[slot]);
+  ++q.n;
+  return true;
+}
+
+// Waits for the next queue entry and reads it (every calling thread); the
+// caller then releases the slot once per warp with tq_release.
+__device__ __forceinline__ bool tq_pop(TileQueue& q, uint32_t& t, uint32_t& slot,
+                                       volatile int* abort_flag, unsigned* status) {
+  slot = q.n % kTq;
+  const uint32_t par = (q.n / kTq) & 1u;
+  if (!mbar_wait_cluster(&q.full[slot], par, abort_flag, status, kWdTileQueue)) return false;
+  t = reinterpret_cast<volatile uint32_t*>(q.tq)[slot];
+  ++q.n;
+  return true;
+}
+
+__device__ __forceinline__ void tq_release(TileQueue& q, uint32_t slot, uint32_t rank) {
+  if (rank == 0)
+    mbar_arrive(&q.empty[slot]);
+  else
+    mbar_arrive_cluster(mapa_shared(smem_u32(&q.empty[slot]), 0));
+}
 
 __device__ __forceinline__ void tile_coords(const Params& p, uint32_t t, uint32_t& tm,
                                             uint32_t& tn) {
@@ -254,6 +322,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* recv_buf = ring;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* bcast = tmem_slot + 2;
+  TileQueue tq{reinterpret_cast<uint32_t*>(bars + 2 * S + 17), bars + 2 * S + 9,
+               bars + 2 * S + 13, 0};
+  static_assert((2 * S + 19) * 8 <= 512, "barrier block");
 
   const uint32_t warp = threadIdx.x / 32;
   const uint32_t lane = threadIdx.x % 32;
@@ -270,6 +341,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(drain, 1);
     mbar_init(recv, 128);  // one arrival per epilogue thread of rank 1
     mbar_init(ring_free, 1);
+    for (uint32_t i = 0; i < kTq; ++i) {
+      mbar_init(&tq.full[i], 1);
+      // consumers: the leader's MMA warp and 4 epilogue warps; in a pair also
+      // the peer's producer and 4 epilogue warps
+      mbar_init(&tq.empty[i], CG == 2 ? 10 : 5);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -313,21 +390,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
           tma_load_3d(dst, map, bar, 0, y, z);
       };
-      while (ok && sc.next(u)) {
+      // dynamic schedule: the leader fetches tile ids one tile ahead and
+      // pushes them; the peer of a pair pops them
+      uint32_t ahead = 0;
+      bool have_ahead = false;
+      auto next_unit = [&](Unit& uu) -> bool {
+        if (sc.next(uu)) return true;
+        if (!sc.dyn) return false;
+        uint32_t t;
+        if (rank == 0) {
+          if (!have_ahead) ahead = sc.sk_tiles + atomicAdd(p.ws_dyn, 1u);
+          t = ahead;
+          if (!tq_push(tq, t, CG == 2, abort_flag, p.status)) return ok = false;
+          have_ahead = t < sc.tiles;
+          if (have_ahead) ahead = sc.sk_tiles + atomicAdd(p.ws_dyn, 1u);
+        } else {
+          uint32_t slot;
+          if (!tq_pop(tq, t, slot, abort_flag, p.status)) return ok = false;
+          tq_release(tq, slot, rank);
+        }
+        if (t >= sc.tiles) return false;
+        sc.whole(uu, t);
+        return true;
+      };
+      while (ok && next_unit(u)) {
         uint32_t tm, tn;
         tile_coords(p, u.tile, tm, tn);
         const int m0 = int(tm * BM * CG + rank * BM), n0 = int(tn * BN + rank * C_::kBRows);
-        // k-block order: cluster split-K CTAs each start at a different point
-        // of their K range (rotated), so at any moment the CTAs stream from
-        // addresses spread across B instead of the same column of every row
-        // (the MMA order does not depend on which k-block a stage holds)
-        const uint32_t klen = u.kb1 - u.kb0;
-        const uint32_t krot =
-            (p.ksplit2 && p.kstagger && klen) ? uint32_t((uint64_t(blockIdx.x >> 1) * klen) /
-                                                         (gridDim.x >> 1)) % klen
-                                              : 0u;
-        for (uint32_t kq = u.kb0; kq < u.kb1; ++kq) {
-          const uint32_t kb = u.kb0 + (kq - u.kb0 + krot) % (klen ? klen : 1u);
+        for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kWdProducerEmpty)) {
             ok = false;
             break;
@@ -398,7 +488,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       Unit u;
       uint32_t stage = 0, phase = 0, i = 0;
       bool ok = true;
-      while (ok && sc.next(u)) {
+      // dynamic schedule: every lane pops (the warp stays converged), lane 0
+      // releases the slot
+      auto next_unit = [&](Unit& uu) -> bool {
+        if (sc.next(uu)) return true;
+        if (!sc.dyn) return false;
+        uint32_t t, slot;
+        const bool got = tq_pop(tq, t, slot, abort_flag, p.status);
+        if (__all_sync(0xffffffffu, got) == 0) return ok = false;
+        __syncwarp();
+        if (lane == 0) tq_release(tq, slot, 0);
+        if (t >= sc.tiles) return false;
+        sc.whole(uu, t);
+        return true;
+      };
+      while (ok && next_unit(u)) {
         const uint32_t buf = i & 1u;
         if (!wait_all(&tempty[buf], ((i >> 1) & 1u) ^ 1u, kWdMmaTmemEmpty)) {
           ok = false;
@@ -479,7 +583,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     sc.init(p);
     Unit u;
     uint32_t i = 0;
-    while (sc.next(u)) {
+    auto next_unit = [&](Unit& uu) -> bool {
+      if (sc.next(uu)) return true;
+      if (!sc.dyn) return false;
+      uint32_t t, slot;
+      if (!tq_pop(tq, t, slot, abort_flag, p.status)) return false;
+      __syncwarp();
+      if (lane == 0) tq_release(tq, slot, rank);
+      if (t >= sc.tiles) return false;
+      sc.whole(uu, t);
+      return true;
+    };
+    while (next_unit(u)) {
       const uint32_t buf = i & 1u;
       if (!mbar_wait(&tfull[buf], (i >> 1) & 1u, abort_flag, p.status, kWdEpilogueTmemFull))
         break;
@@ -683,6 +798,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_sync();  // no CTA exits while its peer may still use its memory
   else
     __syncthreads();
+  if (p.dyn && rank == 0 && threadIdx.x == 0) {
+    // the last leader CTA to finish puts the tile counter back to zero (every
+    // leader has taken its final tile id before it gets here)
+    const uint32_t leaders = CG == 2 ? gridDim.x >> 1 : gridDim.x;
+    __threadfence();
+    if (atomicAdd(p.ws_dyn + 1, 1u) == leaders - 1) {
+      atomicExch(p.ws_dyn, 0u);
+      atomicExch(p.ws_dyn + 1, 0u);
+    }
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -769,6 +894,21 @@ Plan plan_for(uint32_t M, uint32_t N, uint32_t K, int bn, const HgemmOptions& o,
   return pl;
 }
 
+// Whole tiles are handed out at run time (TileQueue) when there are at least
+// four waves of them; fewer waves do not drift apart enough to matter.
+bool uses_dynamic_tiles(const Plan& pl) {
+  if (pl.ksplit2) return false;
+  return pl.grid > 0 && pl.dp_tiles >= 4u * pl.grid;
+}
+
+// Library or caller workspace a plan needs: the counter block (stream-K
+// tickets, the dynamic tile counter) plus the stream-K partial slots.
+size_t workspace_need(const Plan& pl) {
+  if (pl.sk_tiles)
+    return kWsCounterBytes + size_t(pl.grid) * 2 * (pl.pair ? 2 : 1) * BM * pl.bn * sizeof(float);
+  return uses_dynamic_tiles(pl) ? kWsCounterBytes : 0;
+}
+
 // Automatic choice of CTA pairs: large enough for at least one wave of
 // 256 x 256 tiles, and whole 64-wide k-blocks (and n-chunks for "nn") so that
 // the 32 KB 3-D loads are exact. pair_shape_ok carries the layout condition.
@@ -812,9 +952,7 @@ size_t hgemm_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, const HgemmOpti
   size_t need = 0;
   for (int pair_ok = 0; pair_ok < 2; ++pair_ok) {
     Plan pl = make_plan(M, N, K, o, num_sms, pair_ok != 0);
-    if (pl.sk_tiles == 0) continue;
-    const size_t n =
-        kWsCounterBytes + size_t(pl.grid) * 2 * (pl.pair ? 2 : 1) * BM * pl.bn * sizeof(float);
+    const size_t n = workspace_need(pl);
     need = n > need ? n : need;
   }
   return need;
@@ -923,22 +1061,22 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   p.dp_tiles = pl.dp_tiles;
   p.sk_tiles = pl.sk_tiles;
   p.sk_iters = pl.sk_iters;
-  p.group_m = 16;
+  // Grouped raster height (tiles): the CTAs running at the same time cover a
+  // group_m x (CTAs / group_m) block of tiles and share its A and B panels in
+  // L2. Measured at 16384^3 with CTA pairs (74 concurrent 256 x 256 tiles):
+  // group 2 / 4 / 8 / 16 / 32 read 19.2 / 11.4 / 9.2 / 16.8 / 32.5 GB from
+  // DRAM for 1.07 GB of operands, and 8 ran 12 % faster than 16 (the kernel is
+  // power-capped there: fewer DRAM bytes, higher clock); 8192^3: 707 vs 718 us.
+  // Single-CTA 128 x 256 tiles (148 concurrent): 16 (8192^3: 763 vs 789 us).
+  p.group_m = pl.pair ? 8u : 16u;
   p.status = dev->status_word;
   p.ksplit2 = pl.ksplit2 ? 1u : 0u;
-  {
-    static const int stag = [] {
-      const char* e = std::getenv("FELIX_HGEMM_KSTAGGER");
-      return e ? std::atoi(e) : 1;
-    }();
-    p.kstagger = stag ? 1u : 0u;
-  }
   p.pair = pl.pair ? 1u : 0u;
-  if (pl.sk_tiles) {
-    if (uint64_t(pl.sk_tiles) * (pl.pair ? 2 : 1) > kWsMaxCounters)
+  p.dyn = uses_dynamic_tiles(pl) ? 1u : 0u;
+  if (pl.sk_tiles || p.dyn) {
+    if (uint64_t(pl.sk_tiles) * (pl.pair ? 2 : 1) > kWsMaxCounters - 2)
       return api_error("hgemm: too many stream-K tiles");
-    const size_t need =
-        kWsCounterBytes + size_t(pl.grid) * 2 * (pl.pair ? 2 : 1) * BM * pl.bn * sizeof(float);
+    const size_t need = workspace_need(pl);
     if (!workspace) {
       workspace = library_workspace(dev, stream, need);
       if (!workspace) return launch_error(cudaErrorMemoryAllocation, "hgemm: workspace");
@@ -946,6 +1084,7 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
       return api_error("hgemm: workspace too small");
     }
     p.ws_counters = static_cast<unsigned*>(workspace);
+    p.ws_dyn = p.ws_counters + (kWsMaxCounters - 2);
     p.ws_partials =
         reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
   }

@@ -31,7 +31,8 @@ enum WatchdogSite : unsigned {
   kWdAttnMma = 8,
   kWdAttnSoftmax = 9,
   kWdAttnCorrection = 10,
-  kWdSmemAlign = 11,  // dynamic shared memory not 1024-byte aligned: kernel did nothing
+  kWdSmemAlign = 11,
+  kWdTileQueue = 12,  // HGEMM dynamic tile queue (producer push or consumer pop)  // dynamic shared memory not 1024-byte aligned: kernel did nothing
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -140,6 +141,47 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
+}
+
+// 4-byte store to shared memory of a CTA of the cluster (address from mapa_shared).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+// Bounded wait on a local mbarrier whose phase is completed from another CTA
+// of the cluster: acquire at cluster scope, so that data that CTA stored into
+// this CTA's shared memory before its release-arrive is visible.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort_flag, unsigned* status_word,
+                                                  unsigned site,
+                                                  unsigned long long limit_ns = kWaitLimitNs) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_cluster(a, parity)) return true;
+  uint64_t t0 = 0;
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    if ((it & 31u) == 0) {
+      if (*abort_flag) return false;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > limit_ns) {
+        *abort_flag = 1;
+        atomicCAS(status_word, 0u, site);
+        return false;
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------- TMA
