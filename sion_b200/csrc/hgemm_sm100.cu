@@ -29,6 +29,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstdlib>
 
 #include "felix_internal.h"
 #include "sm100_ptx.cuh"
@@ -59,12 +60,17 @@ template <int BN, int CG = 1, int SUB = (CG == 2 ? 2 : 1)>
 struct Cfg {
   static_assert(CG == 1 || SUB == 2, "CTA pairs load two k-blocks per stage");
   static constexpr int kBRows = BN / CG;  // B rows (N) loaded by one CTA
+  // BN = 512 (CTA pairs only): two N = 256 MMAs per k step, each CTA holding
+  // 128 B rows of each half; one accumulator (all 512 TMEM columns)
+  static constexpr int kNH = BN > 256 ? 2 : 1;        // MMA N halves
+  static constexpr int kBoxRows = kBRows / kNH;        // B rows per load box
+  static constexpr int kNBuf = 2 * BN <= 512 ? 2 : 1;  // TMEM accumulators
   static constexpr int kSub = SUB;        // 64-deep k-blocks per stage
   static constexpr int kStages = (192 * 1024) / ((BM + kBRows) * BK * 2 * kSub);
   static constexpr int kABytes = BM * BK * 2 * kSub;
   static constexpr int kBBytes = kBRows * BK * 2 * kSub;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kTmemCols = kNBuf * BN;
   // epilogue staging for TMA stores: 4 warps x 2 buffers x (32 rows x 128 B)
   static constexpr int kStagingBytes = 4 * 2 * 4096;
   // ring + staging + 1 KB alignment slack + barrier block
@@ -298,8 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmC, const Params p) {
   using C_ = Cfg<BN, CG, SUB>;
-  static_assert(CG == 1 || BN == 256, "CTA pairs use 256-wide tiles");
-  static_assert(SUB == 1 || (BK == 64 && C_::kBRows == 128), "3-D loads: 128-row boxes, BK = 64");
+  static_assert(CG == 1 || BN == 256 || BN == 512, "CTA pairs use 256- or 512-wide tiles");
+  static_assert(BN <= 256 || CG == 2, "512-wide tiles only on CTA pairs");
+  static_assert(SUB == 1 || (BK == 64 && C_::kBoxRows == 128), "3-D loads: 128-row boxes, BK = 64");
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
   constexpr int S = C_::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -429,10 +436,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             // A rows [m0, m0 + 128), k-blocks 2 kb, 2 kb + 1; B likewise, or
             // ("nn") k rows [128 kb, 128 kb + 128) of n-chunks n0 / 64, + 1
             load3d(sa, &tmA, &full[stage], m0, int(2 * kb));
-            if (p.b_mn_major)
+            if constexpr (C_::kNH == 2) {
+              // "nt" only: B rows of N half h, this CTA's 128 of them
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                load3d(sb + h * (C_::kBBytes / 2), &tmB, &full[stage],
+                       int(tn * BN + h * (BN / 2) + rank * C_::kBoxRows), int(2 * kb));
+            } else if (p.b_mn_major) {
               load3d(sb, &tmB, &full[stage], int(kb * BK * 2), n0 / 64);
-            else
+            } else {
               load3d(sb, &tmB, &full[stage], n0, int(2 * kb));
+            }
           } else {
             load2d(sa, &tmA, &full[stage], int(kb * BK), m0);
             if (p.b_mn_major) {
@@ -472,7 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto wait_all = [&](uint64_t* bar, uint32_t parity, unsigned site) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, site)) != 0;
       };
-      const uint32_t idesc = make_idesc_f16_f32(BM * CG, BN, false, p.b_mn_major != 0);
+      const uint32_t idesc =
+          make_idesc_f16_f32(BM * CG, BN / C_::kNH, false, p.b_mn_major != 0);
       // completion signals go to the barrier in every CTA of the group
       auto commit_all = [&](uint64_t* bar) {
         if constexpr (CG == 2) {
@@ -503,8 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       while (ok && next_unit(u)) {
-        const uint32_t buf = i & 1u;
-        if (!wait_all(&tempty[buf], ((i >> 1) & 1u) ^ 1u, kWdMmaTmemEmpty)) {
+        const uint32_t buf = C_::kNBuf == 2 ? (i & 1u) : 0u;
+        const uint32_t use_par = C_::kNBuf == 2 ? ((i >> 1) & 1u) : (i & 1u);
+        if (!wait_all(&tempty[buf], use_par ^ 1u, kWdMmaTmemEmpty)) {
           ok = false;
           break;
         }
@@ -539,16 +555,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // MN-major: 64-wide chunks of (BK * kSub) k-rows x 128 B
                 constexpr int kq = BK / 16;
                 aoff = (k / kq) * (BM * BK * 2) + (k % kq) * 32;
-                boff = p.b_mn_major ? k * 2048 : (k / kq) * (C_::kBRows * BK * 2) + (k % kq) * 32;
+                boff = p.b_mn_major ? k * 2048 : (k / kq) * (C_::kBoxRows * BK * 2) + (k % kq) * 32;
               } else {
                 aoff = k * 32;
                 boff = p.b_mn_major ? k * 2048 : k * 32;
               }
               const uint64_t ad = ad0 + (aoff >> 4), bd = bd0 + (boff >> 4);
-              if constexpr (CG == 2)
-                umma_f16_ss_pair(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
-              else
-                umma_f16_ss(d, ad, bd, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+#pragma unroll
+              for (int h = 0; h < C_::kNH; ++h) {
+                // N half h: its B box follows the previous one in the stage
+                const uint64_t bdh = bd + uint64_t(h * (C_::kBBytes / C_::kNH) >> 4);
+                const uint32_t dh = d + uint32_t(h * (BN / C_::kNH));
+                if constexpr (CG == 2)
+                  umma_f16_ss_pair(dh, ad, bdh, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+                else
+                  umma_f16_ss(dh, ad, bdh, idesc, (kb > u.kb0 || k > 0) ? 1u : 0u);
+              }
             }
             commit_all(&empty[stage]);
           }
@@ -595,8 +617,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     while (next_unit(u)) {
-      const uint32_t buf = i & 1u;
-      if (!mbar_wait(&tfull[buf], (i >> 1) & 1u, abort_flag, p.status, kWdEpilogueTmemFull))
+      const uint32_t buf = C_::kNBuf == 2 ? (i & 1u) : 0u;
+      const uint32_t use_par = C_::kNBuf == 2 ? ((i >> 1) & 1u) : (i & 1u);
+      if (!mbar_wait(&tfull[buf], use_par, abort_flag, p.status, kWdEpilogueTmemFull))
         break;
       tc_fence_after();
       uint32_t tm, tn;
@@ -986,6 +1009,24 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   Plan pl = make_plan(M, N, K, o, dev->num_sms, sub2_ok);
   if (pl.pair && !sub2_ok)
     return api_error("hgemm: CTA pairs need K (and N when B is K x N) multiples of 64");
+  bool wide = false;
+  {
+    static const int wide_env = [] {
+      const char* e = std::getenv("FELIX_HGEMM_WIDE");
+      return e ? std::atoi(e) : 0;
+    }();
+    const uint64_t wide_tiles = uint64_t((M + 255) / 256) * ((N + 511) / 512);
+    if (wide_env && pl.pair && !b_kn && o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 &&
+        wide_tiles >= 4u * uint64_t(dev->num_sms / 2)) {
+      pl = plan_for((M + 1) / 2, N, (K + 1) / 2, 512, o, dev->num_sms / 2);
+      pl.pair = true;
+      pl.sk_tiles = 0;
+      pl.sk_iters = 0;
+      pl.dp_tiles = pl.tiles;
+      pl.grid = pl.tiles < uint32_t(dev->num_sms / 2) ? pl.tiles : uint32_t(dev->num_sms / 2);
+      wide = true;
+    }
+  }
   // C through TMA when nothing has to be read back (beta == 0) and its rows
   // are 16-byte multiples.
   const bool tma_store = beta == 0.f && (N % 8 == 0) &&
@@ -1069,6 +1110,13 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   // power-capped there: fewer DRAM bytes, higher clock); 8192^3: 707 vs 718 us.
   // Single-CTA 128 x 256 tiles (148 concurrent): 16 (8192^3: 763 vs 789 us).
   p.group_m = pl.pair ? 8u : 16u;
+  {
+    static const int g = [] {
+      const char* e = std::getenv("FELIX_HGEMM_GROUP");
+      return e ? std::atoi(e) : 0;
+    }();
+    if (g > 0) p.group_m = uint32_t(g);
+  }
   p.status = dev->status_word;
   p.ksplit2 = pl.ksplit2 ? 1u : 0u;
   p.pair = pl.pair ? 1u : 0u;
@@ -1091,12 +1139,12 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
 
   cudaError_t e;
   if (pl.pair) {
-    if ((rc = configure_once<256, 2>(dev->ordinal)))
+    if ((rc = wide ? configure_once<512, 2>(dev->ordinal) : configure_once<256, 2>(dev->ordinal)))
       return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * pl.grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Cfg<256, 2>::kSmemBytes;
+    cfg.dynamicSmemBytes = wide ? Cfg<512, 2>::kSmemBytes : Cfg<256, 2>::kSmemBytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1105,7 +1153,8 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<256, 2>, tmA, tmB, tmC, p);
+    e = wide ? cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<512, 2>, tmA, tmB, tmC, p)
+             : cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<256, 2>, tmA, tmB, tmC, p);
     if (e != cudaSuccess) return launch_error(e, "hgemm: CTA-pair launch failed");
     return FelixCode{FELIX_SUCCESS, cudaSuccess};
   }
