@@ -13,7 +13,9 @@
 //       warp 0  TMA producer (one elected lane), multi-stage smem ring
 //       warp 1  TMEM allocator + single-thread tcgen05.mma issuer
 //       warps 2-5 epilogue: tcgen05.ld -> alpha/beta -> fp16 -> global
-//   * CTA tile 128 x BN (BN = 256, 128 or 64), K step 64 (one 128-byte swizzle row),
+//   * CTA tile 128 x BN (BN = 256, 128 or 64; CTA pairs 256 x 256 or, for many
+//     waves of "nt" tiles, 256 x 512 from two N = 256 MMAs per k step into a
+//     single TMEM accumulator), K step 64 (one 128-byte swizzle row),
 //     UMMA 128 x BN x 16; two TMEM accumulators so the epilogue of tile i
 //     overlaps the main loop of tile i+1.
 //   * schedule: whole tiles over the persistent CTAs ("data-parallel" waves),
@@ -29,7 +31,6 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
-#include <cstdlib>
 
 #include "felix_internal.h"
 #include "sm100_ptx.cuh"
@@ -1009,15 +1010,16 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   Plan pl = make_plan(M, N, K, o, dev->num_sms, sub2_ok);
   if (pl.pair && !sub2_ok)
     return api_error("hgemm: CTA pairs need K (and N when B is K x N) multiples of 64");
+  // Many waves of "nt" pair tiles: 256 x 512 tiles (two N = 256 MMAs per k
+  // step, one TMEM accumulator). Per output they read 3/4 of the operand bytes
+  // of 256 x 256 tiles; the kernel is power-capped at these sizes, so fewer
+  // bytes means a higher clock: 16384^3 5.79 -> 5.59 ms under ncu (DRAM reads
+  // 8.9 -> 7.0 GB, 1.30 -> 1.39 GHz), bench 5.67 -> 5.51 ms; 8192^3 697 -> 683 us.
   bool wide = false;
   {
-    static const int wide_env = [] {
-      const char* e = std::getenv("FELIX_HGEMM_WIDE");
-      return e ? std::atoi(e) : 0;
-    }();
     const uint64_t wide_tiles = uint64_t((M + 255) / 256) * ((N + 511) / 512);
-    if (wide_env && pl.pair && !b_kn && o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 &&
-        wide_tiles >= 4u * uint64_t(dev->num_sms / 2)) {
+    if (pl.pair && !b_kn && o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 &&
+        o.cta_pair == 0 && wide_tiles >= 4u * uint64_t(dev->num_sms / 2)) {
       pl = plan_for((M + 1) / 2, N, (K + 1) / 2, 512, o, dev->num_sms / 2);
       pl.pair = true;
       pl.sk_tiles = 0;
@@ -1109,14 +1111,8 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   // DRAM for 1.07 GB of operands, and 8 ran 12 % faster than 16 (the kernel is
   // power-capped there: fewer DRAM bytes, higher clock); 8192^3: 707 vs 718 us.
   // Single-CTA 128 x 256 tiles (148 concurrent): 16 (8192^3: 763 vs 789 us).
-  p.group_m = pl.pair ? 8u : 16u;
-  {
-    static const int g = [] {
-      const char* e = std::getenv("FELIX_HGEMM_GROUP");
-      return e ? std::atoi(e) : 0;
-    }();
-    if (g > 0) p.group_m = uint32_t(g);
-  }
+  // 256 x 512 pair tiles: 16 (16384^3: 5.51 vs 5.71 ms with 8).
+  p.group_m = wide ? 16u : (pl.pair ? 8u : 16u);
   p.status = dev->status_word;
   p.ksplit2 = pl.ksplit2 ? 1u : 0u;
   p.pair = pl.pair ? 1u : 0u;

@@ -218,3 +218,13 @@ def test_hgemm_cta_pair_stream_k(felix, nt):
 def test_hgemm_cta_pair_alpha_beta(felix):
     ref, out = _run(felix, 384, 512, 256, nt=True, alpha=0.5, beta=-0.75, cta_pair=2)
     assert_fp16_close(ref, out, ctx="CTA pair alpha/beta")
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 10240, 512), (4000, 10000, 1024)])
+def test_hgemm_wide_pair_tiles(felix, M, N, K):
+    # four or more waves of 256 x 512 "nt" pair tiles: two N = 256 MMAs per k
+    # step into one TMEM accumulator, tiles handed out at run time; ragged M
+    # and N clip at the tensor-map edges
+    from sion_b200.workloads import GemmConfig
+    cfg = GemmConfig(f"wide_{M}x{N}x{K}", M, N, K, "f16", "nk", "uniform", 1.0, M + N)
+    _full_size_check(felix, cfg, 256, 512)
