@@ -75,11 +75,14 @@ FA_BWD_8192 = AttnConfig("flash_attn_bwd_f16_4x32x8192x128", 4, 32, 8192, 128, 3
 # a smaller backward case for detailed ncu captures (1/8 of the (b, h, query) rows)
 FA_BWD_4096 = AttnConfig("flash_attn_bwd_f16_2x16x4096x128", 2, 16, 4096, 128, 3,
                          backward=True)
+# a smaller forward case for detailed ncu captures (1/4 of the (b, h) pairs;
+# Q, K, V, O still 4 x 128 MiB, larger than the L2)
+FA_FWD_2x16 = AttnConfig("flash_attn_fwd_f16_2x16x8192x128", 2, 16, 8192, 128, 3)
 HGEMM_16384 = GemmConfig("hgemm_f16_16384_nt", 16384, 16384, 16384, "f16", "nk", "uniform", 1.0,
                          4)
 
 CONFIGS = {c.name: c for c in (SGEMM_1024, HGEMM_4096, HGEMM_SKINNY, FA_8192, HGEMM_16384,
-                               FA_8192_CAUSAL, FA_BWD_8192, FA_BWD_4096)}
+                               FA_8192_CAUSAL, FA_BWD_8192, FA_BWD_4096, FA_FWD_2x16)}
 
 
 def _draw(gen: torch.Generator, shape, dist: str, std: float) -> torch.Tensor:
