@@ -132,6 +132,15 @@ __device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint
                "r"(b), "r"(c), "r"(d)
                : "memory");
 }
+// 16-byte load from shared memory of a CTA of the cluster (address from mapa_shared).
+__device__ __forceinline__ float4 ld_shared_cluster_v4f(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
 // Barrier over all threads of all CTAs of the cluster.
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
