@@ -113,7 +113,11 @@ int felix_hgemm(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* A, 
  * block_n: 0 auto, 64, 128 or 256. stream_k: 0 auto, 1 off, 2 on whenever the last
  * wave of tiles is incomplete. max_ctas: 0 = one persistent CTA per SM.
  * workspace: NULL = library-owned per-(device, stream) scratch; otherwise at
- * least felix_hgemm_workspace_size() bytes, zero-filled before first use.
+ * least felix_hgemm_workspace_size() bytes, zero-filled before first use. Its
+ * first 16 KiB are counters (stream-K tickets; for shapes of four or more
+ * waves of tiles, the counter that hands whole tiles out at run time) that
+ * every launch leaves at zero, so launches that share a workspace must not
+ * overlap on the GPU.
  */
 int felix_hgemm_ex(uint32_t M, uint32_t N, uint32_t K, float alpha, const void* A,
                    const void* B, float beta, void* C, int b_layout, int block_n, int stream_k,
