@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import concurrent.futures as cf
 import os
+import re
 import subprocess
 import sys
 import sysconfig
@@ -52,10 +53,35 @@ def _newer(out: str, deps: list[str]) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def _run(cmd: list[str]) -> None:
+def _run(cmd: list[str]) -> str:
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"build step failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    return r.stdout + r.stderr
+
+
+# The attention forward kernel moves registers between its warpgroups with
+# setmaxnreg; the split is computed for a launch count of 168 registers per
+# thread (flash_attn_sm100.cu kRegsLaunch). The host refuses to launch a build
+# whose count differs; this check reports it at build time instead.
+FA_REGS_LAUNCH = 168
+
+
+def check_attention_registers(ptxas_log: str) -> None:
+    """Raise if ptxas gave the register-split forward kernel another count."""
+    cur = None
+    for line in ptxas_log.splitlines():
+        m = re.search(r"Compiling entry function '([^']+)'", line)
+        if m:
+            cur = m.group(1)
+            continue
+        m = re.search(r"Used (\d+) registers", line)
+        if m and cur and "flash_attn_fwd_kernel" in cur:
+            if int(m.group(1)) != FA_REGS_LAUNCH:
+                raise RuntimeError(
+                    f"{cur}: ptxas used {m.group(1)} registers per thread; the attention "
+                    f"kernel's setmaxnreg split assumes {FA_REGS_LAUNCH} (build with "
+                    f"-DFELIX_FA_REGSPLIT=0 or adjust kRegsLaunch)")
 
 
 def _headers() -> list[str]:
@@ -75,7 +101,8 @@ def build_felix(force: bool = False) -> str:
         obj = os.path.join(BUILD, s + ".o")
         objs.append(obj)
         if force or _newer(obj, [src] + hdrs):
-            jobs.append([NVCC, *NVCC_FLAGS, f"-I{INC}", "-c", src, "-o", obj])
+            extra = ["-Xptxas", "-v"] if s == "flash_attn_sm100.cu" else []
+            jobs.append([NVCC, *NVCC_FLAGS, *extra, f"-I{INC}", "-c", src, "-o", obj])
     for s in CPP_SOURCES:
         src = os.path.join(CSRC, s)
         obj = os.path.join(BUILD, s + ".o")
@@ -85,7 +112,10 @@ def build_felix(force: bool = False) -> str:
                          f"-I{INC}", f"-I{CUDA_HOME}/include",
                          "-c", src, "-o", obj])
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
-        list(ex.map(_run, jobs))
+        logs = list(ex.map(_run, jobs))
+    for job, log in zip(jobs, logs):
+        if "-Xptxas" in job:
+            check_attention_registers(log)
     if force or jobs or _newer(LIB, objs):
         _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a",
               "-cudart", "static", "-o", LIB, *objs, "-ldl"])
