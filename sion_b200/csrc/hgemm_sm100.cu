@@ -324,8 +324,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* recv = bars + 2 * S + 5;   // [1] cluster split-K: rank 1's half arrived (rank 0)
   uint64_t* ring_free = bars + 2 * S + 6;  // [1] cluster split-K: rank 0's ring idle (rank 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
-  // Cluster split-K: rank 1's accumulator (BM x BN fp32) goes into the start
-  // of rank 0's TMA ring once rank 0's MMAs have finished with it.
+  // Cluster split-K: each CTA sends the peer's 64 columns of its accumulator
+  // (BM x 64 fp32) into the start of the peer's TMA ring once the peer's MMAs
+  // have finished with it.
   const uint32_t NS = uint32_t(S);
   uint8_t* recv_buf = ring;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -347,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], 4 * CG);  // a pair's leader counts both CTAs' epilogue warps
     }
     mbar_init(drain, 1);
-    mbar_init(recv, 128);  // one arrival per epilogue thread of rank 1
+    mbar_init(recv, 128);  // one arrival per epilogue thread of the peer CTA
     mbar_init(ring_free, 1);
     for (uint32_t i = 0; i < kTq; ++i) {
       mbar_init(&tq.full[i], 1);
@@ -630,43 +631,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t col0 = tn * BN;
       const uint32_t taddr = tmem_base + ((q * 32u) << 16) + buf * BN;
 
-      if (p.ksplit2 && u.seg == 1) {
-        // Cluster split-K, second half of K: the fp32 accumulator goes to rank
-        // 0's receive buffer over DSMEM (partial_index layout: a warp's 32 rows
-        // are 512 contiguous bytes), then every thread arrives on rank 0's
-        // barrier (release: its stores are visible before the arrival counts).
-        const uint32_t rbuf = mapa_shared(smem_u32(recv_buf), 0);
-        if (!mbar_wait(ring_free, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
+      if (p.ksplit2) {
+        // Cluster split-K: the two CTAs hold the tile's two K halves. Rank r
+        // writes output columns [64 r, 64 r + 64): it sends the peer's 64
+        // columns of its fp32 accumulator into the peer's idle TMA ring over
+        // DSMEM (partial_index layout: a warp's 32 rows are 512 contiguous
+        // bytes; every thread then arrives on the peer's barrier, release),
+        // and adds the peer's 64 columns of its own to its accumulator (fp32
+        // addition of two terms, so both ranks form the same sums), converts
+        // and TMA-stores. Both directions run at once: half the bytes each
+        // way and half the columns per CTA, against one CTA sending 128.
+        const uint32_t me = u.seg, peer = me ^ 1u;
+        // tfull: every MMA of this CTA has completed, so its ring is idle
+        // (nothing more is loaded: this is the CTA's only unit)
+        if (epi_tid == 0) mbar_arrive_cluster(mapa_shared(smem_u32(ring_free), peer));
+        if (!mbar_wait_cluster(ring_free, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
+        const uint32_t rbuf = mapa_shared(smem_u32(recv_buf), peer);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < 64; c += 32) {
           uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + c, r);
+          tmem_ld_32x32b_x32(taddr + peer * 64 + c, r);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             st_shared_cluster_v4(rbuf + partial_index(c / 32, j, row_in_tile) * 16, r[4 * j],
                                  r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
         }
-        mbar_arrive_cluster(mapa_shared(smem_u32(recv), 0));
-      } else if (p.ksplit2) {
-        // Cluster split-K, first half: C = alpha * (own + rank 1's half), in
-        // that order (deterministic), through the TMA-store staging below.
-        // tfull: every MMA of this CTA has completed, so its ring is idle
-        // (nothing more is loaded: this is the CTA's only unit)
-        if (epi_tid == 0) mbar_arrive_cluster(mapa_shared(smem_u32(ring_free), 1));
-        if (!mbar_wait(recv, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
+        mbar_arrive_cluster(mapa_shared(smem_u32(recv), peer));
+        if (!mbar_wait_cluster(recv, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
         const float4* r4 = reinterpret_cast<const float4*>(recv_buf);
         uint8_t* stg = staging + (warp - 2) * 8192;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 64) {
+        {
+          const uint32_t c = me * 64;
           uint32_t r0[32], r1[32];
           tmem_ld_32x32b_x32(taddr + c, r0);
           tmem_ld_32x32b_x32(taddr + c + 32, r1);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float4 x0 = r4[partial_index(c / 32, j, row_in_tile)];
-            const float4 x1 = r4[partial_index(c / 32 + 1, j, row_in_tile)];
+            const float4 x0 = r4[partial_index(0, j, row_in_tile)];
+            const float4 x1 = r4[partial_index(1, j, row_in_tile)];
             r0[4 * j] = __float_as_uint(__uint_as_float(r0[4 * j]) + x0.x);
             r0[4 * j + 1] = __float_as_uint(__uint_as_float(r0[4 * j + 1]) + x0.y);
             r0[4 * j + 2] = __float_as_uint(__uint_as_float(r0[4 * j + 2]) + x0.z);
@@ -676,9 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             r1[4 * j + 2] = __float_as_uint(__uint_as_float(r1[4 * j + 2]) + x1.z);
             r1[4 * j + 3] = __float_as_uint(__uint_as_float(r1[4 * j + 3]) + x1.w);
           }
-          uint8_t* buf = stg + ((c / 64) & 1) * 4096;
-          if (lane == 0) bulk_wait_group_read<1>();
-          __syncwarp();
+          uint8_t* buf = stg;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const uint32_t* src = j < 4 ? &r0[8 * j] : &r1[8 * (j - 4)];
