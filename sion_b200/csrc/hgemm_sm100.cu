@@ -796,6 +796,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 v1[4 * j] += x1[j].x; v1[4 * j + 1] += x1[j].y;
                 v1[4 * j + 2] += x1[j].z; v1[4 * j + 3] += x1[j].w;
               }
+              // the partial is dead once summed: drop its L2 lines without a
+              // write-back to DRAM (a 128-byte line holds 8 rows of one
+              // float4 column; every lane of the warp has its values)
+              __syncwarp();
+              if ((row_in_tile & 7u) == 0) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  l2_discard_line(s4 + partial_index(c / 32, j, row_in_tile));
+                  l2_discard_line(s4 + partial_index(c / 32 + 1, j, row_in_tile));
+                }
+              }
             }
             store_row_chunk(p, row, col0 + c, v0);
             store_row_chunk(p, row, col0 + c + 32, v1);
