@@ -322,7 +322,7 @@ __device__ __forceinline__ bool tma_issue(TmaPipe& q, const CUtensorMap* tmA,
 
 // acc = A[m0 : m0 + 128, kbeg : kend] * B[kbeg : kend, n0 : n0 + 128] with
 // kbeg a multiple of 32 (k past kend inside the last k-tile must be past K).
-template <int AP>
+template <int AP, int AK = kTmaAk>
 __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
                                              const CUtensorMap* tmB, const Params& p,
                                              uint32_t m0, uint32_t n0, uint32_t kbeg,
@@ -347,22 +347,30 @@ __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
     if (j == 0) SG_TR(q.tr_seg * 3 + 1);
     const float* a_s = q.sA + st * (TmaTile<AP>::kA / 4);  // [128][AP]
     const float* b_s = q.sB + st * (kTmaBTile / 4);  // [32][128]
-    // one group of kTmaAk k-steps per iteration, not unrolled: unrolled, the
+    // one group of AK k-steps per iteration, not unrolled: unrolled, the
     // compiler hoists the B loads of later groups and spills at 128 registers
 #pragma unroll 1
-    for (int k2 = 0; k2 < kTmaBk / kTmaAk; ++k2) {
-      // A: kTmaAk consecutive k of each of the thread's 8 rows per load
-      float af[8][kTmaAk];
+    for (int k2 = 0; k2 < kTmaBk / AK; ++k2) {
+      // A: AK consecutive k of each of the thread's 8 rows per load
+      float af[8][AK];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint32_t row = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
-        const float2 v = *reinterpret_cast<const float2*>(a_s + row * AP + k2 * kTmaAk);
-        af[i][0] = v.x;
-        af[i][1] = v.y;
+        if constexpr (AK == 4) {
+          const float4 v = *reinterpret_cast<const float4*>(a_s + row * AP + k2 * AK);
+          af[i][0] = v.x;
+          af[i][1] = v.y;
+          af[i][2 % AK] = v.z;
+          af[i][3 % AK] = v.w;
+        } else {
+          const float2 v = *reinterpret_cast<const float2*>(a_s + row * AP + k2 * AK);
+          af[i][0] = v.x;
+          af[i][1] = v.y;
+        }
       }
 #pragma unroll
-      for (int kk = 0; kk < kTmaAk; ++kk) {
-        const int k = k2 * kTmaAk + kk;
+      for (int kk = 0; kk < AK; ++kk) {
+        const int k = k2 * AK + kk;
         float b[TN];
 #pragma unroll
         for (int g = 0; g < NB; ++g) {
@@ -406,8 +414,11 @@ __device__ __forceinline__ uint32_t sk_cta_of(uint64_t x, uint32_t P, uint64_t I
   return static_cast<uint32_t>(((x + 1) * P - 1) / I);
 }
 
-template <bool VEC, bool TMA, int AP = 32>
-__global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
+// CSK: the cluster split-K instantiation, one CTA per SM (up to 255
+// registers), so its main loop reads A 4 k at a time (128-bit loads); the
+// plain kernels keep two CTAs per SM at 128 registers and 2-k A reads.
+template <bool VEC, bool TMA, int AP = 32, bool CSK = false>
+__global__ void __launch_bounds__(kThreads, CSK ? 1 : FELIX_SGEMM_MINB)
     sgemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const Params p) {
   extern __shared__ __align__(1024) uint8_t dsmem[];
@@ -441,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
   SG_TR(0);
   auto run = [&](uint32_t m0, uint32_t n0, uint32_t kbeg, uint32_t kend) -> bool {
     if constexpr (TMA) {
-      return mainloop_tma<AP>(q, &tmA, &tmB, p, m0, n0, kbeg, kend, acc);
+      return mainloop_tma<AP, CSK ? 4 : kTmaAk>(q, &tmA, &tmB, p, m0, n0, kbeg, kend, acc);
     } else {
       mainloop<VEC>(p, m0, n0, kbeg, kend, As, Bs, acc);
       return true;
@@ -525,8 +536,10 @@ __global__ void __launch_bounds__(kThreads, FELIX_SGEMM_MINB)
   const uint32_t kend = min(p.K, kbeg + p.k_per_split);
   const bool ok = run(m0, n0, kbeg, kend);
   drain_tma<TMA>(q, p);
-  if constexpr (TMA) {
-    if (p.csk) {
+  // (a separate instantiation: the cluster epilogue in the same kernel as the
+  // plain one changed the main loop's code and cost 16 % at 4096^3)
+  if constexpr (TMA && CSK) {
+    {
       // Cluster split-K: each CTA parks its fp32 partial tile in its own
       // (now idle) TMA ring, then CTA r of the cluster sums rows
       // [r * 128 / S, (r + 1) * 128 / S) of all S partials in rank order
@@ -662,7 +675,7 @@ uint32_t choose_stream_k(uint32_t M, uint32_t N, uint32_t K, const SgemmOptions&
   if (o.split_k != 0 || !o.allow_stream_k) return 0;
   const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const uint32_t kt = (K + bk - 1) / bk;
-  const uint32_t slots = 2u * uint32_t(num_sms);
+  const uint32_t slots = uint32_t(FELIX_SGEMM_MINB) * uint32_t(num_sms);
   // (with a full wave or more, plain tiles measured as fast: 4096^3 43.9 vs
   // 43.3 TFLOP/s)
   if (kt < 8 || tiles >= slots || tiles > kWsMaxCounters) return 0;
@@ -723,6 +736,12 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(sgemm_kernel<true, true, 36>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<36>::kSmem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(sgemm_kernel<true, true, 32, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<32>::kSmem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(sgemm_kernel<true, true, 36, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<36>::kSmem);
       return int(e);
     });
     if (rc < 0) return api_error("sgemm: device ordinal");
@@ -764,7 +783,7 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
   // 459 vs 401 and 512 x 512 x 8192 236 vs 127 (left to stream-K).
   {
     const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    const uint32_t slots = 2u * uint32_t(dev->num_sms);
+    const uint32_t slots = uint32_t(dev->num_sms);  // one cluster-split CTA per SM
     const uint32_t kt = (K + p.bk - 1) / p.bk;
     uint32_t S = 0;
     if (tma && o.split_k == 0 && o.allow_stream_k && tiles * 2 <= slots) {
@@ -789,8 +808,8 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       const cudaError_t e = ap == 36
-                                ? cudaLaunchKernelEx(&cfg, sgemm_kernel<true, true, 36>, tmA, tmB, p)
-                                : cudaLaunchKernelEx(&cfg, sgemm_kernel<true, true, 32>, tmA, tmB, p);
+                                ? cudaLaunchKernelEx(&cfg, sgemm_kernel<true, true, 36, true>, tmA, tmB, p)
+                                : cudaLaunchKernelEx(&cfg, sgemm_kernel<true, true, 32, true>, tmA, tmB, p);
       if (e != cudaSuccess) return launch_error(e, "sgemm: cluster launch failed");
       return FelixCode{FELIX_SUCCESS, cudaSuccess};
     }
