@@ -279,6 +279,9 @@ constexpr int kTmaStages = 3;
 // registers). 4 (LDS.128) needs 16 more registers and spilled at the 128 that
 // two CTAs per SM allow: 4096^3 45.4 vs 51.9 TFLOP/s.
 constexpr int kTmaAk = 2;
+// the one-CTA-per-SM loop (4-k A reads) has the registers to unroll four
+// groups: 1024^3 65.5 -> 61.5-62.0 us (2: 62.5, 8: 63.0-63.5)
+constexpr int kAk4Unroll = 4;
 constexpr int kTmaBTile = kTmaBk * BN * 4;  // 16 KB (BN = 128)
 // A tile of AP floats per row (AP = row pitch). AP = 32: the rows a warp reads
 // at once (4 apart) share banks, a 2-way conflict on every A load. AP = 36: the
@@ -347,9 +350,10 @@ __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
     if (j == 0) SG_TR(q.tr_seg * 3 + 1);
     const float* a_s = q.sA + st * (TmaTile<AP>::kA / 4);  // [128][AP]
     const float* b_s = q.sB + st * (kTmaBTile / 4);  // [32][128]
-    // one group of AK k-steps per iteration, not unrolled: unrolled, the
-    // compiler hoists the B loads of later groups and spills at 128 registers
-#pragma unroll 1
+    // one group of AK k-steps per iteration; the 2-k loop is not unrolled:
+    // unrolled, the compiler hoists the B loads of later groups and spills at
+    // 128 registers
+#pragma unroll(AK == 4 ? kAk4Unroll : 1)
     for (int k2 = 0; k2 < kTmaBk / AK; ++k2) {
       // A: AK consecutive k of each of the thread's 8 rows per load
       float af[8][AK];
