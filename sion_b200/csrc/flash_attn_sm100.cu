@@ -96,6 +96,7 @@ struct Params {
   uint32_t q_tiles;  // CTA groups per (b, h) along the query axis
   float scale_log2;  // scale * log2(e)
   uint32_t causal;   // 1: query i attends to keys 0..i only
+  uint32_t items;    // (b, h) x query-tile groups; CTAs (groups) stride over them
   unsigned* status;
 };
 
@@ -190,22 +191,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + 2;             // [2 tiles][2 halves] (leader's counts both CTAs)
   uint64_t* pv_done = s_full + 6;            // [2]
   uint64_t* drain = s_full + 8;              // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 9);
+  uint64_t* q_empty = s_full + 9;            // [1] Q of the current item consumed (MMA commit)
+  uint64_t* o_free = s_full + 10;            // [2] O_t read out by the epilogue (leader's)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = threadIdx.x / 32;
   const uint32_t lane = threadIdx.x % 32;
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
-  const uint32_t grp = blockIdx.x / CG;
-  const uint32_t bh = grp / p.q_tiles;
-  // Causal: the longest query tiles first (they bound the tail of the grid).
-  const uint32_t qt = p.causal ? p.q_tiles - 1 - grp % p.q_tiles : grp % p.q_tiles;
-  const uint32_t grp_q0 = qt * (2 * kBlockQ * CG);
-  const uint32_t q0 = grp_q0 + rank * (2 * kBlockQ);
-  // KV blocks this CTA (group) streams: all, or (causal) up to the block that
-  // holds the group's last query row. Every role of the group uses the same n.
-  const uint32_t n =
-      p.causal ? min(p.n_kv, (grp_q0 + 2 * kBlockQ * CG - 1) / kBlockKV + 1) : p.n_kv;
+  // Work items: (b, h) x group of query tiles. A CTA (group) takes items
+  // first, first + stride, ...: one item when the grid has one CTA (group)
+  // per item, several when the launch is persistent (one CTA per SM). Every
+  // role walks the same items and counts KV blocks globally across them (jg),
+  // so ring stages and barrier parities simply continue from item to item.
+  const uint32_t first_item = blockIdx.x / CG, item_stride = gridDim.x / CG;
+  struct Item {
+    uint32_t bh, grp_q0, q0, n;
+  };
+  auto item_of = [&](uint32_t grp) {
+    Item r;
+    r.bh = grp / p.q_tiles;
+    // Causal: the longest query tiles first (they bound the tail of the grid).
+    const uint32_t qt = p.causal ? p.q_tiles - 1 - grp % p.q_tiles : grp % p.q_tiles;
+    r.grp_q0 = qt * (2 * kBlockQ * CG);
+    r.q0 = r.grp_q0 + rank * (2 * kBlockQ);
+    // KV blocks this item streams: all, or (causal) up to the block that holds
+    // the group's last query row. Every role of the group uses the same n.
+    r.n = p.causal ? min(p.n_kv, (r.grp_q0 + 2 * kBlockQ * CG - 1) / kBlockKV + 1) : p.n_kv;
+    return r;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -224,6 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(drain, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(&o_free[0], 4 * CG);
+    mbar_init(&o_free[1], 4 * CG);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -267,45 +284,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* full = is_k ? k_full : v_full;
       uint64_t* empty = is_k ? k_empty : v_empty;
       uint8_t* ring = smem + (is_k ? C_::kKOff : C_::kVOff);
-      if (is_k) {
-        uint8_t* sq = smem + C_::kQOff;
-        if (rank == 0) mbar_arrive_expect_tx(q_full, CG * 2 * C_::kTileBytes);
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-          for (int c = 0; c < C_::kChunks; ++c)
-            load3d(sq + t * C_::kTileBytes + c * (kBlockQ * 128), &tmQ, q_full, 64 * c,
-                   int(q0 + t * kBlockQ), int(bh));
-      }
-      uint32_t filled = 0;
-      for (uint32_t j = 0; j < n; ++j) {
-        const uint32_t st = j % NS;
-        const uint32_t ph = (j / NS) & 1u;
-        if (!mbar_wait(&empty[st], ph ^ 1u, abort_flag, p.status, kWdAttnLoad)) break;
-        FA_TRACE(3, j, is_k ? 3 : 2);
-        uint8_t* dst = ring + st * slot_bytes;
-        if (rank == 0) mbar_arrive_expect_tx(&full[st], CG * slot_bytes);
+      uint32_t filled = 0, jg = 0, ii = 0, q_issued = 0;
+      bool ok = true;
+      for (uint32_t it = first_item; ok && it < p.items; it += item_stride, ++ii) {
+        const Item w = item_of(it);
         if (is_k) {
-          // K rows [key0, key0 + kKeys) of block j, all D columns
-          const int key0 = int(j * kBlockKV + rank * C_::kKeys);
+          // Q of the previous item must have been consumed by its S MMAs
+          if (ii > 0 &&
+              !(ok = mbar_wait(q_empty, (ii - 1) & 1u, abort_flag, p.status, kWdAttnLoad)))
+            break;
+          uint8_t* sq = smem + C_::kQOff;
+          if (rank == 0) mbar_arrive_expect_tx(q_full, CG * 2 * C_::kTileBytes);
 #pragma unroll
-          for (int c = 0; c < C_::kChunks; ++c)
-            load3d(dst + c * (C_::kKeys * 128), map, &full[st], 64 * c, key0, int(bh));
-        } else {
-          // all keys of block j, D columns [col0, col0 + kVCols)
-          const int col0 = int(rank * C_::kVCols);
+          for (int t = 0; t < 2; ++t)
 #pragma unroll
-          for (int c = 0; c < C_::kVCols / 64; ++c)
-            load3d(dst + c * (kBlockKV * 128), map, &full[st], col0 + 64 * c,
-                   int(j * kBlockKV), int(bh));
+            for (int c = 0; c < C_::kChunks; ++c)
+              load3d(sq + t * C_::kTileBytes + c * (kBlockQ * 128), &tmQ, q_full, 64 * c,
+                     int(w.q0 + t * kBlockQ), int(w.bh));
+          ++q_issued;
         }
-        ++filled;
+        for (uint32_t j = 0; j < w.n; ++j, ++jg) {
+          const uint32_t st = jg % NS;
+          const uint32_t ph = (jg / NS) & 1u;
+          if (!(ok = mbar_wait(&empty[st], ph ^ 1u, abort_flag, p.status, kWdAttnLoad))) break;
+          FA_TRACE(3, j, is_k ? 3 : 2);
+          uint8_t* dst = ring + st * slot_bytes;
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], CG * slot_bytes);
+          if (is_k) {
+            // K rows [key0, key0 + kKeys) of block j, all D columns
+            const int key0 = int(j * kBlockKV + rank * C_::kKeys);
+#pragma unroll
+            for (int c = 0; c < C_::kChunks; ++c)
+              load3d(dst + c * (C_::kKeys * 128), map, &full[st], 64 * c, key0, int(w.bh));
+          } else {
+            // all keys of block j, D columns [col0, col0 + kVCols)
+            const int col0 = int(rank * C_::kVCols);
+#pragma unroll
+            for (int c = 0; c < C_::kVCols / 64; ++c)
+              load3d(dst + c * (kBlockKV * 128), map, &full[st], col0 + 64 * c,
+                     int(j * kBlockKV), int(w.bh));
+          }
+          ++filled;
+        }
       }
-      // drain: the last fill of each stage must land before the CTA exits; the
-      // leader's barriers count the bytes of both CTAs of a pair
+      // drain: the last fill of each stage (and the last Q) must land before
+      // the CTA exits; the leader's barriers count the bytes of both CTAs
       if (rank == 0) {
         int dummy = 0;
-        if (is_k) mbar_wait(q_full, 0, &dummy, p.status, kWdDrain, 100000000ull);
+        if (is_k && q_issued > 0)
+          mbar_wait(q_full, (q_issued - 1) & 1u, &dummy, p.status, kWdDrain, 100000000ull);
         const uint32_t m = filled < uint32_t(NS) ? filled : uint32_t(NS);
         for (uint32_t i = 0; i < m; ++i) {
           const uint32_t f = filled - 1 - i;
@@ -337,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return __all_sync(0xffffffffu,
                           mbar_wait(bar, parity, abort_flag, p.status, kWdAttnMma)) != 0;
       };
-      bool ok = wait_all(q_full, 0);
+      bool ok = true;
       auto issue_s = [&](uint32_t j, int t) {
         const uint32_t sk = smem_u32(smem + C_::kKOff + (j % KST) * C_::kKBytes);
         const uint32_t qa = sq + t * C_::kTileBytes;
@@ -363,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE(3, j, 4 + t);
       };
       // PV_t(j) over keys [64 h, 64 h + 64): P's half h
-      auto issue_pv = [&](uint32_t j, int t, int h) {
+      auto issue_pv = [&](uint32_t j, uint32_t jl, int t, int h) {
         const uint32_t sv = smem_u32(smem + C_::kVOff + (j % VST) * C_::kVBytes);
         if (elect_one()) {
           const uint64_t v0 = vmajor_desc(sv, 0);
@@ -372,9 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t a = tmem + col_s(t) + k * 8;
             const uint64_t vd = v0 + uint64_t(k * (2048 >> 4));
             if constexpr (CG == 2)
-              umma_f16_ts_pair(tmem + col_o(t), a, vd, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+              umma_f16_ts_pair(tmem + col_o(t), a, vd, idesc_pv, (jl > 0 || k > 0) ? 1u : 0u);
             else
-              umma_f16_ts(tmem + col_o(t), a, vd, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+              umma_f16_ts(tmem + col_o(t), a, vd, idesc_pv, (jl > 0 || k > 0) ? 1u : 0u);
           }
           if (h == 1) {
             commit_all(&pv_done[t]);
@@ -383,48 +410,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       };
-      if (ok && n > 0) {
-        ok = wait_all(&k_full[0], 0);
-        if (ok) {
-          tc_fence_after();
-          issue_s(0, 0);
-          issue_s(0, 1);
-        }
-      }
-      // Per block j and tile t: PV_t(j) as soon as P_t(j) is ready, then
-      // S_t(j+1) right behind it (the tensor pipe executes the MMAs in issue
-      // order, so S_t(j+1)'s writes cannot overtake PV_t(j)'s reads of P_t).
-      // The two tiles run half a period apart, so the softmax of one tile
-      // overlaps the other tile's MMAs.
-      for (uint32_t j = 0; ok && j < n; ++j) {
-        FA_TRACE(3, j, 0);
-        if (!(ok = wait_all(&v_full[j % VST], (j / VST) & 1u)))
-          break;
-        FA_TRACE(3, j, 1);
-        for (int t = 0; t < 2; ++t) {
-          FA_TRACE(2, j, 4 * t + 0);
-          // P_t(j) arrives in two halves of 64 keys: PV over the first half
-          // overlaps the softmax of the second
-          if (!(ok = wait_all(&p_full[2 * t], j & 1u))) break;
-          tc_fence_after();
-          FA_TRACE(2, j, 4 * t + 1);
-          issue_pv(j, t, 0);
-          if (!(ok = wait_all(&p_full[2 * t + 1], j & 1u)))
-            break;
-          tc_fence_after();
-          issue_pv(j, t, 1);
-          if (j + 1 < n) {
-            FA_TRACE(2, j, 4 * t + 2);
-            if (t == 0 && !(ok = wait_all(&k_full[(j + 1) % KST], ((j + 1) / KST) & 1u)))
-              break;
-            if (kWaitPV &&
-                !(ok = wait_all(&pv_done[t], j & 1u)))
-              break;
+      // Per item: Q ready, S_A(0), S_B(0); then per block j and tile t:
+      // PV_t(j) as soon as P_t(j) is ready, then S_t(j+1) right behind it
+      // (the tensor pipe executes the MMAs in issue order, so S_t(j+1)'s
+      // writes cannot overtake PV_t(j)'s reads of P_t). The two tiles run half
+      // a period apart, so the softmax of one tile overlaps the other tile's
+      // MMAs. Across items: the first PV of a tile waits until the epilogue
+      // has read O_t out (o_free); Q is released once the item's S MMAs are
+      // done (q_empty), so the loader can bring the next item's Q.
+      uint32_t jg = 0, ii = 0;
+      for (uint32_t it = first_item; ok && it < p.items; it += item_stride, ++ii) {
+        const Item w = item_of(it);
+        if (!(ok = wait_all(q_full, ii & 1u))) break;
+        if (!(ok = wait_all(&k_full[jg % KST], (jg / KST) & 1u))) break;
+        tc_fence_after();
+        issue_s(jg, 0);
+        issue_s(jg, 1);
+        // Q is free once the item's last S MMAs complete: release it right
+        // behind them, so the next item's Q loads during this item's tail
+        auto release_q = [&]() {
+          if (elect_one()) commit_all(q_empty);
+          __syncwarp();
+        };
+        if (w.n == 1) release_q();
+        for (uint32_t j = 0; ok && j < w.n; ++j) {
+          const uint32_t g = jg + j;
+          FA_TRACE(3, j, 0);
+          if (!(ok = wait_all(&v_full[g % VST], (g / VST) & 1u))) break;
+          FA_TRACE(3, j, 1);
+          for (int t = 0; t < 2; ++t) {
+            FA_TRACE(2, j, 4 * t + 0);
+            if (j == 0 && ii > 0 && !(ok = wait_all(&o_free[t], (ii - 1) & 1u))) break;
+            // P_t(j) arrives in two halves of 64 keys: PV over the first half
+            // overlaps the softmax of the second
+            if (!(ok = wait_all(&p_full[2 * t], g & 1u))) break;
             tc_fence_after();
-            FA_TRACE(2, j, 4 * t + 3);
-            issue_s(j + 1, t);
+            FA_TRACE(2, j, 4 * t + 1);
+            issue_pv(g, j, t, 0);
+            if (!(ok = wait_all(&p_full[2 * t + 1], g & 1u))) break;
+            tc_fence_after();
+            issue_pv(g, j, t, 1);
+            if (j + 1 < w.n) {
+              FA_TRACE(2, j, 4 * t + 2);
+              if (t == 0 && !(ok = wait_all(&k_full[(g + 1) % KST], ((g + 1) / KST) & 1u)))
+                break;
+              if (kWaitPV && !(ok = wait_all(&pv_done[t], g & 1u))) break;
+              tc_fence_after();
+              FA_TRACE(2, j, 4 * t + 3);
+              issue_s(g + 1, t);
+              if (t == 1 && j + 2 == w.n) release_q();
+            }
           }
         }
+        if (!ok) break;
+        jg += w.n;
       }
       if (elect_one()) {
         if constexpr (CG == 2)
@@ -448,12 +487,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tS = tmem + lane_addr + col_s(t);
     const uint32_t tO = tmem + lane_addr + col_o(t);
     const float sl2 = p.scale_log2;
+    bool ok = true;
+    uint32_t jg = 0;
+    for (uint32_t it = first_item; ok && it < p.items; it += item_stride) {
+    const Item w = item_of(it);
+    const uint32_t n = w.n, q0 = w.q0, bh = w.bh;
     float m = -INFINITY;  // running max in log2 units (the one P is relative to)
     float l = 0.f;
-    bool ok = true;
     for (uint32_t j = 0; j < n; ++j) {
+      const uint32_t g = jg + j;  // block count across items (barrier parities)
       if (lane == 0 && q == 0) FA_TRACE(t, j, 0);
-      if (!(ok = mbar_wait(&s_full[t], j & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
+      if (!(ok = mbar_wait(&s_full[t], g & 1u, abort_flag, p.status, kWdAttnSoftmax))) break;
       tc_fence_after();
       if (lane == 0 && q == 0) FA_TRACE(t, j, 1);
       // keys of this block the row may see: the ragged tail of the sequence
@@ -561,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
         if (j > 0) {
           // O_t holds PV(0..j-1): rescale it once PV(j-1) has completed.
-          if (!(ok = mbar_wait(&pv_done[t], (j - 1) & 1u, abort_flag, p.status,
+          if (!(ok = mbar_wait(&pv_done[t], (g - 1) & 1u, abort_flag, p.status,
                                kWdAttnCorrection)))
             break;
           tc_fence_after();
@@ -602,8 +646,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
     }
     // ---------------------------------------------------------------- epilogue
-    if (ok && n > 0 &&
-        mbar_wait(&pv_done[t], (n - 1) & 1u, abort_flag, p.status, kWdAttnSoftmax)) {
+    if (!ok) break;
+    if (!(ok = mbar_wait(&pv_done[t], (jg + n - 1) & 1u, abort_flag, p.status,
+                         kWdAttnSoftmax)))
+      break;
+    {
       tc_fence_after();
       const uint32_t qrow = q0 + t * kBlockQ + row;
       const float inv_l = 1.f / l;
@@ -627,6 +674,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (p.lse && qrow < p.S)
         p.lse[size_t(bh) * p.S + qrow] = (m + __log2f(l)) * 0.69314718055994531f;
+    }
+    // O_t has been read out: the next item's first PV_t may overwrite it
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (CG == 2)
+        mbar_arrive_cluster(leader_bar(&o_free[t]));
+      else
+        mbar_arrive(&o_free[t]);
+    }
+    jg += n;
     }
   }
 
@@ -760,18 +818,24 @@ FelixCode flash_attn_launch(const __half* Q, const __half* K, const __half* V, _
   p.status = dev->status_word;
   const uint64_t groups = bh * p.q_tiles;
   if (groups * cg > 0x7fffffffull) return api_error("flash_attn: grid too large");
+  p.items = uint32_t(groups);
+  // Persistent (one CTA per SM walking the items) when there are more items
+  // than SMs and every item is the same length; causal items differ, so they
+  // keep one CTA per item, longest first.
+  const uint64_t grid_groups =
+      (cg == 1 && !causal && groups > uint64_t(dev->num_sms)) ? uint64_t(dev->num_sms) : groups;
 
   int rc;
   cudaError_t e;
   if (head_dim == 128 && cg == 2) {
     if ((rc = configure_once<128, 2>(dev->ordinal))) return configure_error(rc);
-    e = launch<128, 2>(groups, tq, tk, tv, p, stream);
+    e = launch<128, 2>(grid_groups, tq, tk, tv, p, stream);
   } else if (head_dim == 128) {
     if ((rc = configure_once<128, 1>(dev->ordinal))) return configure_error(rc);
-    e = launch<128, 1>(groups, tq, tk, tv, p, stream);
+    e = launch<128, 1>(grid_groups, tq, tk, tv, p, stream);
   } else {
     if ((rc = configure_once<64, 1>(dev->ordinal))) return configure_error(rc);
-    e = launch<64, 1>(groups, tq, tk, tv, p, stream);
+    e = launch<64, 1>(grid_groups, tq, tk, tv, p, stream);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return launch_error(e, "flash_attn: launch failed");
