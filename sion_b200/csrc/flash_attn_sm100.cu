@@ -10,7 +10,8 @@
 //
 // Layout: Q, K, V, O are [B, H, S, D] contiguous; LSE is [B, H, S].
 //
-// CTA = one (b, h) and 256 query rows as two 128-row tiles "A" and "B".
+// Work item = one (b, h) and 256 query rows as two 128-row tiles "A" and "B";
+// a CTA takes one item, or (persistent launch, non-causal) strides over items.
 //   warp 0      TMA loader: Q_A, Q_B once, then the K ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //   warp 2      TMA loader of the V ring
