@@ -58,6 +58,14 @@ def test_attention_reference_test_case(felix):
     _check(*_run(felix, 16, 16, 1280, 128, seed=0, rows=rows), ctx="fa_test 16x16x1280x128")
 
 
+@pytest.mark.parametrize("H,S,D", [(160, 333, 128), (150, 300, 64), (149, 256, 128)])
+def test_attention_persistent_items(felix, H, S, D):
+    # more (b, h) x query-group items than SMs: one CTA per SM strides over
+    # the items (ragged last query group, items not a multiple of the grid)
+    rows = np.r_[0, 1, S // 2, S - 2, S - 1]
+    _check(*_run(felix, 1, H, S, D, seed=H + S, rows=rows), ctx=f"persistent H={H} S={S} D={D}")
+
+
 def test_attention_custom_scale(felix):
     _check(*_run(felix, 1, 1, 300, 64, seed=5, scale=0.05), ctx="scale 0.05")
 

@@ -228,3 +228,35 @@ def test_hgemm_wide_pair_tiles(felix, M, N, K):
     from sion_b200.workloads import GemmConfig
     cfg = GemmConfig(f"wide_{M}x{N}x{K}", M, N, K, "f16", "nk", "uniform", 1.0, M + N)
     _full_size_check(felix, cfg, 256, 512)
+
+
+@pytest.mark.parametrize("M,N,K,nt,cta_pair", [(4608, 4608, 256, False, None),
+                                               (5120, 5120, 128, True, 1)])
+def test_hgemm_dynamic_tiles(felix, M, N, K, nt, cta_pair):
+    # four or more waves of whole tiles: tile ids handed out at run time by a
+    # global counter (CTA pairs with B stored K x N; single CTAs with pairs
+    # turned off). Sampled rows/columns against the fp64 oracle, the whole
+    # output against cuBLAS, bit-identical on a second call (the counter must
+    # be back at zero, and the tile-to-CTA assignment must not matter).
+    from metrics import fp16_ulp
+    g = torch.Generator().manual_seed(M + K)
+    A = (torch.rand(M, K, generator=g) * 2 - 1).half()
+    B = (torch.rand(*((N, K) if nt else (K, N)), generator=g) * 2 - 1).half()
+    dA, dB = A.cuda(), B.cuda()
+    lay = felix.B_NK if nt else felix.B_KN
+    outs = []
+    for _ in range(2):
+        C = torch.empty(M, N, dtype=torch.half, device="cuda")
+        felix.hgemm(dA, dB, C, b_layout=lay, cta_pair=cta_pair)
+        torch.cuda.synchronize()
+        outs.append(C)
+    assert torch.equal(outs[0], outs[1])
+    C = outs[0]
+    rows = _tile_samples(M, 256, 29)
+    Bnk = B if nt else B.t().contiguous()
+    ref = oracle.hgemm(A[rows].numpy(), Bnk.numpy(), True)
+    assert_fp16_close(ref, C[torch.from_numpy(rows).cuda()].cpu().numpy().astype(np.float64),
+                      ctx="dynamic tiles rows")
+    R = torch.matmul(dA.float(), (dB.float().t() if nt else dB.float()))
+    tol = torch.from_numpy(np.maximum(1e-2, 2 * fp16_ulp(R.cpu().numpy()))).cuda()
+    assert int(((C.float() - R).abs() > tol).sum()) == 0
