@@ -59,7 +59,7 @@ constexpr int kThreads = 192;
 // B/clk per SM from L2 against ~90 for 32 KB ones, and the pair needs ~63.
 template <int BN, int CG = 1, int SUB = (CG == 2 ? 2 : 1)>
 struct Cfg {
-  static_assert(CG == 1 || SUB == 2, "CTA pairs load two k-blocks per stage");
+  static_assert(CG == 1 || SUB == 2 || BN == 512, "CTA pairs load two k-blocks per stage");
   static constexpr int kBRows = BN / CG;  // B rows (N) loaded by one CTA
   // BN = 512 (CTA pairs only): two N = 256 MMAs per k step, each CTA holding
   // 128 B rows of each half; one accumulator (all 512 TMEM columns)
@@ -389,7 +389,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       // loads of a pair's CTAs complete on the leader's barrier
       auto load2d = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-        tma_load_2d(dst, map, bar, x, y);
+        if constexpr (CG == 2)
+          tma_load_2d_pair(dst, map, mapa_shared(smem_u32(bar), 0), x, y);
+        else
+          tma_load_2d(dst, map, bar, x, y);
       };
       // two-k-block stages: 3-D views (64-element inner, rows, 64-wide k-blocks
       // or n-chunks); a pair's loads complete on the leader's barrier
@@ -449,6 +452,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               load3d(sb, &tmB, &full[stage], n0, int(2 * kb));
             }
+          } else if constexpr (C_::kNH == 2) {
+            // 256 x 512 pair tiles, one 64-deep k-block per stage ("nt")
+            load2d(sa, &tmA, &full[stage], int(kb * BK), m0);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              load2d(sb + h * (C_::kBBytes / 2), &tmB, &full[stage], int(kb * BK),
+                     int(tn * BN + h * (BN / 2) + rank * C_::kBoxRows));
           } else {
             load2d(sa, &tmA, &full[stage], int(kb * BK), m0);
             if (p.b_mn_major) {
@@ -1028,12 +1038,15 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   // of 256 x 256 tiles; the kernel is power-capped at these sizes, so fewer
   // bytes means a higher clock: 16384^3 5.79 -> 5.59 ms under ncu (DRAM reads
   // 8.9 -> 7.0 GB, 1.30 -> 1.39 GHz), bench 5.67 -> 5.51 ms; 8192^3 697 -> 683 us.
+  // 256 x 512 tiles load one 64-deep k-block per stage (48 KB per CTA, four
+  // stages) rather than two (96 KB, two stages): 8192^3 676 vs 678 us.
+  constexpr int kWideSub = 1;
   bool wide = false;
   {
     const uint64_t wide_tiles = uint64_t((M + 255) / 256) * ((N + 511) / 512);
     if (pl.pair && !b_kn && o.block_n == 0 && o.stream_k == 0 && o.max_ctas == 0 &&
         o.cta_pair == 0 && wide_tiles >= 4u * uint64_t(dev->num_sms / 2)) {
-      pl = plan_for((M + 1) / 2, N, (K + 1) / 2, 512, o, dev->num_sms / 2);
+      pl = plan_for((M + 1) / 2, N, kWideSub == 2 ? (K + 1) / 2 : K, 512, o, dev->num_sms / 2);
       pl.pair = true;
       pl.sk_tiles = 0;
       pl.sk_iters = 0;
@@ -1062,14 +1075,11 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   }
   // 128-wide single-CTA tiles also take stages of two 64-deep k-blocks (32 KB
   // requests) when the view is exact: plan in 128-deep k-blocks
-#ifndef FELIX_HGEMM_SKINNY_SUB1
-#define FELIX_HGEMM_SKINNY_SUB1 0
-#endif
-  if (!pl.pair && pl.bn == 128 && sub2_ok && K >= 128 && !(FELIX_HGEMM_SKINNY_SUB1 && ksplit2)) {
+  if (!pl.pair && pl.bn == 128 && sub2_ok && K >= 128) {
     pl = plan_for(M, N, (K + 1) / 2, 128, o, dev->num_sms);
     pl.sub = 2;
   }
-  if (pl.pair) pl.sub = 2;
+  if (pl.pair) pl.sub = wide ? kWideSub : 2;
   if (ksplit2) {
     pl.ksplit2 = true;
     pl.sk_tiles = 0;
@@ -1094,7 +1104,8 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
     if (b_kn)
       rc = encode_tmap_2d_f16(&tmB, B, N, K, uint64_t(N) * 2, 64, BK);
     else
-      rc = encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK, pl.bn, kSwizzleK);
+      rc = encode_tmap_2d_f16_swizzle(&tmB, B, K, N, uint64_t(K) * 2, BK,
+                                      wide ? 128 : pl.bn, kSwizzleK);
     if (rc) return api_error("hgemm: cuTensorMapEncodeTiled(B) failed");
   }
   CUtensorMap tmC;
@@ -1148,12 +1159,13 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
 
   cudaError_t e;
   if (pl.pair) {
-    if ((rc = wide ? configure_once<512, 2>(dev->ordinal) : configure_once<256, 2>(dev->ordinal)))
+    if ((rc = wide ? configure_once<512, 2, kWideSub>(dev->ordinal)
+                   : configure_once<256, 2>(dev->ordinal)))
       return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * pl.grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = wide ? Cfg<512, 2>::kSmemBytes : Cfg<256, 2>::kSmemBytes;
+    cfg.dynamicSmemBytes = wide ? Cfg<512, 2, kWideSub>::kSmemBytes : Cfg<256, 2>::kSmemBytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1162,7 +1174,7 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = wide ? cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<512, 2>, tmA, tmB, tmC, p)
+    e = wide ? cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<512, 2, kWideSub>, tmA, tmB, tmC, p)
              : cudaLaunchKernelEx(&cfg, hgemm_persistent_kernel<256, 2>, tmA, tmB, tmC, p);
     if (e != cudaSuccess) return launch_error(e, "hgemm: CTA-pair launch failed");
     return FelixCode{FELIX_SUCCESS, cudaSuccess};
