@@ -1135,8 +1135,10 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   // DRAM for 1.07 GB of operands, and 8 ran 12 % faster than 16 (the kernel is
   // power-capped there: fewer DRAM bytes, higher clock); 8192^3: 707 vs 718 us.
   // Single-CTA 128 x 256 tiles (148 concurrent): 16 (8192^3: 763 vs 789 us).
-  // 256 x 512 pair tiles: 16 (16384^3: 5.51 vs 5.71 ms with 8).
-  p.group_m = wide ? 16u : (pl.pair ? 8u : 16u);
+  // 256 x 512 pair tiles (four 48 KB stages): 12. DRAM reads at 16384^3 for
+  // group 6 / 8 / 10 / 12 / 16 / 20 / 24 / 32: 9.2 / 8.5 / 8.6 / 8.3 / 10.4 /
+  // 12.0 / 13.3 / 16.3 GB; 12 and 8 ran fastest (5.49-5.67 ms median).
+  p.group_m = wide ? 12u : (pl.pair ? 8u : 16u);
   p.status = dev->status_word;
   p.ksplit2 = pl.ksplit2 ? 1u : 0u;
   p.pair = pl.pair ? 1u : 0u;
