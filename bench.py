@@ -381,7 +381,7 @@ def cpu_sample(cfg, budget_s: float = 10.0):
     if isinstance(cfg, W.AttnConfig):
         Q, K, V = W.attn_inputs(W.AttnConfig(cfg.name, 1, 1, cfg.S, cfg.D, cfg.seed))
         q, k, v = Q[0, 0].float(), K[0, 0].float(), V[0, 0].float()
-        rows = 1024
+        rows = min(1024, cfg.S)
         flops_per = 4.0 * rows * cfg.S * cfg.D
         def fn():
             s = (q[:rows] @ k.t()) / (cfg.D ** 0.5)
