@@ -32,7 +32,8 @@ enum WatchdogSite : unsigned {
   kWdAttnSoftmax = 9,
   kWdAttnCorrection = 10,
   kWdSmemAlign = 11,
-  kWdTileQueue = 12,  // HGEMM dynamic tile queue (producer push or consumer pop)  // dynamic shared memory not 1024-byte aligned: kernel did nothing
+  kWdTileQueue = 12,  // HGEMM dynamic tile queue (producer push or consumer pop)
+  kWdTopkLoad = 13,   // top-k: bulk copy of a staged slice  // dynamic shared memory not 1024-byte aligned: kernel did nothing
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -197,6 +198,17 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 // back: for scratch data that is dead after its last read.
 __device__ __forceinline__ void l2_discard_line(const void* p) {
   asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
+// Untiled bulk copy global -> shared memory of this CTA, completing on an
+// mbarrier (both addresses 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // ---------------------------------------------------------------- TMA

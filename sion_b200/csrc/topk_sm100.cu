@@ -25,6 +25,7 @@
 #include <cstdint>
 
 #include "felix_internal.h"
+#include "sm100_ptx.cuh"
 
 namespace felix_sm100 {
 namespace topk {
@@ -32,6 +33,8 @@ namespace topk {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr uint32_t kSmemKeys = 48 * 1024;  // staged keys per slice (192 KB)
+constexpr uint32_t kChunkBytes = 16 * 1024;  // bulk copies of a staged slice
+constexpr uint32_t kChunks = kSmemKeys * 4 / kChunkBytes;
 
 __device__ __forceinline__ uint32_t to_key(float v) {
   const uint32_t x = __float_as_uint(v);
@@ -84,35 +87,98 @@ __device__ __forceinline__ void pick_digit(const uint32_t* hist, uint32_t rank, 
 __global__ void __launch_bounds__(kThreads) select_per_slice_kernel(const float* __restrict__ data,
                                                                   float* __restrict__ out,
                                                                   uint32_t slice_size, uint32_t k,
-                                                                  int largest, int staged) {
-  extern __shared__ uint32_t keys[];                  // [slice_size] when staged
+                                                                  int largest, int staged,
+                                                                  unsigned* status) {
+  extern __shared__ __align__(16) uint32_t keys[];    // [slice_size] when staged
   __shared__ uint32_t hist[kWarps][256];
   __shared__ uint32_t merged[256];
   __shared__ uint32_t s_prefix, s_rank;
+  __shared__ __align__(8) uint64_t chunk_full[kChunks];
+  __shared__ int s_abort;
   const uint32_t t = threadIdx.x, w = t / 32;
   const float* src = data + size_t(blockIdx.x) * slice_size;
-  if (staged) {
-    for (uint32_t i = t; i < slice_size; i += kThreads) keys[i] = to_key(__ldg(src + i));
-  }
+  // sub-histograms: one per warp for large slices, fewer for small ones (each
+  // pass clears and merges them all)
+  const uint32_t nh = slice_size >= 16384 ? uint32_t(kWarps) : slice_size >= 4096 ? 4u : 1u;
+  uint32_t* my_hist = hist[w % nh];
+  // Staged and 16-byte aligned: the slice streams into shared memory as bulk
+  // copies of kChunkBytes, each completing on its own mbarrier, and the first
+  // pass converts and counts each chunk as soon as it lands (HBM read once,
+  // the load overlapped with the first histogram).
+  const bool bulk = staged && (slice_size & 3u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+  const uint32_t bytes = slice_size * 4u;
+  const uint32_t nchunks = bulk ? (bytes + kChunkBytes - 1) / kChunkBytes : 0u;
   if (t == 0) {
     s_prefix = 0;
     s_rank = largest ? slice_size - k : k - 1;
+    s_abort = 0;
+    for (uint32_t c = 0; c < nchunks; ++c) felix_sm100::mbar_init(&chunk_full[c], 1);
+    felix_sm100::fence_mbar_init();
+  }
+  for (uint32_t i = t; i < nh * 256; i += kThreads) (&hist[0][0])[i] = 0;
+  __syncthreads();
+  if (bulk) {
+    if (t == 0) {
+      for (uint32_t c = 0; c < nchunks; ++c) {
+        const uint32_t off = c * kChunkBytes;
+        const uint32_t len = bytes - off < kChunkBytes ? bytes - off : kChunkBytes;
+        felix_sm100::mbar_arrive_expect_tx(&chunk_full[c], len);
+        felix_sm100::bulk_load_1d(reinterpret_cast<uint8_t*>(keys) + off,
+                                  reinterpret_cast<const uint8_t*>(src) + off, len, &chunk_full[c]);
+      }
+    }
+    // pass 1 (top digit, every key counts) chunk by chunk as the copies land
+    bool ok = true;
+    for (uint32_t c = 0; c < nchunks; ++c) {
+      if (ok && !felix_sm100::mbar_wait(&chunk_full[c], 0, &s_abort, status,
+                                       felix_sm100::kWdTopkLoad))
+        ok = false;
+      const uint32_t beg = c * (kChunkBytes / 4);
+      const uint32_t end = min(slice_size, beg + kChunkBytes / 4);
+      if (ok) {
+        for (uint32_t i = beg + t; i < end; i += kThreads) {
+          const uint32_t key = to_key(__uint_as_float(keys[i]));
+          keys[i] = key;
+          atomicAdd(&my_hist[key >> 24], 1u);
+        }
+      }
+    }
+    ok = __syncthreads_and(ok) != 0;  // one decision for the whole CTA
+    if (!ok) {
+      // a copy never landed (watchdog recorded): wait (bounded) for the rest
+      // so that none is in flight when the CTA exits
+      if (t == 0) {
+        int dummy = 0;
+        for (uint32_t c = 0; c < nchunks; ++c)
+          felix_sm100::mbar_wait(&chunk_full[c], 0, &dummy, status, felix_sm100::kWdDrain,
+                                 100000000ull);
+      }
+      __syncthreads();
+      return;
+    }
+  } else if (staged) {
+    for (uint32_t i = t; i < slice_size; i += kThreads) keys[i] = to_key(__ldg(src + i));
   }
   uint32_t mask = 0;
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (uint32_t i = t; i < kWarps * 256; i += kThreads) (&hist[0][0])[i] = 0;
-    __syncthreads();
-    const uint32_t prefix = s_prefix;
-    for (uint32_t i = t; i < slice_size; i += kThreads) {
-      const uint32_t key = staged ? keys[i] : to_key(__ldg(src + i));
-      if ((key & mask) == prefix) atomicAdd(&hist[w][(key >> shift) & 255u], 1u);
+    if (pass > 0 || !bulk) {
+      if (pass > 0) {
+        for (uint32_t i = t; i < nh * 256; i += kThreads) (&hist[0][0])[i] = 0;
+      }
+      __syncthreads();
+      const uint32_t prefix = s_prefix;
+      for (uint32_t i = t; i < slice_size; i += kThreads) {
+        const uint32_t key = staged ? keys[i] : to_key(__ldg(src + i));
+        if ((key & mask) == prefix) atomicAdd(&my_hist[(key >> shift) & 255u], 1u);
+      }
     }
     __syncthreads();
+    const uint32_t prefix = s_prefix;
     for (uint32_t b = t; b < 256; b += kThreads) {
       uint32_t s = 0;
-#pragma unroll
-      for (int ww = 0; ww < kWarps; ++ww) s += hist[ww][b];
+      for (uint32_t ww = 0; ww < nh; ++ww) s += hist[ww][b];
       merged[b] = s;
     }
     __syncthreads();
@@ -128,6 +194,51 @@ __global__ void __launch_bounds__(kThreads) select_per_slice_kernel(const float*
     __syncthreads();
   }
   if (t == 0) out[blockIdx.x] = from_key(s_prefix);
+}
+
+// Small slices (<= kWarpKeys values): one warp per slice, the keys held in
+// registers (kWarpKeys / 32 per lane), a 256-bin histogram per warp in shared
+// memory and warp-level synchronisation only, so a CTA of kWarps warps selects
+// kWarps slices at once.
+constexpr uint32_t kWarpKeys = 2048;
+constexpr int kPerLane = kWarpKeys / 32;
+
+__global__ void __launch_bounds__(kThreads) select_warp_per_slice_kernel(
+    const float* __restrict__ data, float* __restrict__ out, uint32_t num_slices,
+    uint32_t slice_size, uint32_t k, int largest) {
+  __shared__ uint32_t hist[kWarps][256];
+  const uint32_t lane = threadIdx.x & 31u, w = threadIdx.x / 32;
+  const uint32_t slice = blockIdx.x * kWarps + w;
+  if (slice >= num_slices) return;  // whole warps only: no CTA-wide barrier below
+  const float* src = data + size_t(slice) * slice_size;
+  uint32_t key[kPerLane];
+#pragma unroll
+  for (int j = 0; j < kPerLane; ++j) {
+    const uint32_t i = uint32_t(j) * 32 + lane;  // coalesced across the warp
+    key[j] = i < slice_size ? to_key(__ldg(src + i)) : 0u;
+  }
+  uint32_t* h = hist[w];
+  uint32_t prefix = 0, mask = 0;
+  uint32_t rank = largest ? slice_size - k : k - 1;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) h[lane * 8 + b] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const uint32_t i = uint32_t(j) * 32 + lane;
+      if (i < slice_size && (key[j] & mask) == prefix) atomicAdd(&h[(key[j] >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    uint32_t d, below;
+    pick_digit(h, rank, d, below);
+    rank -= below;
+    prefix |= d << shift;
+    mask |= 255u << shift;
+    __syncwarp();
+  }
+  if (lane == 0) out[slice] = from_key(prefix);
 }
 
 // Grid-wide pass for few large slices: histogram of the digit at `shift` of
@@ -225,7 +336,11 @@ FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
   const bool grid_wide = num_slices < uint32_t(dev->num_sms) / 2 && slice_size >= (1u << 20) &&
                          num_slices <= 65535u;
   cudaError_t e;
-  if (!grid_wide) {
+  if (!grid_wide && slice_size <= kWarpKeys) {
+    const uint32_t blocks = (num_slices + kWarps - 1) / kWarps;
+    select_warp_per_slice_kernel<<<blocks, kThreads, 0, stream>>>(data, out, num_slices,
+                                                                  slice_size, k, largest ? 1 : 0);
+  } else if (!grid_wide) {
     const int staged = slice_size <= kSmemKeys ? 1 : 0;
     const size_t smem = staged ? size_t(slice_size) * 4 : 0;
     static PerDeviceOnce once;
@@ -236,8 +351,8 @@ FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
     });
     if (rc < 0) return api_error("topk: device ordinal");
     if (rc > 0) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    select_per_slice_kernel<<<num_slices, kThreads, smem, stream>>>(data, out, slice_size, k,
-                                                                    largest ? 1 : 0, staged);
+    select_per_slice_kernel<<<num_slices, kThreads, smem, stream>>>(
+        data, out, slice_size, k, largest ? 1 : 0, staged, dev->status_word);
   } else {
     const size_t need = kWsCounterBytes + size_t(num_slices) * (256 * 4 + sizeof(SliceState));
     uint8_t* ws = static_cast<uint8_t*>(library_workspace(dev, stream, need));

@@ -9,6 +9,12 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
+# Paths: <= 2048 values one warp per slice (keys in registers); up to 48K
+# values staged in shared memory, by bulk copies when the slice is 16-byte
+# aligned (n % 4 == 0) and by loads otherwise; larger slices read from global
+# memory every pass; few slices of >= 1M values the grid-wide passes.
+
+
 def _check(felix, x, k, largest):
     out = torch.empty(x.shape[0], device="cuda")
     felix.topk_select(torch.from_numpy(x).cuda(), out, k, largest)
@@ -19,6 +25,8 @@ def _check(felix, x, k, largest):
 
 @pytest.mark.parametrize("largest", [True, False])
 @pytest.mark.parametrize("ns,n,k", [(1, 1, 1), (7, 100, 1), (7, 100, 100), (300, 1000, 17),
+                                    (33, 2048, 2048), (17, 2049, 1000), (19, 2052, 1),
+                                    (40, 3001, 1500), (9, 32768, 16384), (5, 4096, 7),
                                     (64, 49152, 1000), (3, 49153, 5), (2, 200000, 77777)])
 def test_topk_random(felix, ns, n, k, largest):
     rng = np.random.default_rng(ns * 7 + n)
