@@ -137,10 +137,19 @@ __global__ void __launch_bounds__(kThreads) select_per_slice_kernel(const float*
       const uint32_t beg = c * (kChunkBytes / 4);
       const uint32_t end = min(slice_size, beg + kChunkBytes / 4);
       if (ok) {
-        for (uint32_t i = beg + t; i < end; i += kThreads) {
-          const uint32_t key = to_key(__uint_as_float(keys[i]));
-          keys[i] = key;
-          atomicAdd(&my_hist[key >> 24], 1u);
+        // 16-byte pieces (the chunk bounds are multiples of 4 keys here)
+        uint4* k4 = reinterpret_cast<uint4*>(keys);
+        for (uint32_t i = beg / 4 + t; i < end / 4; i += kThreads) {
+          uint4 v = k4[i];
+          v.x = to_key(__uint_as_float(v.x));
+          v.y = to_key(__uint_as_float(v.y));
+          v.z = to_key(__uint_as_float(v.z));
+          v.w = to_key(__uint_as_float(v.w));
+          k4[i] = v;
+          atomicAdd(&my_hist[v.x >> 24], 1u);
+          atomicAdd(&my_hist[v.y >> 24], 1u);
+          atomicAdd(&my_hist[v.z >> 24], 1u);
+          atomicAdd(&my_hist[v.w >> 24], 1u);
         }
       }
     }
@@ -169,9 +178,21 @@ __global__ void __launch_bounds__(kThreads) select_per_slice_kernel(const float*
       }
       __syncthreads();
       const uint32_t prefix = s_prefix;
-      for (uint32_t i = t; i < slice_size; i += kThreads) {
-        const uint32_t key = staged ? keys[i] : to_key(__ldg(src + i));
-        if ((key & mask) == prefix) atomicAdd(&my_hist[(key >> shift) & 255u], 1u);
+      if (bulk) {
+        // staged keys, 4 per 16-byte read
+        const uint4* k4 = reinterpret_cast<const uint4*>(keys);
+        for (uint32_t i = t; i < slice_size / 4; i += kThreads) {
+          const uint4 v = k4[i];
+          if ((v.x & mask) == prefix) atomicAdd(&my_hist[(v.x >> shift) & 255u], 1u);
+          if ((v.y & mask) == prefix) atomicAdd(&my_hist[(v.y >> shift) & 255u], 1u);
+          if ((v.z & mask) == prefix) atomicAdd(&my_hist[(v.z >> shift) & 255u], 1u);
+          if ((v.w & mask) == prefix) atomicAdd(&my_hist[(v.w >> shift) & 255u], 1u);
+        }
+      } else {
+        for (uint32_t i = t; i < slice_size; i += kThreads) {
+          const uint32_t key = staged ? keys[i] : to_key(__ldg(src + i));
+          if ((key & mask) == prefix) atomicAdd(&my_hist[(key >> shift) & 255u], 1u);
+        }
       }
     }
     __syncthreads();
