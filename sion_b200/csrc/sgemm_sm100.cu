@@ -39,10 +39,11 @@ namespace sgemm {
 __device__ unsigned long long g_sg_trace[1024][8];
 #define SG_TR(ev)                                                          \
   do {                                                                     \
-    if (threadIdx.x == 0 && blockIdx.x < 1024) {                           \
+    const unsigned b_ = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x; \
+    if (threadIdx.x == 0 && b_ < 1024) {                                   \
       unsigned long long t_;                                               \
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                \
-      g_sg_trace[blockIdx.x][ev] = t_;                                     \
+      g_sg_trace[b_][ev] = t_;                                             \
     }                                                                      \
   } while (0)
 #else
@@ -413,6 +414,42 @@ __device__ __forceinline__ void drain_tma(TmaPipe& q, const Params& p) {
   }
 }
 
+// Cluster split-K reduction: CTA `rank` of the (1, 1, S) cluster sums rows
+// [rank * 128 / S, (rank + 1) * 128 / S) of the S partial tiles parked at
+// red_addr in every CTA of the cluster, in rank order (deterministic), and
+// writes them to C. All S x U loads of a thread are issued before the first
+// sum, so the distributed-shared-memory latency is paid once, not per row.
+template <bool VEC, uint32_t S>
+__device__ __forceinline__ void csk_reduce(const Params& p, uint32_t m0, uint32_t n0,
+                                           uint32_t rank, uint32_t red_addr, bool ok) {
+  constexpr uint32_t kRows = BM / S, kF4 = kRows * (BN / 4), U = kF4 / kThreads;
+  static_assert(kF4 % kThreads == 0, "cluster reduction: whole float4s per thread");
+  const uint32_t t = threadIdx.x;
+  float4 x[U][S];
+#pragma unroll
+  for (uint32_t u = 0; u < U; ++u) {
+    const uint32_t f = t + u * kThreads;
+    const uint32_t off = ((rank * kRows + f / (BN / 4)) * BN + (f % (BN / 4)) * 4) * 4;
+#pragma unroll
+    for (uint32_t src = 0; src < S; ++src)
+      x[u][src] = felix_sm100::ld_shared_cluster_v4f(felix_sm100::mapa_shared(red_addr + off, src));
+  }
+#pragma unroll
+  for (uint32_t u = 0; u < U; ++u) {
+    const uint32_t f = t + u * kThreads;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (uint32_t src = 0; src < S; ++src) {
+      sum.x += x[u][src].x;
+      sum.y += x[u][src].y;
+      sum.z += x[u][src].z;
+      sum.w += x[u][src].w;
+    }
+    const float v[4] = {sum.x, sum.y, sum.z, sum.w};
+    if (ok) store_out<VEC>(p, m0 + rank * kRows + f / (BN / 4), n0 + (f % (BN / 4)) * 4, v);
+  }
+}
+
 // Stream-K: CTA of iteration x (iterations = tiles x k-tiles, split evenly).
 __device__ __forceinline__ uint32_t sk_cta_of(uint64_t x, uint32_t P, uint64_t I) {
   return static_cast<uint32_t>(((x + 1) * P - 1) / I);
@@ -539,6 +576,7 @@ __global__ void __launch_bounds__(kThreads, CSK ? 1 : FELIX_SGEMM_MINB)
   const uint32_t kbeg = z * p.k_per_split;
   const uint32_t kend = min(p.K, kbeg + p.k_per_split);
   const bool ok = run(m0, n0, kbeg, kend);
+  SG_TR(2);
   drain_tma<TMA>(q, p);
   // (a separate instantiation: the cluster epilogue in the same kernel as the
   // plain one changed the main loop's code and cost 16 % at 4096^3)
@@ -564,23 +602,15 @@ __global__ void __launch_bounds__(kThreads, CSK ? 1 : FELIX_SGEMM_MINB)
         }
       }
       felix_sm100::cluster_sync();
-      const uint32_t S = gridDim.z, rank = z;
-      const uint32_t rows = BM / S;
       const uint32_t red_addr = felix_sm100::smem_u32(red);
-      for (uint32_t f = t; f < rows * (BN / 4); f += kThreads) {
-        const uint32_t r = rank * rows + f / (BN / 4), c4 = f % (BN / 4);
-        const uint32_t off = (r * BN + c4 * 4) * 4;
-        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t src = 0; src < S; ++src) {
-          const float4 x = felix_sm100::ld_shared_cluster_v4f(felix_sm100::mapa_shared(red_addr + off, src));
-          sum.x += x.x;
-          sum.y += x.y;
-          sum.z += x.z;
-          sum.w += x.w;
-        }
-        const float v[4] = {sum.x, sum.y, sum.z, sum.w};
-        if (ok) store_out<VEC>(p, m0 + r, n0 + c4 * 4, v);
-      }
+      SG_TR(3);
+      if (gridDim.z == 2)
+        csk_reduce<VEC, 2>(p, m0, n0, z, red_addr, ok);
+      else if (gridDim.z == 4)
+        csk_reduce<VEC, 4>(p, m0, n0, z, red_addr, ok);
+      else
+        csk_reduce<VEC, 8>(p, m0, n0, z, red_addr, ok);
+      SG_TR(4);
       felix_sm100::cluster_sync();  // no CTA exits while another reads its ring
       return;
     }
