@@ -299,6 +299,20 @@ __device__ __forceinline__ void store_row_chunk(const Params& p, uint32_t row, u
   }
 }
 
+#ifdef FELIX_HGEMM_TRACE
+// Development-only per-CTA timeline (compiled out of the library build):
+// [cta][event] = globaltimer ns.
+__device__ unsigned long long g_hg_trace[1024][12];
+#define HG_TR(ev)                                                   \
+  do {                                                              \
+    if (blockIdx.x < 1024) g_hg_trace[blockIdx.x][ev] = globaltimer_ns(); \
+  } while (0)
+#else
+#define HG_TR(ev) \
+  do {            \
+  } while (0)
+#endif
+
 template <int BN, int CG = 1, int SUB = (CG == 2 ? 2 : 1)>
 __global__ void __launch_bounds__(kThreads, 1)
     hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -377,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) HG_TR(0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -476,6 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      HG_TR(9);
       // Drain: wait (bounded) for the last fill of every stage so that no TMA
       // write is in flight when the CTA exits (a pair's leader counts both
       // CTAs' bytes; the final cluster barrier holds the peer until then).
@@ -543,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (lane == 0 && i == 0 && kb == u.kb0) HG_TR(1);
           tc_fence_after();
           if (elect_one()) {
             const uint32_t a0 = smem_u32(ring + stage * C_::kStageBytes);
@@ -594,6 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         if (elect_one()) commit_all(&tfull[buf]);
+        if (lane == 0) HG_TR(2);
         __syncwarp();
         ++i;
       }
@@ -652,10 +670,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // and TMA-stores. Both directions run at once: half the bytes each
         // way and half the columns per CTA, against one CTA sending 128.
         const uint32_t me = u.seg, peer = me ^ 1u;
+        if (epi_tid == 0) HG_TR(3);
         // tfull: every MMA of this CTA has completed, so its ring is idle
         // (nothing more is loaded: this is the CTA's only unit)
         if (epi_tid == 0) mbar_arrive_cluster(mapa_shared(smem_u32(ring_free), peer));
         if (!mbar_wait_cluster(ring_free, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
+        if (epi_tid == 0) HG_TR(4);
         const uint32_t rbuf = mapa_shared(smem_u32(recv_buf), peer);
 #pragma unroll 1
         for (int c = 0; c < 64; c += 32) {
@@ -667,8 +687,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             st_shared_cluster_v4(rbuf + partial_index(c / 32, j, row_in_tile) * 16, r[4 * j],
                                  r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
         }
+        if (epi_tid == 0) HG_TR(5);
         mbar_arrive_cluster(mapa_shared(smem_u32(recv), peer));
         if (!mbar_wait_cluster(recv, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
+        if (epi_tid == 0) HG_TR(6);
         const float4* r4 = reinterpret_cast<const float4*>(recv_buf);
         uint8_t* stg = staging + (warp - 2) * 8192;
         {
@@ -707,6 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_store_2d(&tmC, buf, int(col0 + c), int(row0 + q * 32));
             bulk_commit_group();
           }
+          if (epi_tid == 0) HG_TR(7);
         }
       } else if (!u.partial && p.tma_store) {
         // 64-column chunks: TMEM -> registers -> fp16 -> 128-byte-swizzled
@@ -837,6 +860,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // staging smem must stay valid until the TMA stores have read it
     if (lane == 0) bulk_wait_group<0>();
+    if (epi_tid == 0) HG_TR(10);
     __syncwarp();
   }
 
@@ -855,6 +879,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicExch(p.ws_dyn + 1, 0u);
     }
   }
+  if (threadIdx.x == 64) HG_TR(8);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -867,6 +892,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace hgemm
 }  // namespace felix_sm100
+
+#ifdef FELIX_HGEMM_TRACE
+extern "C" void hg_trace_fetch(void* dst) {
+  cudaMemcpyFromSymbol(dst, felix_sm100::hgemm::g_hg_trace, sizeof(felix_sm100::hgemm::g_hg_trace));
+}
+#endif
 
 // ============================================================ host launcher
 namespace felix_impl {

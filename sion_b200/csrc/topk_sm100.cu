@@ -12,17 +12,20 @@
 // Design (HBM-bound integer work, no tensor cores):
 //   * the k-th largest is the (n - k)-th smallest (0-based rank), so one
 //     ascending select serves both directions;
-//   * four passes over 8-bit digits, most significant first; each pass builds
-//     a 256-bin histogram of the keys that still match the chosen prefix and
-//     picks the digit where the running count passes the rank;
+//   * radix passes, most significant digit first; each pass builds a
+//     histogram of the keys that still match the chosen prefix and picks the
+//     digit where the running count passes the rank;
 //   * many slices: one CTA per slice; slices up to 48K values are staged once
-//     into shared memory (so HBM is read once), per-warp sub-histograms limit
-//     atomic contention;
+//     into shared memory (so HBM is read once). Aligned staged slices take
+//     three passes (11-, 11- and 10-bit digits), the third over a compacted
+//     list of candidates only; the others four 8-bit passes with per-warp
+//     sub-histograms against atomic contention;
 //   * few large slices: every pass is a grid-wide histogram kernel over all
 //     SMs plus a one-warp digit pick per slice, with the histograms and the
 //     per-slice (prefix, rank) state in library scratch.
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "felix_internal.h"
 #include "sm100_ptx.cuh"
@@ -217,6 +220,244 @@ __global__ void __launch_bounds__(kThreads) select_per_slice_kernel(const float*
   if (t == 0) out[blockIdx.x] = from_key(s_prefix);
 }
 
+// Staged slices that are 16-byte aligned (n % 4 == 0): three passes over
+// 11-, 11- and 10-bit digits instead of four over 8-bit ones, and only the
+// first two over the whole slice. Pass 1 converts and counts the top 11 bits
+// of each bulk-copied chunk as it lands; pass 2 reads the staged keys once
+// more, counts the next 11 bits of the keys whose top digit matches and
+// appends those keys to a candidate list behind the slice in shared memory
+// (each warp its own region, positions from ballots: no atomics); pass 3
+// counts the last 10 bits over the candidates only, or over the staged keys
+// again when the list overflowed (many equal top digits). Digits are picked
+// by the whole CTA (a block-wide scan of the 2048 counts).
+#ifdef FELIX_TOPK_TRACE
+// Development-only per-CTA timeline (compiled out of the library build).
+__device__ unsigned long long g_tk_trace[8192][8];
+#define TK_TR(ev)                                                             \
+  do {                                                                        \
+    if (threadIdx.x == 0 && blockIdx.x < 8192)                                \
+      g_tk_trace[blockIdx.x][ev] = felix_sm100::globaltimer_ns();             \
+  } while (0)
+#else
+#define TK_TR(ev) \
+  do {            \
+  } while (0)
+#endif
+constexpr uint32_t kBins = 2048;
+constexpr uint32_t kSubH = 2;  // sub-histograms (warp w counts into w % kSubH)
+// dynamic shared memory of the staged kernel: the slice plus the candidates
+// (with the static part, 16.2 KB, within the 227 KB per-CTA limit)
+constexpr uint32_t kStagedDynBytes = 210 * 1024;
+
+// Digit whose cumulative count first exceeds `rank` among nbins counts (a
+// multiple of kThreads, at most 4 per thread); called by every thread of the
+// CTA. s_out[0] = the digit, s_out[1] = the count of keys below it, both
+// visible to every thread on return.
+__device__ __forceinline__ void pick_digit_cta(const uint32_t* h, uint32_t nbins, uint32_t rank,
+                                               uint32_t* wsum, uint32_t* s_out) {
+  const uint32_t t = threadIdx.x, lane = t & 31u, w = t >> 5;
+  const uint32_t per = nbins / kThreads;
+  uint32_t c[4], sum = 0;
+#pragma unroll
+  for (uint32_t i = 0; i < 4; ++i) {
+    c[i] = i < per ? h[t * per + i] : 0u;
+    sum += c[i];
+  }
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= uint32_t(o)) incl += v;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  uint32_t off = 0;
+  for (uint32_t ww = 0; ww < w; ++ww) off += wsum[ww];
+  const uint32_t excl = off + incl - sum;
+  if (rank >= excl && rank < excl + sum) {
+    uint32_t run = excl;
+    for (uint32_t i = 0; i < per; ++i) {
+      if (rank < run + c[i]) {
+        s_out[0] = t * per + i;
+        s_out[1] = run;
+        break;
+      }
+      run += c[i];
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads, 4) select_staged_kernel(const float* __restrict__ data,
+                                                                float* __restrict__ out,
+                                                                uint32_t slice_size, uint32_t k,
+                                                                int largest, uint32_t cap,
+                                                                unsigned* status) {
+  extern __shared__ __align__(16) uint32_t dyn[];  // [slice_size] keys, then [cap] candidates
+  __shared__ uint32_t hist[kSubH][kBins];
+  __shared__ uint32_t wsum[kWarps], s_pick[2], s_wcount[kWarps];
+  __shared__ __align__(8) uint64_t chunk_full[kChunks];
+  __shared__ int s_abort;
+  const uint32_t t = threadIdx.x, w = t / 32, lane = t % 32;
+  uint32_t* keys = dyn;
+  uint32_t* cand = dyn + slice_size;
+  uint32_t* my_hist = hist[w % kSubH];
+  const float* src = data + size_t(blockIdx.x) * slice_size;
+  const uint32_t bytes = slice_size * 4u;
+  const uint32_t nchunks = (bytes + kChunkBytes - 1) / kChunkBytes;
+  auto clear_hist = [&]() {
+    for (uint32_t i = t; i < kSubH * kBins; i += kThreads) (&hist[0][0])[i] = 0;
+  };
+  auto merge_hist = [&](uint32_t nbins) {
+    for (uint32_t b = t; b < nbins; b += kThreads) {
+      uint32_t v = hist[0][b];
+#pragma unroll
+      for (uint32_t h = 1; h < kSubH; ++h) v += hist[h][b];
+      hist[0][b] = v;
+    }
+  };
+  TK_TR(0);
+  if (t == 0) {
+    s_abort = 0;
+    for (uint32_t c = 0; c < nchunks; ++c) felix_sm100::mbar_init(&chunk_full[c], 1);
+    felix_sm100::fence_mbar_init();
+  }
+  clear_hist();
+  __syncthreads();
+  if (t == 0) {
+    for (uint32_t c = 0; c < nchunks; ++c) {
+      const uint32_t off = c * kChunkBytes;
+      const uint32_t len = bytes - off < kChunkBytes ? bytes - off : kChunkBytes;
+      felix_sm100::mbar_arrive_expect_tx(&chunk_full[c], len);
+      felix_sm100::bulk_load_1d(reinterpret_cast<uint8_t*>(keys) + off,
+                                reinterpret_cast<const uint8_t*>(src) + off, len, &chunk_full[c]);
+    }
+  }
+  // pass 1: convert each chunk in place as it lands and count the top 11 bits
+  bool ok = true;
+  uint4* k4 = reinterpret_cast<uint4*>(keys);
+  for (uint32_t c = 0; c < nchunks; ++c) {
+    if (ok && !felix_sm100::mbar_wait(&chunk_full[c], 0, &s_abort, status,
+                                     felix_sm100::kWdTopkLoad))
+      ok = false;
+    const uint32_t beg = c * (kChunkBytes / 16);
+    const uint32_t end = min(slice_size / 4, beg + kChunkBytes / 16);
+    if (ok) {
+      for (uint32_t i = beg + t; i < end; i += kThreads) {
+        uint4 v = k4[i];
+        v.x = to_key(__uint_as_float(v.x));
+        v.y = to_key(__uint_as_float(v.y));
+        v.z = to_key(__uint_as_float(v.z));
+        v.w = to_key(__uint_as_float(v.w));
+        k4[i] = v;
+        atomicAdd(&my_hist[v.x >> 21], 1u);
+        atomicAdd(&my_hist[v.y >> 21], 1u);
+        atomicAdd(&my_hist[v.z >> 21], 1u);
+        atomicAdd(&my_hist[v.w >> 21], 1u);
+      }
+    }
+  }
+  ok = __syncthreads_and(ok) != 0;
+  if (!ok) {
+    // a copy never landed (watchdog recorded): wait (bounded) for the rest so
+    // that none is in flight when the CTA exits
+    if (t == 0) {
+      int dummy = 0;
+      for (uint32_t c = 0; c < nchunks; ++c)
+        felix_sm100::mbar_wait(&chunk_full[c], 0, &dummy, status, felix_sm100::kWdDrain,
+                               100000000ull);
+    }
+    __syncthreads();
+    return;
+  }
+  TK_TR(1);
+  merge_hist(kBins);
+  __syncthreads();
+  uint32_t rank = largest ? slice_size - k : k - 1;
+  pick_digit_cta(hist[0], kBins, rank, wsum, s_pick);
+  const uint32_t d1 = s_pick[0];
+  rank -= s_pick[1];
+  clear_hist();
+  __syncthreads();
+  TK_TR(2);
+  // pass 2: count bits 20..10 of the keys with top digit d1 and collect them,
+  // warp w into cand[w * region ..), positions from ballots
+  const uint32_t n4 = slice_size / 4;
+  const uint32_t n4w = (n4 + 31u) & ~31u;  // whole warps take part in the ballots
+  const uint32_t region = cap / kWarps;
+  uint32_t* my_cand = cand + w * region;
+  const uint32_t lt = (1u << lane) - 1u;
+  uint32_t wn = 0;  // candidates of this warp so far (same in every lane)
+  // U 16-byte groups per thread and step, loaded before any candidate is
+  // stored (the stores could otherwise alias the loads and serialise them);
+  // U = 4 for long slices, 1 for short ones (fewer idle ballots)
+  auto compact = [&](auto unroll) {
+    constexpr int U = decltype(unroll)::value;
+    for (uint32_t i0 = t; i0 < n4w; i0 += U * kThreads) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t i = i0 + u * kThreads;
+        v[u] = i < n4 ? k4[i] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t i = i0 + u * kThreads;
+        const uint32_t kk[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const bool match = i < n4 && (kk[j] >> 21) == d1;
+          const uint32_t b = __ballot_sync(0xffffffffu, match);
+          if (match) {
+            atomicAdd(&my_hist[(kk[j] >> 10) & (kBins - 1)], 1u);
+            const uint32_t pos = wn + __popc(b & lt);
+            if (pos < region) my_cand[pos] = kk[j];
+          }
+          wn += __popc(b);
+        }
+      }
+    }
+  };
+  if (n4 >= 8 * kThreads)
+    compact(std::integral_constant<int, 4>{});
+  else
+    compact(std::integral_constant<int, 1>{});
+  if (lane == 0) s_wcount[w] = wn;
+  __syncthreads();
+  TK_TR(3);
+  merge_hist(kBins);
+  __syncthreads();
+  pick_digit_cta(hist[0], kBins, rank, wsum, s_pick);
+  const uint32_t prefix22 = (d1 << 11) | s_pick[0];
+  rank -= s_pick[1];
+  clear_hist();
+  __syncthreads();
+  // pass 3: the last 10 bits of the keys whose top 22 bits match
+  bool fits = true;
+  for (uint32_t ww = 0; ww < kWarps; ++ww) fits = fits && s_wcount[ww] <= region;
+  if (fits) {
+    // each warp its own region
+    for (uint32_t i = lane; i < wn; i += 32) {
+      const uint32_t key = my_cand[i];
+      if ((key >> 10) == prefix22) atomicAdd(&my_hist[key & 1023u], 1u);
+    }
+  } else {
+    for (uint32_t i = t; i < n4; i += kThreads) {
+      const uint4 v = k4[i];
+      if ((v.x >> 10) == prefix22) atomicAdd(&my_hist[v.x & 1023u], 1u);
+      if ((v.y >> 10) == prefix22) atomicAdd(&my_hist[v.y & 1023u], 1u);
+      if ((v.z >> 10) == prefix22) atomicAdd(&my_hist[v.z & 1023u], 1u);
+      if ((v.w >> 10) == prefix22) atomicAdd(&my_hist[v.w & 1023u], 1u);
+    }
+  }
+  __syncthreads();
+  merge_hist(1024);
+  __syncthreads();
+  pick_digit_cta(hist[0], 1024, rank, wsum, s_pick);
+  if (t == 0) out[blockIdx.x] = from_key((prefix22 << 10) | s_pick[0]);
+  TK_TR(4);
+}
+
 // Small slices (<= kWarpKeys values): one warp per slice, the keys held in
 // registers (kWarpKeys / 32 per lane), a 256-bin histogram per warp in shared
 // memory and warp-level synchronisation only, so a CTA of kWarps warps selects
@@ -336,6 +577,12 @@ __global__ void init_state_kernel(SliceState* state, uint32_t num_slices, uint32
 }  // namespace topk
 }  // namespace felix_sm100
 
+#ifdef FELIX_TOPK_TRACE
+extern "C" void tk_trace_fetch(void* dst) {
+  cudaMemcpyFromSymbol(dst, felix_sm100::topk::g_tk_trace, sizeof(felix_sm100::topk::g_tk_trace));
+}
+#endif
+
 namespace felix_impl {
 
 using namespace felix_sm100::topk;
@@ -361,6 +608,22 @@ FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
     const uint32_t blocks = (num_slices + kWarps - 1) / kWarps;
     select_warp_per_slice_kernel<<<blocks, kThreads, 0, stream>>>(data, out, num_slices,
                                                                   slice_size, k, largest ? 1 : 0);
+  } else if (!grid_wide && slice_size <= kSmemKeys && (slice_size & 3u) == 0 &&
+             (reinterpret_cast<uintptr_t>(data) & 15u) == 0) {
+    // staged, bulk-copied: candidates after the slice, at most half its size
+    const uint32_t room = (kStagedDynBytes - slice_size * 4u) / 4u;
+    const uint32_t cap = min(slice_size / 2, room);
+    const size_t smem = size_t(slice_size + cap) * 4;
+    static PerDeviceOnce once_staged;
+    const int rc = once_staged.run(dev->ordinal, [] {
+      return int(cudaFuncSetAttribute(select_staged_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(kStagedDynBytes)));
+    });
+    if (rc < 0) return api_error("topk: device ordinal");
+    if (rc > 0) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    select_staged_kernel<<<num_slices, kThreads, smem, stream>>>(
+        data, out, slice_size, k, largest ? 1 : 0, cap, dev->status_word);
   } else if (!grid_wide) {
     const int staged = slice_size <= kSmemKeys ? 1 : 0;
     const size_t smem = staged ? size_t(slice_size) * 4 : 0;

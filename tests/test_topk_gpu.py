@@ -64,3 +64,25 @@ def test_topk_argument_errors(felix):
         with pytest.raises(felix.FelixError) as e:
             felix.topk_select(x, out, k)
         assert e.value.code == felix.API_ERROR
+
+
+@pytest.mark.parametrize("largest", [True, False])
+def test_topk_staged_candidate_overflow_in_one_warp(felix, largest):
+    # Aligned staged slices collect the keys whose top digit matches into one
+    # candidate region per warp; here every such key sits in the 16-byte
+    # groups that warp 0 reads (group g goes to warp (g % 512) // 32), so that
+    # region overflows while the slice as a whole has few candidates, and the
+    # last pass must fall back to the staged keys.
+    rng = np.random.default_rng(11)
+    n = 32768
+    x = np.where(rng.random((3, n)) < 0.5, -100.0, 100.0).astype(np.float32)
+    groups = np.arange(n) // 4
+    warp0 = (groups % 512) // 32 == 0
+    x[:, warp0] = (1.0 + rng.random((3, int(warp0.sum()))) * 0.5).astype(np.float32)
+    m = int(warp0.sum())
+    big = int((x[0] > 50).sum())
+    for k in (big + 1, big + m // 2, big + m):
+        _check(felix, x[:1], k, True)
+    small = int((x[1] < -50).sum())
+    _check(felix, x[1:2], small + 7, False)
+    _check(felix, x, n // 2, largest)
