@@ -244,6 +244,7 @@ __device__ unsigned long long g_tk_trace[8192][8];
   } while (0)
 #endif
 constexpr uint32_t kBins = 2048;
+constexpr uint32_t kL2MinKeys = 8192;  // unstaged three-pass select from this slice size
 constexpr uint32_t kSubH = 2;  // sub-histograms (warp w counts into w % kSubH)
 // dynamic shared memory of the staged kernel: the slice plus the candidates
 // (with the static part, 16.2 KB, within the 227 KB per-CTA limit)
@@ -288,23 +289,46 @@ __device__ __forceinline__ void pick_digit_cta(const uint32_t* h, uint32_t nbins
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kThreads, 4) select_staged_kernel(const float* __restrict__ data,
-                                                                float* __restrict__ out,
-                                                                uint32_t slice_size, uint32_t k,
-                                                                int largest, uint32_t cap,
-                                                                unsigned* status) {
-  extern __shared__ __align__(16) uint32_t dyn[];  // [slice_size] keys, then [cap] candidates
+// STAGED = false: the same three passes without staging. Pass 1 streams the
+// slice from HBM, passes 2 (and 3 when the candidates overflow) read it again
+// through the L2, which still holds it: shared memory then holds only the
+// histograms and the candidates, so several CTAs share an SM and their loads
+// overlap each other's passes.
+template <bool STAGED>
+__global__ void __launch_bounds__(kThreads, 4) select_radix3_kernel(const float* __restrict__ data,
+                                                                 float* __restrict__ out,
+                                                                 uint32_t slice_size, uint32_t k,
+                                                                 int largest, uint32_t cap,
+                                                                 unsigned* status) {
+  // staged: [slice_size] keys, then [cap] candidates; otherwise the candidates
+  extern __shared__ __align__(16) uint32_t dyn[];
   __shared__ uint32_t hist[kSubH][kBins];
   __shared__ uint32_t wsum[kWarps], s_pick[2], s_wcount[kWarps];
   __shared__ __align__(8) uint64_t chunk_full[kChunks];
   __shared__ int s_abort;
   const uint32_t t = threadIdx.x, w = t / 32, lane = t % 32;
   uint32_t* keys = dyn;
-  uint32_t* cand = dyn + slice_size;
+  uint32_t* cand = STAGED ? dyn + slice_size : dyn;
   uint32_t* my_hist = hist[w % kSubH];
   const float* src = data + size_t(blockIdx.x) * slice_size;
   const uint32_t bytes = slice_size * 4u;
-  const uint32_t nchunks = (bytes + kChunkBytes - 1) / kChunkBytes;
+  const uint32_t nchunks = STAGED ? (bytes + kChunkBytes - 1) / kChunkBytes : 0u;
+  const uint4* g4 = reinterpret_cast<const uint4*>(src);
+  uint4* k4 = reinterpret_cast<uint4*>(keys);
+  const uint32_t n4 = slice_size / 4;
+  // four keys of 16-byte group i (converted)
+  auto load4 = [&](uint32_t i) -> uint4 {
+    if constexpr (STAGED) {
+      return k4[i];
+    } else {
+      uint4 v = __ldcg(g4 + i);
+      v.x = to_key(__uint_as_float(v.x));
+      v.y = to_key(__uint_as_float(v.y));
+      v.z = to_key(__uint_as_float(v.z));
+      v.w = to_key(__uint_as_float(v.w));
+      return v;
+    }
+  };
   auto clear_hist = [&]() {
     for (uint32_t i = t; i < kSubH * kBins; i += kThreads) (&hist[0][0])[i] = 0;
   };
@@ -334,8 +358,27 @@ __global__ void __launch_bounds__(kThreads, 4) select_staged_kernel(const float*
     }
   }
   // pass 1: convert each chunk in place as it lands and count the top 11 bits
+  // (unstaged: stream the slice, four 16-byte loads in flight per thread)
   bool ok = true;
-  uint4* k4 = reinterpret_cast<uint4*>(keys);
+  if constexpr (!STAGED) {
+    for (uint32_t i0 = t; i0 < n4; i0 += 4 * kThreads) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t i = i0 + u * kThreads;
+        if (i < n4) v[u] = __ldcg(g4 + i);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (i0 + u * kThreads < n4) {
+          atomicAdd(&my_hist[to_key(__uint_as_float(v[u].x)) >> 21], 1u);
+          atomicAdd(&my_hist[to_key(__uint_as_float(v[u].y)) >> 21], 1u);
+          atomicAdd(&my_hist[to_key(__uint_as_float(v[u].z)) >> 21], 1u);
+          atomicAdd(&my_hist[to_key(__uint_as_float(v[u].w)) >> 21], 1u);
+        }
+      }
+    }
+  }
   for (uint32_t c = 0; c < nchunks; ++c) {
     if (ok && !felix_sm100::mbar_wait(&chunk_full[c], 0, &s_abort, status,
                                      felix_sm100::kWdTopkLoad))
@@ -382,7 +425,6 @@ __global__ void __launch_bounds__(kThreads, 4) select_staged_kernel(const float*
   TK_TR(2);
   // pass 2: count bits 20..10 of the keys with top digit d1 and collect them,
   // warp w into cand[w * region ..), positions from ballots
-  const uint32_t n4 = slice_size / 4;
   const uint32_t n4w = (n4 + 31u) & ~31u;  // whole warps take part in the ballots
   const uint32_t region = cap / kWarps;
   uint32_t* my_cand = cand + w * region;
@@ -398,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 4) select_staged_kernel(const float*
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const uint32_t i = i0 + u * kThreads;
-        v[u] = i < n4 ? k4[i] : make_uint4(0u, 0u, 0u, 0u);
+        v[u] = i < n4 ? load4(i) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -443,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 4) select_staged_kernel(const float*
     }
   } else {
     for (uint32_t i = t; i < n4; i += kThreads) {
-      const uint4 v = k4[i];
+      const uint4 v = load4(i);
       if ((v.x >> 10) == prefix22) atomicAdd(&my_hist[v.x & 1023u], 1u);
       if ((v.y >> 10) == prefix22) atomicAdd(&my_hist[v.y & 1023u], 1u);
       if ((v.z >> 10) == prefix22) atomicAdd(&my_hist[v.z & 1023u], 1u);
@@ -608,6 +650,23 @@ FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
     const uint32_t blocks = (num_slices + kWarps - 1) / kWarps;
     select_warp_per_slice_kernel<<<blocks, kThreads, 0, stream>>>(data, out, num_slices,
                                                                   slice_size, k, largest ? 1 : 0);
+  } else if (!grid_wide && slice_size >= kL2MinKeys && (slice_size & 3u) == 0 &&
+             (reinterpret_cast<uintptr_t>(data) & 15u) == 0) {
+    // aligned slices of 8K values and more: unstaged, re-read through the L2
+    // (4096 x 32768: 354 us staged, 234 us this way; 512 x 200000: 1190 us
+    // with four passes from global memory, 242 us)
+    const uint32_t cap = min(slice_size / 2, 8192u);
+    const size_t smem = size_t(cap) * 4;
+    static PerDeviceOnce once_l2;
+    const int rc = once_l2.run(dev->ordinal, [] {
+      return int(cudaFuncSetAttribute(select_radix3_kernel<false>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(kStagedDynBytes)));
+    });
+    if (rc < 0) return api_error("topk: device ordinal");
+    if (rc > 0) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
+    select_radix3_kernel<false><<<num_slices, kThreads, smem, stream>>>(
+        data, out, slice_size, k, largest ? 1 : 0, cap, dev->status_word);
   } else if (!grid_wide && slice_size <= kSmemKeys && (slice_size & 3u) == 0 &&
              (reinterpret_cast<uintptr_t>(data) & 15u) == 0) {
     // staged, bulk-copied: candidates after the slice, at most half its size
@@ -616,13 +675,13 @@ FelixCode topk_select_launch(const float* data, float* out, uint32_t num_slices,
     const size_t smem = size_t(slice_size + cap) * 4;
     static PerDeviceOnce once_staged;
     const int rc = once_staged.run(dev->ordinal, [] {
-      return int(cudaFuncSetAttribute(select_staged_kernel,
+      return int(cudaFuncSetAttribute(select_radix3_kernel<true>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       int(kStagedDynBytes)));
     });
     if (rc < 0) return api_error("topk: device ordinal");
     if (rc > 0) return FelixCode{FELIX_API_ERROR, cudaError_t(rc)};
-    select_staged_kernel<<<num_slices, kThreads, smem, stream>>>(
+    select_radix3_kernel<true><<<num_slices, kThreads, smem, stream>>>(
         data, out, slice_size, k, largest ? 1 : 0, cap, dev->status_word);
   } else if (!grid_wide) {
     const int staged = slice_size <= kSmemKeys ? 1 : 0;

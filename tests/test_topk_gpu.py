@@ -9,10 +9,12 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-# Paths: <= 2048 values one warp per slice (keys in registers); up to 48K
-# values staged in shared memory, by bulk copies when the slice is 16-byte
-# aligned (n % 4 == 0) and by loads otherwise; larger slices read from global
-# memory every pass; few slices of >= 1M values the grid-wide passes.
+# Paths: <= 2048 values one warp per slice (keys in registers); aligned
+# slices (n % 4 == 0) below 8K values staged in shared memory by bulk copies,
+# from 8K values on read from HBM and again through the L2 (three passes,
+# candidate lists); other slices up to 48K values staged by loads, larger
+# ones read from global memory every pass; few slices of >= 1M values the
+# grid-wide passes.
 
 
 def _check(felix, x, k, largest):
@@ -27,7 +29,9 @@ def _check(felix, x, k, largest):
 @pytest.mark.parametrize("ns,n,k", [(1, 1, 1), (7, 100, 1), (7, 100, 100), (300, 1000, 17),
                                     (33, 2048, 2048), (17, 2049, 1000), (19, 2052, 1),
                                     (40, 3001, 1500), (9, 32768, 16384), (5, 4096, 7),
-                                    (64, 49152, 1000), (3, 49153, 5), (2, 200000, 77777)])
+                                    (6, 8188, 4000), (6, 8192, 1),
+                                    (64, 49152, 1000), (3, 49153, 5), (2, 200000, 77777),
+                                    (2, 200003, 100000)])
 def test_topk_random(felix, ns, n, k, largest):
     rng = np.random.default_rng(ns * 7 + n)
     _check(felix, rng.standard_normal((ns, n)).astype(np.float32), k, largest)
@@ -67,14 +71,15 @@ def test_topk_argument_errors(felix):
 
 
 @pytest.mark.parametrize("largest", [True, False])
-def test_topk_staged_candidate_overflow_in_one_warp(felix, largest):
-    # Aligned staged slices collect the keys whose top digit matches into one
-    # candidate region per warp; here every such key sits in the 16-byte
-    # groups that warp 0 reads (group g goes to warp (g % 512) // 32), so that
-    # region overflows while the slice as a whole has few candidates, and the
-    # last pass must fall back to the staged keys.
+@pytest.mark.parametrize("n", [4096, 32768])
+def test_topk_candidate_overflow_in_one_warp(felix, n, largest):
+    # Aligned slices (staged below 8K values, re-read through the L2 from 8K
+    # on) collect the keys whose top digit matches into one candidate region
+    # per warp; here every such key sits in the 16-byte groups that warp 0
+    # reads (group g goes to warp (g % 512) // 32), so that region overflows
+    # while the slice as a whole has few candidates, and the last pass must
+    # fall back to reading every key again.
     rng = np.random.default_rng(11)
-    n = 32768
     x = np.where(rng.random((3, n)) < 0.5, -100.0, 100.0).astype(np.float32)
     groups = np.arange(n) // 4
     warp0 = (groups % 512) // 32 == 0
