@@ -44,6 +44,11 @@ __device__ __forceinline__ uint32_t to_key(float v) {
   if (v != v) return 0xffffffffu;  // NaN above everything
   return x ^ ((x & 0x80000000u) ? 0xffffffffu : 0x80000000u);
 }
+// The same map on the value's bits, integer operations only.
+__device__ __forceinline__ uint32_t to_key_bits(uint32_t x) {
+  const uint32_t k = x ^ (uint32_t(int32_t(x) >> 31) | 0x80000000u);
+  return (x & 0x7fffffffu) > 0x7f800000u ? 0xffffffffu : k;  // NaN above everything
+}
 __device__ __forceinline__ float from_key(uint32_t k) {
   return __uint_as_float(k ^ ((k & 0x80000000u) ? 0x80000000u : 0xffffffffu));
 }
@@ -322,10 +327,10 @@ __global__ void __launch_bounds__(kThreads, 4) select_radix3_kernel(const float*
       return k4[i];
     } else {
       uint4 v = __ldcg(g4 + i);
-      v.x = to_key(__uint_as_float(v.x));
-      v.y = to_key(__uint_as_float(v.y));
-      v.z = to_key(__uint_as_float(v.z));
-      v.w = to_key(__uint_as_float(v.w));
+      v.x = to_key_bits(v.x);
+      v.y = to_key_bits(v.y);
+      v.z = to_key_bits(v.z);
+      v.w = to_key_bits(v.w);
       return v;
     }
   };
@@ -371,10 +376,10 @@ __global__ void __launch_bounds__(kThreads, 4) select_radix3_kernel(const float*
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (i0 + u * kThreads < n4) {
-          atomicAdd(&my_hist[to_key(__uint_as_float(v[u].x)) >> 21], 1u);
-          atomicAdd(&my_hist[to_key(__uint_as_float(v[u].y)) >> 21], 1u);
-          atomicAdd(&my_hist[to_key(__uint_as_float(v[u].z)) >> 21], 1u);
-          atomicAdd(&my_hist[to_key(__uint_as_float(v[u].w)) >> 21], 1u);
+          atomicAdd(&my_hist[to_key_bits(v[u].x) >> 21], 1u);
+          atomicAdd(&my_hist[to_key_bits(v[u].y) >> 21], 1u);
+          atomicAdd(&my_hist[to_key_bits(v[u].z) >> 21], 1u);
+          atomicAdd(&my_hist[to_key_bits(v[u].w) >> 21], 1u);
         }
       }
     }
@@ -388,10 +393,10 @@ __global__ void __launch_bounds__(kThreads, 4) select_radix3_kernel(const float*
     if (ok) {
       for (uint32_t i = beg + t; i < end; i += kThreads) {
         uint4 v = k4[i];
-        v.x = to_key(__uint_as_float(v.x));
-        v.y = to_key(__uint_as_float(v.y));
-        v.z = to_key(__uint_as_float(v.z));
-        v.w = to_key(__uint_as_float(v.w));
+        v.x = to_key_bits(v.x);
+        v.y = to_key_bits(v.y);
+        v.z = to_key_bits(v.z);
+        v.w = to_key_bits(v.w);
         k4[i] = v;
         atomicAdd(&my_hist[v.x >> 21], 1u);
         atomicAdd(&my_hist[v.y >> 21], 1u);
@@ -433,6 +438,13 @@ __global__ void __launch_bounds__(kThreads, 4) select_radix3_kernel(const float*
   // U 16-byte groups per thread and step, loaded before any candidate is
   // stored (the stores could otherwise alias the loads and serialise them);
   // U = 4 for long slices, 1 for short ones (fewer idle ballots)
+  // Unstaged, the match test runs on the raw bits: keys with top digit d1
+  // are exactly the values whose bits 31..21 equal t1 (d1 ^ 1024 for the
+  // positive half, ~d1 for the negative one), except that NaN bit patterns
+  // share the digits 0..3 and 2044..2047 with real values (all NaNs have the
+  // key 0xffffffff); for those d1 every key is converted first.
+  const bool raw_ok = !STAGED && d1 >= 4u && d1 <= 2043u;
+  const uint32_t t1 = d1 >= 1024u ? (d1 ^ 1024u) : (~d1 & 2047u);
   auto compact = [&](auto unroll) {
     constexpr int U = decltype(unroll)::value;
     for (uint32_t i0 = t; i0 < n4w; i0 += U * kThreads) {
@@ -440,20 +452,29 @@ __global__ void __launch_bounds__(kThreads, 4) select_radix3_kernel(const float*
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const uint32_t i = i0 + u * kThreads;
-        v[u] = i < n4 ? load4(i) : make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (STAGED)
+          v[u] = i < n4 ? k4[i] : make_uint4(0u, 0u, 0u, 0u);
+        else
+          v[u] = i < n4 ? __ldcg(g4 + i) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const uint32_t i = i0 + u * kThreads;
-        const uint32_t kk[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        uint32_t kk[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        if (!STAGED && !raw_ok) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) kk[j] = to_key_bits(kk[j]);
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const bool match = i < n4 && (kk[j] >> 21) == d1;
+          const bool match =
+              i < n4 && (raw_ok ? (kk[j] >> 21) == t1 : (kk[j] >> 21) == d1);
           const uint32_t b = __ballot_sync(0xffffffffu, match);
           if (match) {
-            atomicAdd(&my_hist[(kk[j] >> 10) & (kBins - 1)], 1u);
+            const uint32_t key = raw_ok ? to_key_bits(kk[j]) : kk[j];
+            atomicAdd(&my_hist[(key >> 10) & (kBins - 1)], 1u);
             const uint32_t pos = wn + __popc(b & lt);
-            if (pos < region) my_cand[pos] = kk[j];
+            if (pos < region) my_cand[pos] = key;
           }
           wn += __popc(b);
         }
