@@ -373,13 +373,20 @@ __global__ void __launch_bounds__(kThreads, 4) select_radix3_kernel(const float*
         const uint32_t i = i0 + u * kThreads;
         if (i < n4) v[u] = __ldcg(g4 + i);
       }
+      // counted by the raw bits 31..21 (a permutation of the key digit,
+      // undone when the sub-histograms merge); every NaN goes to raw digit
+      // 1023, which holds only NaNs and maps to key digit 2047, where the
+      // key of every NaN lies
+      auto raw_bin = [](uint32_t x) -> uint32_t {
+        return (x & 0x7fffffffu) > 0x7f800000u ? 1023u : x >> 21;
+      };
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (i0 + u * kThreads < n4) {
-          atomicAdd(&my_hist[to_key_bits(v[u].x) >> 21], 1u);
-          atomicAdd(&my_hist[to_key_bits(v[u].y) >> 21], 1u);
-          atomicAdd(&my_hist[to_key_bits(v[u].z) >> 21], 1u);
-          atomicAdd(&my_hist[to_key_bits(v[u].w) >> 21], 1u);
+          atomicAdd(&my_hist[raw_bin(v[u].x)], 1u);
+          atomicAdd(&my_hist[raw_bin(v[u].y)], 1u);
+          atomicAdd(&my_hist[raw_bin(v[u].z)], 1u);
+          atomicAdd(&my_hist[raw_bin(v[u].w)], 1u);
         }
       }
     }
@@ -419,7 +426,27 @@ __global__ void __launch_bounds__(kThreads, 4) select_radix3_kernel(const float*
     return;
   }
   TK_TR(1);
-  merge_hist(kBins);
+  if constexpr (STAGED) {
+    merge_hist(kBins);
+  } else {
+    // merge, and move raw digit r to its key digit: r ^ 1024 for the
+    // positive half, ~r for the negative one
+    uint32_t sums[kBins / kThreads];
+#pragma unroll
+    for (uint32_t q = 0; q < kBins / kThreads; ++q) {
+      const uint32_t b = t + q * kThreads;
+      uint32_t v = hist[0][b];
+#pragma unroll
+      for (uint32_t h = 1; h < kSubH; ++h) v += hist[h][b];
+      sums[q] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (uint32_t q = 0; q < kBins / kThreads; ++q) {
+      const uint32_t r = t + q * kThreads;
+      hist[0][r < 1024u ? r ^ 1024u : ~r & (kBins - 1)] = sums[q];
+    }
+  }
   __syncthreads();
   uint32_t rank = largest ? slice_size - k : k - 1;
   pick_digit_cta(hist[0], kBins, rank, wsum, s_pick);
