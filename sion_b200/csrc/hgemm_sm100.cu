@@ -335,14 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = bars + 2 * S;      // [2]
   uint64_t* tempty = bars + 2 * S + 2; // [2]
   uint64_t* drain = bars + 2 * S + 4;  // [1]
-  uint64_t* recv = bars + 2 * S + 5;   // [1] cluster split-K: rank 1's half arrived (rank 0)
-  uint64_t* ring_free = bars + 2 * S + 6;  // [1] cluster split-K: rank 0's ring idle (rank 1)
+  uint64_t* recv = bars + 2 * S + 5;   // [1] cluster split-K: the peer's half has arrived
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
-  // Cluster split-K: each CTA sends the peer's 64 columns of its accumulator
-  // (BM x 64 fp32) into the start of the peer's TMA ring once the peer's MMAs
-  // have finished with it.
   const uint32_t NS = uint32_t(S);
-  uint8_t* recv_buf = ring;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* bcast = tmem_slot + 2;
   TileQueue tq{reinterpret_cast<uint32_t*>(bars + 2 * S + 17), bars + 2 * S + 9,
@@ -363,7 +358,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(drain, 1);
     mbar_init(recv, 128);  // one arrival per epilogue thread of the peer CTA
-    mbar_init(ring_free, 1);
     for (uint32_t i = 0; i < kTq; ++i) {
       mbar_init(&tq.full[i], 1);
       // consumers: the leader's MMA warp and 4 epilogue warps; in a pair also
@@ -612,6 +606,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         if (elect_one()) commit_all(&tfull[buf]);
         if (lane == 0) HG_TR(2);
+#ifdef FELIX_HGEMM_TRACE_UNITS
+        if (lane == 0 && i < 5) HG_TR(3 + i);
+        if (lane == 0 && i == 0) g_hg_trace[blockIdx.x < 1024 ? blockIdx.x : 0][11] = u.partial ? 1000u + u.kb1 - u.kb0 : u.kb1 - u.kb0;
+#endif
         __syncwarp();
         ++i;
       }
@@ -661,22 +659,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (p.ksplit2) {
         // Cluster split-K: the two CTAs hold the tile's two K halves. Rank r
-        // writes output columns [64 r, 64 r + 64): it sends the peer's 64
-        // columns of its fp32 accumulator into the peer's idle TMA ring over
-        // DSMEM (partial_index layout: a warp's 32 rows are 512 contiguous
-        // bytes; every thread then arrives on the peer's barrier, release),
-        // and adds the peer's 64 columns of its own to its accumulator (fp32
-        // addition of two terms, so both ranks form the same sums), converts
-        // and TMA-stores. Both directions run at once: half the bytes each
-        // way and half the columns per CTA, against one CTA sending 128.
+        // writes output columns [64 r, 64 r + 64): as soon as its own MMAs
+        // have completed it sends the peer's 64 columns of its fp32
+        // accumulator over DSMEM into the peer's epilogue staging area (warp
+        // q's 32 rows fill warp q's 8 KB there, 512 contiguous bytes per
+        // 4-column group; every thread then arrives on the peer's barrier,
+        // release), then waits for the peer's half, adds it to its own 64
+        // columns (fp32 addition of two terms, so both ranks form the same
+        // sums), converts into the same staging bytes (each warp has read its
+        // region first) and TMA-stores. The staging area is idle until then,
+        // so no CTA waits for its peer's MMAs before sending.
         const uint32_t me = u.seg, peer = me ^ 1u;
         if (epi_tid == 0) HG_TR(3);
-        // tfull: every MMA of this CTA has completed, so its ring is idle
-        // (nothing more is loaded: this is the CTA's only unit)
-        if (epi_tid == 0) mbar_arrive_cluster(mapa_shared(smem_u32(ring_free), peer));
-        if (!mbar_wait_cluster(ring_free, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
-        if (epi_tid == 0) HG_TR(4);
-        const uint32_t rbuf = mapa_shared(smem_u32(recv_buf), peer);
+        uint8_t* stg = staging + (warp - 2) * 8192;
+        const uint32_t rbuf = mapa_shared(smem_u32(stg), peer);
 #pragma unroll 1
         for (int c = 0; c < 64; c += 32) {
           uint32_t r[32];
@@ -684,15 +680,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            st_shared_cluster_v4(rbuf + partial_index(c / 32, j, row_in_tile) * 16, r[4 * j],
+            st_shared_cluster_v4(rbuf + ((uint32_t(c / 32) * 8u + j) * 32u + lane) * 16u, r[4 * j],
                                  r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
         }
         if (epi_tid == 0) HG_TR(5);
         mbar_arrive_cluster(mapa_shared(smem_u32(recv), peer));
         if (!mbar_wait_cluster(recv, 0, abort_flag, p.status, kWdEpilogueTmemFull)) break;
         if (epi_tid == 0) HG_TR(6);
-        const float4* r4 = reinterpret_cast<const float4*>(recv_buf);
-        uint8_t* stg = staging + (warp - 2) * 8192;
+        const float4* r4 = reinterpret_cast<const float4*>(stg);
         {
           const uint32_t c = me * 64;
           uint32_t r0[32], r1[32];
@@ -701,8 +696,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float4 x0 = r4[partial_index(0, j, row_in_tile)];
-            const float4 x1 = r4[partial_index(1, j, row_in_tile)];
+            const float4 x0 = r4[j * 32 + lane];
+            const float4 x1 = r4[(8 + j) * 32 + lane];
             r0[4 * j] = __float_as_uint(__uint_as_float(r0[4 * j]) + x0.x);
             r0[4 * j + 1] = __float_as_uint(__uint_as_float(r0[4 * j + 1]) + x0.y);
             r0[4 * j + 2] = __float_as_uint(__uint_as_float(r0[4 * j + 2]) + x0.z);
@@ -712,6 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             r1[4 * j + 2] = __float_as_uint(__uint_as_float(r1[4 * j + 2]) + x1.z);
             r1[4 * j + 3] = __float_as_uint(__uint_as_float(r1[4 * j + 3]) + x1.w);
           }
+          __syncwarp();  // every lane has read the received partials
           uint8_t* buf = stg;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -972,11 +968,14 @@ Plan plan_for(uint32_t M, uint32_t N, uint32_t K, int bn, const HgemmOptions& o,
   return pl;
 }
 
+#ifndef FELIX_HGEMM_DYN_WAVES
+#define FELIX_HGEMM_DYN_WAVES 4
+#endif
 // Whole tiles are handed out at run time (TileQueue) when there are at least
 // four waves of them; fewer waves do not drift apart enough to matter.
 bool uses_dynamic_tiles(const Plan& pl) {
   if (pl.ksplit2) return false;
-  return pl.grid > 0 && pl.dp_tiles >= 4u * pl.grid;
+  return pl.grid > 0 && pl.dp_tiles >= uint32_t(FELIX_HGEMM_DYN_WAVES) * pl.grid;
 }
 
 // Library or caller workspace a plan needs: the counter block (stream-K
