@@ -303,6 +303,7 @@ __device__ __forceinline__ void store_row_chunk(const Params& p, uint32_t row, u
 // Development-only per-CTA timeline (compiled out of the library build):
 // [cta][event] = globaltimer ns.
 __device__ unsigned long long g_hg_trace[1024][12];
+__device__ unsigned g_hg_tiles[1024][8];
 #define HG_TR(ev)                                                   \
   do {                                                              \
     if (blockIdx.x < 1024) g_hg_trace[blockIdx.x][ev] = globaltimer_ns(); \
@@ -609,6 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef FELIX_HGEMM_TRACE_UNITS
         if (lane == 0 && i < 5) HG_TR(3 + i);
         if (lane == 0 && i == 0) g_hg_trace[blockIdx.x < 1024 ? blockIdx.x : 0][11] = u.partial ? 1000u + u.kb1 - u.kb0 : u.kb1 - u.kb0;
+        if (lane == 0 && i < 8 && blockIdx.x < 1024) g_hg_tiles[blockIdx.x][i] = (u.partial ? 0x80000000u : 0u) | u.tile;
 #endif
         __syncwarp();
         ++i;
@@ -892,6 +894,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef FELIX_HGEMM_TRACE
 extern "C" void hg_trace_fetch(void* dst) {
   cudaMemcpyFromSymbol(dst, felix_sm100::hgemm::g_hg_trace, sizeof(felix_sm100::hgemm::g_hg_trace));
+}
+extern "C" void hg_tiles_fetch(void* dst) {
+  cudaMemcpyFromSymbol(dst, felix_sm100::hgemm::g_hg_tiles, sizeof(felix_sm100::hgemm::g_hg_tiles));
 }
 #endif
 
