@@ -1177,7 +1177,9 @@ FelixCode hgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const __
   // partial unit and, as the last contributor, its fix-up: 4096^3 with CTA
   // pairs (34 split tiles over 74 pairs, c = 2) 98.3 -> 94.2 us.
   p.sk_units = 0;
-  if (FELIX_HGEMM_SK_HALVES && pl.sk_tiles) {
+  // (not for 512-wide pair tiles, whose single accumulator serialises a
+  // unit's epilogue with the next unit: 2048 x 16384 x 16384 707.6 -> 773 us)
+  if (FELIX_HGEMM_SK_HALVES && pl.sk_tiles && !wide) {
     const uint32_t units = pl.grid;  // CTAs, or pairs of CTAs
     uint32_t c = units / pl.sk_tiles;
     while (c >= 2 && (pl.kblocks % c != 0 || pl.kblocks / c < 4)) --c;
