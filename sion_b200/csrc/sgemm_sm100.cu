@@ -283,17 +283,24 @@ constexpr int kTmaAk = 2;
 // the one-CTA-per-SM loop (4-k A reads) has the registers to unroll four
 // groups: 1024^3 65.5 -> 61.5-62.0 us (2: 62.5, 8: 63.0-63.5)
 constexpr int kAk4Unroll = 4;
-constexpr int kTmaBTile = kTmaBk * BN * 4;  // 16 KB (BN = 128)
 // A tile of AP floats per row (AP = row pitch). AP = 32: the rows a warp reads
 // at once (4 apart) share banks, a 2-way conflict on every A load. AP = 36: the
 // box is 36 k wide (the last 4 columns are the next k-tile's, unused) and the
 // 144-byte pitch puts those rows in different banks; each row then spans two
 // L2 lines. Measured: 36 is faster for K <= 2048 (1024^3 69.6 -> 67.6 us,
 // 2048^3 390 -> 376 us), 32 for long K (4096^3 2650 vs 2803 us).
+// The k-tile follows from the pitch: AP = 32 / 36 take 32-deep k-tiles, AP =
+// 64 / 68 (the same two layouts) 64-deep ones. The cluster split-K kernel (one
+// CTA per SM, room for 3 x 67.6 KB of stages) takes the 64-deep tiles: half
+// the barrier waits and loop trips per FFMA (1024^3 61.4 -> 59.4 us,
+// 300 x 520 x 2004 36.9 -> 34.8 us).
 template <int AP>
 struct TmaTile {
+  static constexpr int kBk = AP & ~31;
+  static_assert(kBk == 32 || kBk == 64, "A row pitch");
   static constexpr int kA = BM * AP * 4;
-  static constexpr int kSmem = kTmaStages * (kA + kTmaBTile) + 2 * kTmaStages * 8 + 16;
+  static constexpr int kB = kBk * BN * 4;
+  static constexpr int kSmem = kTmaStages * (kA + kB) + 2 * kTmaStages * 8 + 16;
 };
 static_assert(BN == 128, "TMA main loop: 128 x 128 tiles");
 
@@ -315,11 +322,12 @@ __device__ __forceinline__ bool tma_issue(TmaPipe& q, const CUtensorMap* tmA,
   if (!felix_sm100::mbar_wait(q.empty + st, (use & 1u) ^ 1u, q.abort_flag, p.status,
                               felix_sm100::kWdProducerEmpty))
     return false;
-  felix_sm100::mbar_arrive_expect_tx(q.full + st, TmaTile<AP>::kA + kTmaBTile);
-  felix_sm100::tma_load_2d(q.sA + st * (TmaTile<AP>::kA / 4), tmA, q.full + st, int(kb * kTmaBk),
+  constexpr int kBk = TmaTile<AP>::kBk;
+  felix_sm100::mbar_arrive_expect_tx(q.full + st, TmaTile<AP>::kA + TmaTile<AP>::kB);
+  felix_sm100::tma_load_2d(q.sA + st * (TmaTile<AP>::kA / 4), tmA, q.full + st, int(kb * kBk),
                            int(m0));
-  felix_sm100::tma_load_2d(q.sB + st * (kTmaBTile / 4), tmB, q.full + st, int(n0),
-                           int(kb * kTmaBk));
+  felix_sm100::tma_load_2d(q.sB + st * (TmaTile<AP>::kB / 4), tmB, q.full + st, int(n0),
+                           int(kb * kBk));
   ++q.kt_load;
   return true;
 }
@@ -337,8 +345,9 @@ __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
-  const uint32_t kb0 = kbeg / kTmaBk;
-  const uint32_t n = kend > kbeg ? (kend - kbeg + kTmaBk - 1) / kTmaBk : 0;
+  constexpr int kBk = TmaTile<AP>::kBk;
+  const uint32_t kb0 = kbeg / kBk;
+  const uint32_t n = kend > kbeg ? (kend - kbeg + kBk - 1) / kBk : 0;
   bool ok = true;
   if (t == 0)
     for (uint32_t j = 0; ok && j < n && j < kTmaStages - 1; ++j)
@@ -350,12 +359,12 @@ __device__ __forceinline__ bool mainloop_tma(TmaPipe& q, const CUtensorMap* tmA,
       return false;
     if (j == 0) SG_TR(q.tr_seg * 3 + 1);
     const float* a_s = q.sA + st * (TmaTile<AP>::kA / 4);  // [128][AP]
-    const float* b_s = q.sB + st * (kTmaBTile / 4);  // [32][128]
+    const float* b_s = q.sB + st * (TmaTile<AP>::kB / 4);  // [kBk][128]
     // one group of AK k-steps per iteration; the 2-k loop is not unrolled:
     // unrolled, the compiler hoists the B loads of later groups and spills at
     // 128 registers
 #pragma unroll(AK == 4 ? kAk4Unroll : 1)
-    for (int k2 = 0; k2 < kTmaBk / AK; ++k2) {
+    for (int k2 = 0; k2 < kBk / AK; ++k2) {
       // A: AK consecutive k of each of the thread's 8 rows per load
       float af[8][AK];
 #pragma unroll
@@ -475,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, CSK ? 1 : FELIX_SGEMM_MINB)
   if constexpr (TMA) {
     q.sA = reinterpret_cast<float*>(dsmem);
     q.sB = reinterpret_cast<float*>(dsmem + kTmaStages * TmaTile<AP>::kA);
-    q.full = reinterpret_cast<uint64_t*>(dsmem + kTmaStages * (TmaTile<AP>::kA + kTmaBTile));
+    q.full = reinterpret_cast<uint64_t*>(dsmem + kTmaStages * (TmaTile<AP>::kA + TmaTile<AP>::kB));
     q.empty = q.full + kTmaStages;
     q.abort_flag = &s_abort;
     if (t == 0) {
@@ -771,11 +780,11 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
         e = cudaFuncSetAttribute(sgemm_kernel<true, true, 36>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<36>::kSmem);
       if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(sgemm_kernel<true, true, 32, true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<32>::kSmem);
+        e = cudaFuncSetAttribute(sgemm_kernel<true, true, 64, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<64>::kSmem);
       if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(sgemm_kernel<true, true, 36, true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<36>::kSmem);
+        e = cudaFuncSetAttribute(sgemm_kernel<true, true, 68, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, TmaTile<68>::kSmem);
       return int(e);
     });
     if (rc < 0) return api_error("sgemm: device ordinal");
@@ -826,13 +835,21 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
       if (S >= 2 && (kt + S - 1) / S > 16) S = 0;
     }
     if (S >= 2 && (M + BM - 1) / BM <= 65535u) {
+      // 64-deep k-tiles: their own tensor maps (A box 68 or 64 wide, B box 64 high)
+      const int ap64 = ap + 32;
+      CUtensorMap tmA64{}, tmB64{};
+      if (encode_tmap_2d_f32(&tmA64, A, K, M, uint64_t(K) * 4, uint32_t(ap64), BM) ||
+          encode_tmap_2d_f32(&tmB64, B, N, K, uint64_t(N) * 4, BN, 64))
+        return api_error("sgemm: cuTensorMapEncodeTiled failed");
+      p.bk = 64;
+      const uint32_t kt64 = (K + 63) / 64;
       p.csk = 1;
       p.splits = S;
-      p.k_per_split = ((kt + S - 1) / S) * p.bk;
+      p.k_per_split = ((kt64 + S - 1) / S) * 64;
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = dim3((N + BN - 1) / BN, (M + BM - 1) / BM, S);
       cfg.blockDim = dim3(kThreads);
-      cfg.dynamicSmemBytes = ap == 36 ? TmaTile<36>::kSmem : TmaTile<32>::kSmem;
+      cfg.dynamicSmemBytes = ap64 == 68 ? TmaTile<68>::kSmem : TmaTile<64>::kSmem;
       cfg.stream = stream;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -841,9 +858,9 @@ FelixCode sgemm_launch(uint32_t M, uint32_t N, uint32_t K, float alpha, const fl
       attr[0].val.clusterDim.z = S;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      const cudaError_t e = ap == 36
-                                ? cudaLaunchKernelEx(&cfg, sgemm_kernel<true, true, 36, true>, tmA, tmB, p)
-                                : cudaLaunchKernelEx(&cfg, sgemm_kernel<true, true, 32, true>, tmA, tmB, p);
+      const cudaError_t e =
+          ap64 == 68 ? cudaLaunchKernelEx(&cfg, sgemm_kernel<true, true, 68, true>, tmA64, tmB64, p)
+                     : cudaLaunchKernelEx(&cfg, sgemm_kernel<true, true, 64, true>, tmA64, tmB64, p);
       if (e != cudaSuccess) return launch_error(e, "sgemm: cluster launch failed");
       return FelixCode{FELIX_SUCCESS, cudaSuccess};
     }
